@@ -1,0 +1,362 @@
+"""Benchmark: MoE-layer decode on B200.
+
+Workload (N = 1): the one-layer decode configuration -- 256 experts, top-8,
+Q3_K gate/up and Q4_K down (1,490,944 B per expert), a Q8_0 shared expert
+(3,342,336 B), an fp32 router [256 x 2048] and shared gate vector; one fp32
+token per step.  Algorithmic bytes per token = 8 x 1,490,944 + 3,342,336 +
+2,097,152 + 8,192 = 17,375,232 B (packed weights actually read + router +
+gate vector).  To keep the timing out of L2 (126 MB), steps rotate over
+`--copies` resident copies of the layer at distinct HBM addresses (16 copies:
+278 MB touched per rotation > 2x L2) and over distinct tokens.
+
+Multi-GPU (torchrun, N > 1): expert parallel.  Each rank holds 256/N
+experts of every layer copy plus the router and shared expert; each rank
+decodes its own token per step (weak scaling): route locally, all-gather the
+tokens and routing, compute the held experts' contributions for every
+rank's token, reduce-scatter the partial outputs back to each token's owner.
+
+`--impl reference` times the reference's own CPU implementation of the same
+step on the host cores: the reference's AVX2 moe_quant_expert (compiled from
+its sources into oracle/_ref) for the 8 routed experts on a thread pool, and
+the numpy router / combine / shared expert of its Python layer.
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "intel-optimized-moe-streaming_b200"))
+sys.path.insert(0, str(ROOT / "oracle"))
+
+METRIC = "MoE-layer decode µs/token & quant-weight HBM GB/s (% of 8 TB/s) at 1/2/4/8 GPU"
+UNIT = "GB/s"
+EXPERT_BYTES = 1_490_944
+SHARED_BYTES = 3_342_336
+ROUTER_BYTES = 2_097_152
+GATE_VEC_BYTES = 8_192
+
+
+def step_bytes(n_experts_read: int, shared: bool = True) -> int:
+    return n_experts_read * EXPERT_BYTES + (SHARED_BYTES if shared else 0) + ROUTER_BYTES + GATE_VEC_BYTES
+
+
+def measured_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.proc, self.lines = gpu, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------- CPU arms
+
+def cpu_reference_step_fn(lw, threads: int):
+    """One token through the layer with the reference's CPU implementation:
+    the reference AVX2 kernel per routed expert (oracle/_ref) on a thread
+    pool, numpy router/combine/shared expert.  Falls back to the scalar
+    oracle port when the reference library was not built."""
+    from concurrent.futures import ThreadPoolExecutor
+    import oracle as O
+    try:
+        lib, kind = O.ReferenceLibrary(), "reference"
+    except FileNotFoundError:
+        lib, kind = O.KQuantOracle(), "port"
+    shared = O.shared_weights_from_packed(lib, lw.shared(), lw.shared_kinds, lw.hidden,
+                                          lw.shared_inter, lw.shared_gate_inp)
+    gate_he = lw.gate_he()
+    pool = ThreadPoolExecutor(max_workers=threads)
+    experts = [lw.expert(e) for e in range(lw.n_experts)]
+
+    def expert_fn(e, x):
+        rc, y = lib.expert(experts[e], lw.kinds, x, lw.hidden, lw.inter, 0)
+        if rc:
+            raise RuntimeError(f"native expert failed with status {rc}")
+        return y
+
+    def step(x):
+        ids, w, _ = O.route(x, gate_he, lw.top_k)
+        outs = list(pool.map(lambda e: expert_fn(e, x), ids))
+        comb = np.zeros(lw.hidden, np.float32)
+        for o, wk in zip(outs, w):
+            comb += wk * o
+        return comb + O.shared_forward(x, shared)
+    return step, kind, pool
+
+
+def time_cpu(lw, tokens, threads, min_seconds=10.0, max_tokens=2000):
+    step, kind, pool = cpu_reference_step_fn(lw, threads)
+    step(tokens[0])
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step(tokens[n % len(tokens)])
+        n += 1
+        el = time.perf_counter() - t0
+        if (el >= min_seconds and n >= 8) or n >= max_tokens:
+            break
+    pool.shutdown()
+    return el / n, n, kind
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from flash_moe_b200 import synth
+    lw = synth.make_layer(seed=0)
+    tokens = synth.make_tokens(0, 64, lw.hidden)
+    threads = os.cpu_count() or 1
+    step, kind, pool = cpu_reference_step_fn(lw, threads)
+    for i in range(args.warmup):
+        step(tokens[i % 64])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(tokens[i % 64])
+    el = time.perf_counter() - t0
+    pool.shutdown()
+    per = el / args.steps
+    gbs = step_bytes(8) / per / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 4), "us_per_token": round(per * 1e6, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, config-2 shapes and distributions)",
+        "config": {"workload": "config 2: one MoE layer decode, 1 token/step, 256 experts top-8, "
+                               "Q3_K/Q3_K/Q4_K experts + Q8_0 shared expert", "tokens_per_step": 1},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{args.steps} tokens, {cpu_model()}"},
+        "e2e": {"value": round(gbs, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- GPU arm
+
+def run_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from flash_moe_b200 import synth
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    from flash_moe_b200 import ep as EP
+
+    lw = synth.make_layer(seed=0)
+    E = lw.n_experts
+    per = E // world
+    begin = rank * per
+    arena = ExpertArena(dev)
+    first = arena.add_layer(0, lw, expert_begin=begin, expert_count=per)
+    # further copies at distinct addresses: clone the device buffers
+    for c in range(1, args.copies):
+        arena.add_device_layer(c, first.clone())
+    backend = B200ExpertBackend(arena, exact=args.engine == "exact")
+    H = lw.hidden
+    ntok = 64
+    tokens = torch.from_numpy(synth.make_tokens(1000 + rank, ntok, H)).to(dev)
+
+    runner = EP.DecodeRunner(backend, list(range(args.copies)), tokens, world, rank)
+    stream = torch.cuda.current_stream(dev)
+
+    # warm-up (also compiles nothing; the library is prebuilt)
+    for i in range(args.warmup):
+        runner.step(i)
+    torch.cuda.synchronize()
+
+    graph = None
+    if not args.no_graph:
+        graph = runner.capture(args.steps)
+
+    peaks, peak_kind = measured_peaks()
+    with ClockSampler(local) as clk:
+        # soak ~0.5 s so the clock sampler sees the GPU under this load
+        t_end = time.perf_counter() + args.soak
+        while time.perf_counter() < t_end:
+            if graph is not None:
+                graph.replay()
+            else:
+                for i in range(args.steps):
+                    runner.step(i)
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                runner.step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    ms_t = torch.tensor([ms], device=dev)
+    bytes_local = runner.algorithmic_bytes(args.steps)
+    bytes_t = torch.tensor([float(bytes_local)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(bytes_t, op=dist.ReduceOp.SUM)
+    ms_max = float(ms_t.item())
+    total_bytes = float(bytes_t.item())
+    per_step_ms = ms_max / args.steps
+    gbs = total_bytes / (ms_max / 1e3) / 1e9
+
+    # roofline of the decode kernel chain on this rank (one launch sequence
+    # per step), from the same timed region
+    ach = bytes_local / (ms / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(ach, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": EP.profiled_traffic(ROOT),
+            "peak_source": f"{peak_kind} hbm_gbs", "kernel": runner.kernel_name}
+
+    # end to end through the public API: pinned host token in, host result out
+    e2e = runner.e2e(args.steps, args.warmup)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        per_tok, n, kind = time_cpu(lw, synth.make_tokens(1000, 64, H), os.cpu_count() or 1,
+                                    min_seconds=args.cpu_seconds)
+        cpu = {"value": round(step_bytes(8) / per_tok / 1e9, 4), "unit": UNIT,
+               "cores": os.cpu_count() or 1, "kind": kind,
+               "sample": f"{n} tokens of the same layer ({per_tok * 1e6:.0f} us/token), {cpu_model()}"}
+    if graph is not None:
+        del graph
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(gbs, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 6),
+            "us_per_token": round(per_step_ms * 1e3 / 1, 3),
+            "hbm_frac_of_8tbs": round(gbs / (8000.0 * world), 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, config-2 shapes and distributions)",
+            "config": {"workload": "config 2: one MoE layer decode, 1 token/step/GPU, 256 experts "
+                                   "top-8, Q3_K/Q3_K/Q4_K experts + Q8_0 shared expert",
+                       "tokens_per_step_per_gpu": 1, "layer_copies": args.copies,
+                       "l2": f"rotating {args.copies} layer copies at distinct addresses "
+                             f"({args.copies * step_bytes(8) / 1e6:.0f} MB touched per rotation > 2x L2)",
+                       "parallelism": f"ep{world}" if world > 1 else "single",
+                       "engine": args.engine, "cuda_graph": graph is not None or not args.no_graph,
+                       "algorithmic_bytes_per_token": step_bytes(8)},
+            "roofline": roof,
+            "e2e": e2e,
+            "gpu_launches": runner.launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    runner.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--copies", type=int, default=16)
+    ap.add_argument("--engine", choices=["fast", "exact"], default="fast")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--soak", type=float, default=0.5)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

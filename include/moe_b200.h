@@ -1,0 +1,157 @@
+/*
+ * moe_b200.h -- C ABI of libmoe_b200.so, the B200 (sm_100a) routed-expert
+ * MoE library.
+ *
+ * Two groups of entry points:
+ *
+ * 1. Drop-ins for the reference's native exports.  Same names, argument
+ *    meaning, return codes and synchronous behaviour as the functions of
+ *    vin10122/Intel-optimized-MoE-streaming that Python binds with ctypes.
+ *    Pointers may be host memory (copied to the GPU and back inside the
+ *    call) or device memory (used in place).  The calling thread's current
+ *    CUDA device is used.
+ *
+ * 2. A device-resident API: weights stay in HBM in their GGUF block layout,
+ *    every pointer is a device pointer, every call is asynchronous on the
+ *    given cudaStream_t (passed as void*), and argument errors are returned
+ *    before anything is enqueued.
+ *
+ * Status codes (all functions returning int): 0 success;
+ *   -1 bad argument (null pointer, size <= 0 or out of range, bad flag),
+ *   -2 unsupported ggml type or columns not a multiple of its block size,
+ *   -3 tensor byte count does not match its shape,
+ *   -4 an output value is not finite,
+ *   -5 host-side failure (allocation),
+ * and, for conditions the CPU reference cannot have,
+ *   -6 a CUDA call failed (moe_b200_last_cuda_error() gives the cudaError_t),
+ *   -7 a device pointer is not 16-byte aligned,
+ *   -8 workspace too small,
+ *   -9 a bounded device-side wait gave up.
+ *
+ * ggml type ids: Q8_0 = 8, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_B200_API __attribute__((visibility("default")))
+#else
+#define MOE_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------
+ * 1. Reference-compatible exports
+ * ---------------------------------------------------------------------- */
+
+/* 1 if `type` is one of the five supported ggml types, else 0.
+ * Replaces dequant_k_supported (cpp/dequant_k.cpp:342-344). */
+MOE_B200_API int dequant_k_supported(int type);
+
+/* Values per block of `type` (32 or 256), 0 if unsupported.
+ * Replaces dequant_k_block_size (cpp/dequant_k.cpp:346-348). */
+MOE_B200_API int dequant_k_block_size(int type);
+
+/* Dequantise n values of `type` from src into dst: fp32, or binary16
+ * rounded to nearest even when want_f16 != 0.  Bit-identical to the
+ * reference.  Returns 0, or -1 on an unknown type, a null pointer, n <= 0 or
+ * n not a multiple of the block size (-6 on a CUDA failure).
+ * Replaces dequant_k (cpp/dequant_k.cpp:350-394); bound by ctypes in
+ * src/run_q4k_f16_openvino.py:37-59 and tools/test_dequant_k.py:52-76. */
+MOE_B200_API int dequant_k(int type, const uint8_t* src, void* dst, int64_t n, int want_f16);
+
+/* One SwiGLU expert for one token over raw quantised rows:
+ *   g = gate.x, u = up.x, a = (g * sigmoid(g)) * u, output = down.a
+ * gate/up are [intermediate x hidden], down is [hidden x intermediate], each
+ * a row-major sequence of GGUF blocks.  fp16_graph = 1 rounds x, every
+ * weight, g, u, sigmoid, silu, a and the output to binary16 like the
+ * reference; 0 computes in fp32.  Status codes as listed above, checked in
+ * the reference's order; on -4 the rows after the first non-finite one are
+ * left untouched.
+ * Replaces moe_quant_expert (cpp/moe_quant_dot.cpp:171-214); bound by
+ * ctypes in src/flash_moe/native_expert.py:14-20. */
+MOE_B200_API int moe_quant_expert(int gate_type, const uint8_t* gate, int64_t gate_bytes,
+                     int up_type, const uint8_t* up, int64_t up_bytes,
+                     int down_type, const uint8_t* down, int64_t down_bytes,
+                     const float* input, int hidden, int intermediate, float* output,
+                     int fp16_graph);
+
+/* ------------------------------------------------------------------------
+ * 2. Device-resident API
+ * ---------------------------------------------------------------------- */
+
+/* One MoE layer resident in device memory.  Routed-expert tensors are the
+ * GGUF ffn_{gate,up,down}_exps tensors (or the slice of them this GPU holds):
+ * `expert_count` consecutive per-expert tensors, expert e (global id) at
+ * byte offset (e - expert_begin) * per-expert size.  Base pointers must be
+ * 16-byte aligned.  Replaces the per-expert byte ranges the reference slices
+ * out of the GGUF file (src/run_q4k_f16_openvino.py:88-133) and keeps them
+ * resident instead of streaming them (src/flash_moe/store.py:138-239). */
+typedef struct moe_b200_layer {
+    int32_t hidden;              /* H */
+    int32_t intermediate;        /* I of the routed experts */
+    int32_t n_experts;           /* E: experts the router scores */
+    int32_t top_k;               /* K, 1..16 */
+    int32_t expert_begin;        /* first expert held in gate/up/down */
+    int32_t expert_count;        /* experts held (E when not sharded) */
+    int32_t gate_type, up_type, down_type;
+    int32_t shared_intermediate; /* 0: no shared expert */
+    int32_t shared_gate_type, shared_up_type, shared_down_type;
+    int32_t flags;               /* MOE_B200_* flags below */
+    const uint8_t* gate;         /* expert_count x [I x H] blocks */
+    const uint8_t* up;           /* expert_count x [I x H] blocks */
+    const uint8_t* down;         /* expert_count x [H x I] blocks */
+    const float* router;         /* [E x H] fp32, the GGUF ffn_gate_inp layout */
+    const float* router_bias;    /* [E] fp32 added to the logits, or NULL */
+    const uint8_t* shared_gate;  /* [Is x H] */
+    const uint8_t* shared_up;    /* [Is x H] */
+    const uint8_t* shared_down;  /* [H x Is] */
+    const float* shared_gate_inp;/* [H] fp32 */
+} moe_b200_layer;
+
+/* flags */
+#define MOE_B200_FP16_GRAPH   1  /* routed experts with the fp16_graph rounding */
+#define MOE_B200_NO_SHARED    2  /* skip the shared expert on this call */
+#define MOE_B200_EXACT        4  /* use the exact (fp32 dequant + FMA) engine */
+#define MOE_B200_SHARED_ONLY  8  /* only the shared expert (no routing, no routed experts) */
+
+/* Bytes of workspace moe_b200_decode needs for `max_tokens` tokens. */
+MOE_B200_API int moe_b200_decode_workspace(const moe_b200_layer* layer, int32_t max_tokens,
+                              size_t* bytes);
+
+/* Decode `tokens` tokens through one layer, all on `stream`:
+ *   route (fp32 scores, top-k, float64 softmax over the k) ->
+ *   k routed SwiGLU experts -> sum of weight_k * out_k in top-k order ->
+ *   + sigmoid(x . shared_gate_inp) * shared_expert(x).
+ * x: [tokens x H] fp32, y: [tokens x H] fp32.  topk_ids ([tokens x K]
+ * int32) and topk_weights ([tokens x K] fp32) receive the routing when not
+ * NULL.  Experts outside [expert_begin, expert_begin + expert_count)
+ * contribute zero (expert-parallel partial output).
+ * Replaces run_moe_layer (src/flash_moe/moe_layer.py:39-107) with the
+ * router of src/flash_moe/router.py:241-271 and the shared expert of
+ * src/flash_moe/shared_expert.py:416-446, for each token. */
+MOE_B200_API int moe_b200_decode(const moe_b200_layer* layer, const float* x, int32_t tokens,
+                    float* y, int32_t* topk_ids, float* topk_weights,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Device-pointer dequantisation on a stream: out_dtype 0 = fp32,
+ * 1 = binary16 (round to nearest even).  Same values as dequant_k. */
+MOE_B200_API int moe_b200_dequant(int type, const void* src, void* dst, int64_t n, int out_dtype,
+                     void* stream);
+
+/* cudaError_t of the last failed CUDA call on this thread (0 if none). */
+MOE_B200_API int moe_b200_last_cuda_error(void);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+MOE_B200_API int moe_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H */

@@ -1,0 +1,388 @@
+// abi.cu -- the extern "C" entry points of libmoe_b200.so (include/moe_b200.h).
+//
+// Reference-compatible exports accept host or device pointers.  Host buffers
+// are copied through a per-thread, per-device scratch allocation on a
+// per-thread stream, so concurrent callers (the reference fans experts out
+// over a ThreadPoolExecutor, src/flash_moe/moe_layer.py:76-97) never share
+// device state and each call is deterministic.
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "launch.h"
+
+namespace moeb200 {
+
+static thread_local int tl_last_cuda = 0;
+
+static int fail(cudaError_t e, int code) {
+    tl_last_cuda = (int)e;
+    return code;
+}
+
+int sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!cache[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+static inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Per-thread scratch on one device: a stream and a growable device buffer.
+struct Scratch {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    void* buf = nullptr;
+    size_t cap = 0;
+
+    cudaError_t ensure(size_t bytes) {
+        if (!stream) {
+            cudaError_t e = cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking);
+            if (e != cudaSuccess) return e;
+        }
+        if (bytes <= cap) return cudaSuccess;
+        if (buf) cudaFree(buf);
+        buf = nullptr;
+        cap = 0;
+        const size_t want = align256(bytes + bytes / 4);
+        cudaError_t e = cudaMalloc(&buf, want);
+        if (e != cudaSuccess) return e;
+        cap = want;
+        return cudaSuccess;
+    }
+    ~Scratch() {
+        if (device < 0) return;
+        int prev = 0;
+        if (cudaGetDevice(&prev) != cudaSuccess) return;
+        cudaSetDevice(device);
+        if (buf) cudaFree(buf);
+        if (stream) cudaStreamDestroy(stream);
+        cudaSetDevice(prev);
+    }
+};
+
+static Scratch* thread_scratch() {
+    static thread_local Scratch per_device[16];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return nullptr;
+    per_device[dev].device = dev;
+    return &per_device[dev];
+}
+
+// true when p is device (or managed) memory the GPU can use in place.
+static bool on_device(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// Lays out host->device staging regions inside one scratch buffer.
+struct Stager {
+    size_t used = 0;
+    size_t take(size_t bytes) {
+        const size_t at = used;
+        used += align256(bytes);
+        return at;
+    }
+};
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+static int check_qmat(int type, const void* base, int rows, int cols) {
+    if (!supported(type) || cols % block_size(type)) return ST_TYPE;
+    if (!base) return ST_ARG;
+    if (!aligned16(base)) return ST_ALIGN;
+    (void)rows;
+    return ST_OK;
+}
+
+static QMat qmat(int type, const void* base, int rows, int cols) {
+    QMat m;
+    m.base = static_cast<const uint8_t*>(base);
+    m.type = type;
+    m.rows = rows;
+    m.cols = cols;
+    m.row_bytes = row_bytes(type, cols);
+    m.stride = m.row_bytes * rows;
+    return m;
+}
+
+static int check_layer(const moe_b200_layer* L) {
+    if (!L) return ST_ARG;
+    if (L->hidden <= 0 || L->intermediate <= 0 || L->hidden > 65536 || L->intermediate > 65536)
+        return ST_ARG;
+    if (L->n_experts < 1 || L->top_k < 1 || L->top_k > 16 || L->top_k > L->n_experts) return ST_ARG;
+    if (L->expert_begin < 0 || L->expert_count < 1 ||
+        L->expert_begin + L->expert_count > L->n_experts)
+        return ST_ARG;
+    if (!L->router || !aligned16(L->router)) return L->router ? ST_ALIGN : ST_ARG;
+    int st;
+    if ((st = check_qmat(L->gate_type, L->gate, L->intermediate, L->hidden)) != ST_OK) return st;
+    if ((st = check_qmat(L->up_type, L->up, L->intermediate, L->hidden)) != ST_OK) return st;
+    if ((st = check_qmat(L->down_type, L->down, L->hidden, L->intermediate)) != ST_OK) return st;
+    if (L->shared_intermediate < 0 || L->shared_intermediate > 65536) return ST_ARG;
+    if (L->shared_intermediate > 0) {
+        const int Is = L->shared_intermediate;
+        if ((st = check_qmat(L->shared_gate_type, L->shared_gate, Is, L->hidden)) != ST_OK) return st;
+        if ((st = check_qmat(L->shared_up_type, L->shared_up, Is, L->hidden)) != ST_OK) return st;
+        if ((st = check_qmat(L->shared_down_type, L->shared_down, L->hidden, Is)) != ST_OK) return st;
+        if (!L->shared_gate_inp) return ST_ARG;
+    }
+    return ST_OK;
+}
+
+// Workspace regions of one decode call.
+struct DecodeWs {
+    size_t scores, ids, w, sg, act, total;
+};
+
+static DecodeWs decode_ws(const moe_b200_layer* L, int T) {
+    const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate
+                                                              : L->intermediate;
+    Stager s;
+    DecodeWs w;
+    w.scores = s.take((size_t)T * L->n_experts * 4);
+    w.ids = s.take((size_t)T * L->top_k * 4);
+    w.w = s.take((size_t)T * L->top_k * 4);
+    w.sg = s.take((size_t)T * 4);
+    w.act = s.take((size_t)T * (L->top_k + 1) * Imax * 4);
+    w.total = s.used;
+    return w;
+}
+
+}  // namespace moeb200
+
+using namespace moeb200;
+
+extern "C" {
+
+int moe_b200_version(void) { return 100; }
+
+int moe_b200_last_cuda_error(void) { return tl_last_cuda; }
+
+int dequant_k_supported(int type) { return supported(type) ? 1 : 0; }
+
+int dequant_k_block_size(int type) { return block_size(type); }
+
+int dequant_k(int type, const uint8_t* src, void* dst, int64_t n, int want_f16) {
+    const int bs = block_size(type);
+    if (bs == 0 || src == nullptr || dst == nullptr) return ST_ARG;
+    if (n <= 0 || n % bs != 0) return ST_ARG;
+    Scratch* sc = thread_scratch();
+    if (!sc) return fail(cudaErrorInvalidDevice, ST_CUDA);
+    const size_t in_bytes = (size_t)(n / bs) * block_bytes(type);
+    const size_t out_bytes = (size_t)n * (want_f16 ? 2 : 4);
+    const bool src_dev = on_device(src), dst_dev = on_device(dst);
+    Stager st;
+    const size_t o_src = src_dev ? 0 : st.take(in_bytes);
+    const size_t o_dst = dst_dev ? 0 : st.take(out_bytes);
+    cudaError_t e = sc->ensure(st.used ? st.used : 256);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    char* base = static_cast<char*>(sc->buf);
+    const void* dsrc = src_dev ? static_cast<const void*>(src) : base + o_src;
+    void* ddst = dst_dev ? dst : base + o_dst;
+    if (!src_dev) {
+        e = cudaMemcpyAsync(base + o_src, src, in_bytes, cudaMemcpyHostToDevice, sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_CUDA);
+    }
+    e = launch_dequant(type, dsrc, ddst, n, want_f16 != 0, sc->stream);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    if (!dst_dev) {
+        e = cudaMemcpyAsync(dst, ddst, out_bytes, cudaMemcpyDeviceToHost, sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_CUDA);
+    }
+    e = cudaStreamSynchronize(sc->stream);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    return ST_OK;
+}
+
+int moe_quant_expert(int gate_type, const uint8_t* gate, int64_t gate_bytes,
+                     int up_type, const uint8_t* up, int64_t up_bytes,
+                     int down_type, const uint8_t* down, int64_t down_bytes,
+                     const float* input, int hidden, int intermediate, float* output,
+                     int fp16_graph) {
+    // argument checks in the reference's order (cpp/moe_quant_dot.cpp:177-188)
+    const int types[3] = {gate_type, up_type, down_type};
+    const int cols[3] = {hidden, hidden, intermediate};
+    const int rows[3] = {intermediate, intermediate, hidden};
+    const int64_t sizes[3] = {gate_bytes, up_bytes, down_bytes};
+    if (!gate || !up || !down || !input || !output || hidden <= 0 || intermediate <= 0 ||
+        hidden > 65536 || intermediate > 65536 || (fp16_graph != 0 && fp16_graph != 1))
+        return ST_ARG;
+    for (int i = 0; i < 3; ++i) {
+        const int bs = block_size(types[i]);
+        if (!bs || cols[i] % bs) return ST_TYPE;
+        if (sizes[i] != (int64_t)rows[i] * (cols[i] / bs) * block_bytes(types[i])) return ST_BYTES;
+    }
+    try {
+        Scratch* sc = thread_scratch();
+        if (!sc) return fail(cudaErrorInvalidDevice, ST_INTERNAL);
+        const void* ptrs[4] = {gate, up, down, input};
+        const size_t bytes[4] = {(size_t)gate_bytes, (size_t)up_bytes, (size_t)down_bytes,
+                                 (size_t)hidden * 4};
+        bool dev[4];
+        size_t off[4];
+        Stager st;
+        for (int i = 0; i < 4; ++i) {
+            dev[i] = on_device(ptrs[i]) && aligned16(ptrs[i]);
+            off[i] = dev[i] ? 0 : st.take(bytes[i]);
+        }
+        const size_t o_act = st.take((size_t)2 * intermediate * 4);
+        const size_t o_y = st.take((size_t)hidden * 4);
+        cudaError_t e = sc->ensure(st.used);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        char* base = static_cast<char*>(sc->buf);
+        const void* dptr[4];
+        for (int i = 0; i < 4; ++i) {
+            if (dev[i]) {
+                dptr[i] = ptrs[i];
+            } else {
+                e = cudaMemcpyAsync(base + off[i], ptrs[i], bytes[i], cudaMemcpyDefault,
+                                    sc->stream);
+                if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+                dptr[i] = base + off[i];
+            }
+        }
+        ExactPlan p{};
+        p.T = 1;
+        p.K = 1;
+        p.H = hidden;
+        p.I = intermediate;
+        p.Is = 0;
+        p.Imax = intermediate;
+        p.round16 = fp16_graph;
+        p.expert_begin = 0;
+        p.expert_count = 1;
+        p.x = static_cast<const float*>(dptr[3]);
+        p.gate = qmat(gate_type, dptr[0], intermediate, hidden);
+        p.up = qmat(up_type, dptr[1], intermediate, hidden);
+        p.down = qmat(down_type, dptr[2], hidden, intermediate);
+        p.act = reinterpret_cast<float*>(base + o_act);
+        p.y = reinterpret_cast<float*>(base + o_y);
+        e = launch_exact(p, sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        std::vector<float> y(hidden);
+        e = cudaMemcpyAsync(y.data(), p.y, (size_t)hidden * 4, cudaMemcpyDeviceToHost, sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        e = cudaStreamSynchronize(sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        // rows up to and including the first non-finite one are written,
+        // as the reference's output loop stops there (moe_quant_dot.cpp:207-211)
+        int n_out = hidden, status = ST_OK;
+        for (int r = 0; r < hidden; ++r) {
+            if (!std::isfinite(y[r])) {
+                n_out = r + 1;
+                status = ST_NONFINITE;
+                break;
+            }
+        }
+        if (on_device(output)) {
+            e = cudaMemcpy(output, y.data(), (size_t)n_out * 4, cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        } else {
+            std::memcpy(output, y.data(), (size_t)n_out * 4);
+        }
+        return status;
+    } catch (...) {
+        return ST_INTERNAL;
+    }
+}
+
+int moe_b200_dequant(int type, const void* src, void* dst, int64_t n, int out_dtype,
+                     void* stream) {
+    const int bs = block_size(type);
+    if (bs == 0 || !src || !dst || n <= 0 || n % bs || (out_dtype != 0 && out_dtype != 1))
+        return ST_ARG;
+    cudaError_t e = launch_dequant(type, src, dst, n, out_dtype == 1,
+                                   static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ST_OK : fail(e, ST_CUDA);
+}
+
+int moe_b200_decode_workspace(const moe_b200_layer* L, int32_t max_tokens, size_t* bytes) {
+    const int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (max_tokens < 1 || !bytes) return ST_ARG;
+    *bytes = decode_ws(L, max_tokens).total;
+    return ST_OK;
+}
+
+int moe_b200_decode(const moe_b200_layer* L, const float* x, int32_t T, float* y,
+                    int32_t* topk_ids, float* topk_weights, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+    int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (T < 1 || !x || !y || !workspace) return ST_ARG;
+    if (!aligned16(x) || !aligned16(y) || ((uintptr_t)workspace & 255u)) return ST_ALIGN;
+    const DecodeWs ws = decode_ws(L, T);
+    if (workspace_bytes < ws.total) return ST_WORKSPACE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    char* base = static_cast<char*>(workspace);
+    const bool shared_only = (L->flags & MOE_B200_SHARED_ONLY) != 0;
+    const bool with_shared = L->shared_intermediate > 0 && !(L->flags & MOE_B200_NO_SHARED);
+    if (shared_only && !with_shared) return ST_ARG;
+
+    RoutePlan r{};
+    r.T = T;
+    r.E = L->n_experts;
+    r.K = shared_only ? 0 : L->top_k;
+    r.H = L->hidden;
+    r.x = x;
+    r.router = L->router;
+    r.bias = L->router_bias;
+    r.gate_inp = with_shared ? L->shared_gate_inp : nullptr;
+    r.scores = reinterpret_cast<float*>(base + ws.scores);
+    r.ids = reinterpret_cast<int32_t*>(base + ws.ids);
+    r.w = reinterpret_cast<float*>(base + ws.w);
+    r.sg = reinterpret_cast<float*>(base + ws.sg);
+    cudaError_t e = launch_route(r, s);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+
+    ExactPlan p{};
+    p.T = T;
+    p.K = L->top_k;
+    p.H = L->hidden;
+    p.I = L->intermediate;
+    p.Is = with_shared ? L->shared_intermediate : 0;
+    p.Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate : L->intermediate;
+    p.round16 = (L->flags & MOE_B200_FP16_GRAPH) ? 1 : 0;
+    p.expert_begin = L->expert_begin;
+    p.expert_count = shared_only ? 0 : L->expert_count;
+    p.x = x;
+    p.ids = r.ids;
+    p.w = r.w;
+    p.sg = with_shared ? r.sg : nullptr;
+    p.gate = qmat(L->gate_type, L->gate, L->intermediate, L->hidden);
+    p.up = qmat(L->up_type, L->up, L->intermediate, L->hidden);
+    p.down = qmat(L->down_type, L->down, L->hidden, L->intermediate);
+    if (with_shared) {
+        p.sgate = qmat(L->shared_gate_type, L->shared_gate, L->shared_intermediate, L->hidden);
+        p.sup = qmat(L->shared_up_type, L->shared_up, L->shared_intermediate, L->hidden);
+        p.sdown = qmat(L->shared_down_type, L->shared_down, L->hidden, L->shared_intermediate);
+    }
+    p.act = reinterpret_cast<float*>(base + ws.act);
+    p.y = y;
+    e = launch_exact(p, s);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    if (topk_ids && !shared_only) {
+        e = cudaMemcpyAsync(topk_ids, r.ids, (size_t)T * L->top_k * 4, cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return fail(e, ST_CUDA);
+    }
+    if (topk_weights && !shared_only) {
+        e = cudaMemcpyAsync(topk_weights, r.w, (size_t)T * L->top_k * 4, cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return fail(e, ST_CUDA);
+    }
+    return ST_OK;
+}
+
+}  // extern "C"

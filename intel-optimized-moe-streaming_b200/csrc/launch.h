@@ -1,0 +1,48 @@
+// launch.h -- internal launchers shared by the translation units.
+#pragma once
+
+#include "common.cuh"
+#include "moe_b200.h"
+
+namespace moeb200 {
+
+int sm_count();  // multiprocessors of the current device (cached per device)
+
+cudaError_t launch_dequant(int type, const void* src, void* dst, int64_t n, bool f16,
+                           cudaStream_t stream);
+
+// Routing of T tokens: fp32 scores [T x E] (+ bias), top-K ids/weights, and
+// the shared-expert gate sigmoid(x . gate_inp) per token.
+struct RoutePlan {
+    int T, E, K, H;
+    const float* x;          // [T x H]
+    const float* router;     // [E x H]
+    const float* bias;       // [E] or null
+    const float* gate_inp;   // [H] or null (no shared expert)
+    float* scores;           // [T x E]
+    int32_t* ids;            // [T x K]
+    float* w;                // [T x K]
+    float* sg;               // [T]
+};
+cudaError_t launch_route(const RoutePlan& p, cudaStream_t stream);
+
+// Expert work of T tokens with K routed slots each (+ the shared expert),
+// computed by the exact engine: every weight dequantised bit-exactly, fp32
+// fused multiply-add accumulation.
+struct ExactPlan {
+    int T, K, H, I, Is, Imax;
+    int round16;             // fp16_graph rounding points on routed experts
+    int expert_begin;        // global id of the first held expert
+    int expert_count;
+    const float* x;          // [T x H]
+    const int32_t* ids;      // [T x K] global expert ids, or null (expert 0)
+    const float* w;          // [T x K] routing weights, or null (1.0)
+    const float* sg;         // [T] shared gate, null without shared expert
+    QMat gate, up, down;
+    QMat sgate, sup, sdown;  // base null without shared expert
+    float* act;              // [T x (K+1) x Imax]
+    float* y;                // [T x H]
+};
+cudaError_t launch_exact(const ExactPlan& p, cudaStream_t stream);
+
+}  // namespace moeb200

@@ -1,0 +1,144 @@
+// route.cu -- router scores, top-k selection and routing weights.
+//
+// Device form of ExpertRouter.scores/route (reference
+// src/flash_moe/router.py:241-271) for a batch of tokens, plus the
+// shared-expert gate sigmoid(x . w_inp) (src/flash_moe/shared_expert.py:437).
+//
+//  k_scores: one warp per (token, expert) fp32 dot product over H, 16-byte
+//            loads of the [E x H] router rows; + the optional bias.
+//  k_topk:   one warp per token.  K rounds of a warp arg-max over the E
+//            scores (ties go to the lower expert id), then the softmax over
+//            the K selected scores in float64 with numpy's summation order
+//            for the denominator, rounded to fp32 as numpy rounds the Python
+//            float when it multiplies an fp32 array.
+#include <math.h>
+
+#include "launch.h"
+
+namespace moeb200 {
+
+__global__ void __launch_bounds__(256) k_scores(RoutePlan p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * 8 + warp, t = blockIdx.y;
+    if (e >= p.E) return;
+    const float* xr = p.x + (size_t)t * p.H;
+    const float* wr = p.router + (size_t)e * p.H;
+    float acc = 0.f;
+    if ((((uintptr_t)xr | (uintptr_t)wr) & 15u) == 0 && (p.H & 3) == 0) {
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        const float4* w4 = reinterpret_cast<const float4*>(wr);
+        for (int i = lane; i < (p.H >> 2); i += 32) {
+            const float4 a = __ldg(x4 + i), b = __ldg(w4 + i);
+            acc = fmaf(a.x, b.x, acc);
+            acc = fmaf(a.y, b.y, acc);
+            acc = fmaf(a.z, b.z, acc);
+            acc = fmaf(a.w, b.w, acc);
+        }
+    } else {
+        for (int i = lane; i < p.H; i += 32) acc = fmaf(__ldg(xr + i), __ldg(wr + i), acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+        if (p.bias) acc = __fadd_rn(acc, p.bias[e]);
+        p.scores[(size_t)t * p.E + e] = acc;
+    }
+}
+
+// numpy's pairwise summation of n <= 128 float64 values (np.add.reduce on a
+// contiguous array): sequential below 8, eight interleaved partial sums
+// combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) from 8 on.
+__device__ double np_sum(const double* v, int n) {
+    if (n < 8) {
+        double r = 0.0;
+        for (int i = 0; i < n; ++i) r += v[i];
+        return r;
+    }
+    double r[8];
+    for (int j = 0; j < 8; ++j) r[j] = v[j];
+    int i = 8;
+    for (; i < n - (n % 8); i += 8)
+        for (int j = 0; j < 8; ++j) r[j] += v[i + j];
+    double res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+    for (; i < n; ++i) res += v[i];
+    return res;
+}
+
+constexpr int kMaxTopK = 16;
+
+__global__ void __launch_bounds__(32) k_topk(RoutePlan p) {
+    extern __shared__ float s_scores[];
+    unsigned char* taken = reinterpret_cast<unsigned char*>(s_scores + p.E);
+    const int t = blockIdx.x, lane = threadIdx.x;
+    for (int e = lane; e < p.E && p.K > 0; e += 32) {
+        s_scores[e] = p.scores[(size_t)t * p.E + e];
+        taken[e] = 0;
+    }
+    __syncwarp();
+    float sel_v[kMaxTopK];
+    int sel_i[kMaxTopK];
+    for (int k = 0; k < p.K; ++k) {
+        float best = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < p.E; e += 32) {
+            const float v = s_scores[e];
+            if (!taken[e] && (v > best || (v == best && e < bi) || bi == 0x7fffffff)) {
+                best = v;
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > best || (ov == best && oi < bi))) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) taken[bi] = 1;
+        __syncwarp();
+        sel_v[k] = best;
+        sel_i[k] = bi;
+    }
+    if (lane == 0 && p.K > 0) {
+        double m = (double)sel_v[0];
+        for (int k = 1; k < p.K; ++k) m = fmax(m, (double)sel_v[k]);
+        double ex[kMaxTopK];
+        for (int k = 0; k < p.K; ++k) ex[k] = exp((double)sel_v[k] - m);
+        const double tot = np_sum(ex, p.K);
+        const bool uniform = !isfinite(tot) || tot <= 0.0;
+        for (int k = 0; k < p.K; ++k) {
+            p.ids[(size_t)t * p.K + k] = sel_i[k];
+            p.w[(size_t)t * p.K + k] = uniform ? (float)(1.0 / p.K) : (float)(ex[k] / tot);
+        }
+    }
+    if (p.gate_inp) {
+        const float* xr = p.x + (size_t)t * p.H;
+        float acc = 0.f;
+        for (int i = lane; i < p.H; i += 32) acc = fmaf(xr[i], p.gate_inp[i], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            float g;
+            if (acc >= 0.f) {
+                g = 1.0f / (1.0f + expf(-acc));
+            } else {
+                const float e = expf(acc);
+                g = e / (1.0f + e);
+            }
+            p.sg[t] = g;
+        }
+    }
+}
+
+cudaError_t launch_route(const RoutePlan& p, cudaStream_t stream) {
+    if (p.T <= 0) return cudaSuccess;
+    if (p.K > 0) {
+        dim3 g1((p.E + 7) / 8, p.T);
+        k_scores<<<g1, 256, 0, stream>>>(p);
+    }
+    const size_t sm = (size_t)p.E * sizeof(float) + (size_t)p.E;
+    k_topk<<<p.T, 32, sm, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace moeb200

@@ -1,0 +1,152 @@
+"""Expert execution backend for the B200.
+
+Drop-in for the backend object the reference's MoE layer drives
+(``OpenVINOExpertBackend``, ``src/flash_moe/backend_ov.py:91-431``): it has
+``forward``, ``forward_batch``, ``prefetch_weights``, ``store``,
+``_moe_executor``, ``begin_decode`` and ``begin_prefill`` with the same
+arguments and results, so ``run_moe_layer`` / ``run_moe_sequence`` (the
+reference's or ``flash_moe_b200.moe_layer``'s) work unchanged.  It adds
+``forward_layer``: the whole layer (routing, the top-k experts, the weighted
+sum and the shared expert) for a batch of tokens in one device call, which
+``flash_moe_b200.moe_layer.run_moe_layer`` uses when present.
+
+Weights never leave HBM; a call moves only the activations (8 KB per token
+in, 8 KB out).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+import torch
+
+from . import _lib
+from .key import ExpertKey
+from .store import ExpertArena
+
+
+class B200ExpertBackend:
+    """Expert backend over an ``ExpertArena``.
+
+    ``fp16_graph`` selects the reference native kernel's binary16 rounding
+    (``cpp/moe_quant_dot.cpp:192-209``) for routed experts; the default is
+    the fp32 arithmetic of ``fp16_graph=0``."""
+
+    def __init__(self, arena: ExpertArena, expert_workers: int = 4,
+                 fp16_graph: bool = False, exact: bool = False):
+        if expert_workers < 1:
+            raise ValueError("thread and worker counts must be positive")
+        self.lib = _lib.load()
+        self.store = arena
+        self.device = arena.device
+        self.tensor_types = arena.tensor_types()
+        self.fp16_graph = bool(fp16_graph)
+        self.exact = bool(exact)
+        self._moe_executor = ThreadPoolExecutor(max_workers=expert_workers)
+        self._native_enabled = False
+        self._tls = threading.local()
+
+    # ---------------------------------------------------------------- policy
+
+    def begin_decode(self):
+        self._native_enabled = True
+
+    def begin_prefill(self):
+        self._native_enabled = False
+
+    def prefetch_weights(self, keys):
+        return self.store.prefetch_many(keys)
+
+    def close(self):
+        self._moe_executor.shutdown(wait=True)
+
+    @property
+    def flags(self) -> int:
+        return (_lib.FP16_GRAPH if self.fp16_graph else 0) | (_lib.EXACT if self.exact else 0)
+
+    # ------------------------------------------------------------ workspaces
+
+    def _workspace(self, dl, tokens: int) -> torch.Tensor:
+        cache = getattr(self._tls, "ws", None)
+        if cache is None:
+            cache = self._tls.ws = {}
+        need = C.c_size_t(0)
+        _lib.check(self.lib.moe_b200_decode_workspace(C.byref(dl.struct), tokens, C.byref(need)),
+                   "moe_b200_decode_workspace")
+        ws = cache.get(self.device)
+        if ws is None or ws.numel() < need.value:
+            ws = torch.empty(max(need.value, 256), dtype=torch.uint8, device=self.device)
+            cache[self.device] = ws
+        return ws
+
+    # -------------------------------------------------------------- forward
+
+    def forward_layer_device(self, layer: int, x: torch.Tensor, y: torch.Tensor,
+                             topk_ids: torch.Tensor | None = None,
+                             topk_weights: torch.Tensor | None = None,
+                             flags: int | None = None, stream=None) -> None:
+        """Asynchronous layer decode on device tensors: x, y fp32 [T, H]."""
+        dl = self.store.layer(layer)
+        t = x.shape[0]
+        s = dl.with_flags(self.flags if flags is None else flags)
+        ws = self._workspace(dl, t)
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        st = self.lib.moe_b200_decode(
+            C.byref(s), x.data_ptr(), t, y.data_ptr(),
+            topk_ids.data_ptr() if topk_ids is not None else None,
+            topk_weights.data_ptr() if topk_weights is not None else None,
+            ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        _lib.check(st, "moe_b200_decode")
+
+    def forward_layer(self, layer: int, activations, return_routing: bool = False):
+        """Whole MoE layer for T tokens (host arrays in, host array out)."""
+        x = np.ascontiguousarray(activations, dtype=np.float32)
+        squeeze = x.ndim == 1
+        x = x.reshape(-1, self.store.layer(layer).weights.hidden)
+        with torch.cuda.device(self.device):
+            xd = torch.from_numpy(x).to(self.device, non_blocking=False)
+            yd = torch.empty_like(xd)
+            k = self.store.layer(layer).weights.top_k
+            ids = torch.empty((x.shape[0], k), dtype=torch.int32, device=self.device)
+            w = torch.empty((x.shape[0], k), dtype=torch.float32, device=self.device)
+            self.forward_layer_device(layer, xd, yd, ids, w)
+            y = yd.cpu().numpy()
+            routing = (ids.cpu().numpy(), w.cpu().numpy())
+        y = y[0] if squeeze else y
+        return (y, routing) if return_routing else y
+
+    def forward(self, key: ExpertKey, activation, hidden_size: int,
+                intermediate_size: int) -> np.ndarray:
+        """One routed expert for one token (reference ``backend_ov.py:385-405``)."""
+        dl = self.store.layer(key.layer)
+        lw = dl.weights
+        if hidden_size != lw.hidden or intermediate_size != lw.inter:
+            raise ValueError("expert shape does not match the resident layer")
+        views = dl.expert_views(key.expert)
+        x = np.ascontiguousarray(activation, dtype=np.float32).reshape(-1)
+        if x.size != hidden_size:
+            raise ValueError("native expert activation shape mismatch")
+        out = np.empty(hidden_size, np.float32)
+        with torch.cuda.device(self.device):
+            st = self.lib.moe_quant_expert(
+                lw.gate_type, views["gate"].data_ptr(), views["gate"].numel(),
+                lw.up_type, views["up"].data_ptr(), views["up"].numel(),
+                lw.down_type, views["down"].data_ptr(), views["down"].numel(),
+                x.ctypes.data, hidden_size, intermediate_size, out.ctypes.data,
+                1 if self.fp16_graph else 0)
+        _lib.check(st, "native expert")
+        return out
+
+    def forward_batch(self, key: ExpertKey, activations: np.ndarray, hidden_size: int,
+                      intermediate_size: int) -> np.ndarray:
+        """One expert for several tokens (reference ``backend_ov.py:407-431``)."""
+        x = np.ascontiguousarray(activations, dtype=np.float32)
+        if x.ndim != 2 or x.shape[1] != hidden_size:
+            raise ValueError(f"expert activations must have shape (tokens, {hidden_size}), "
+                             f"got {x.shape}")
+        if x.shape[0] == 0:
+            return np.empty((0, hidden_size), dtype=np.float32)
+        return np.stack([self.forward(key, row, hidden_size, intermediate_size) for row in x])

@@ -1,0 +1,176 @@
+"""Decode stepping on one GPU or expert-parallel over several.
+
+Expert parallelism (EP): rank r of N holds routed experts
+[r*E/N, (r+1)*E/N) of every layer plus full copies of the router and the
+shared expert.  One decode step for the T tokens each rank owns:
+
+  1. all-gather the N*T tokens (dispatch: every rank sees every token);
+  2. one device call per rank routes all N*T tokens with the replicated
+     router and adds the contributions of the experts it holds (experts held
+     elsewhere contribute zero) -- ``moe_b200_decode`` with NO_SHARED;
+  3. reduce-scatter the N*T partial outputs (combine: each token's owner
+     receives the sum over ranks of the held experts' weighted outputs);
+  4. the owner adds the sigmoid-gated shared expert of its own tokens
+     (``moe_b200_decode`` with SHARED_ONLY).
+
+For one token per rank this moves N*8 KB each way, the same bytes as an
+all-to-all of the tokens to the ranks holding their top-8 experts, with
+fixed-size collectives.  With N = 1 a step is a single device call and no
+collective runs.
+"""
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import _lib
+
+def profiled_traffic(root: Path, name: str = "decode_layer") -> float | None:
+    """DRAM bytes per launch of the decode kernel from the committed ncu
+    summary (``profiles/<name>*.txt`` line ``traffic_bytes_per_launch: N``)."""
+    for p in sorted((root / "profiles").glob(f"{name}*.txt")):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+class DecodeRunner:
+    """Runs decode steps over a rotation of resident layers.
+
+    Step i decodes token ``i % len(tokens)`` of this rank through layer
+    ``layers[i % len(layers)]``."""
+
+    kernel_name = "moe_b200_decode"
+
+    def __init__(self, backend, layers, tokens: torch.Tensor, world: int = 1, rank: int = 0,
+                 max_steps: int = 4096):
+        self.be = backend
+        self.layers = list(layers)
+        self.tokens = tokens                      # [n, H] fp32 on device
+        self.world, self.rank = world, rank
+        dl = backend.store.layer(self.layers[0])
+        self.lw = dl.weights
+        self.dev = tokens.device
+        H, K = self.lw.hidden, self.lw.top_k
+        self.y = torch.empty((1, H), dtype=torch.float32, device=self.dev)
+        self.max_steps = max_steps
+        self.ids = torch.full((max_steps, world, K), -1, dtype=torch.int32, device=self.dev)
+        if world > 1:
+            self.x_all = torch.empty((world, H), dtype=torch.float32, device=self.dev)
+            self.y_part = torch.empty((world, H), dtype=torch.float32, device=self.dev)
+            self.y_routed = torch.empty((1, H), dtype=torch.float32, device=self.dev)
+            self.y_sh = torch.empty((1, H), dtype=torch.float32, device=self.dev)
+        self.launches_per_step = 4 if world == 1 else 7
+        self.recorded = 0
+        self._graph = None
+
+    # ------------------------------------------------------------------ step
+
+    def _flags(self, extra=0):
+        return self.be.flags | extra
+
+    def step(self, i: int, x: torch.Tensor | None = None, y: torch.Tensor | None = None) -> None:
+        layer = self.layers[i % len(self.layers)]
+        x = self.tokens[i % self.tokens.shape[0]].view(1, -1) if x is None else x
+        y = self.y if y is None else y
+        slot = i % self.max_steps
+        self.recorded = max(self.recorded, slot + 1)
+        if self.world == 1:
+            self.be.forward_layer_device(layer, x, y, topk_ids=self.ids[slot])
+            return
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(self.x_all, x)
+        self.be.forward_layer_device(layer, self.x_all, self.y_part, topk_ids=self.ids[slot],
+                                     flags=self._flags(_lib.NO_SHARED))
+        dist.reduce_scatter_tensor(self.y_routed, self.y_part)
+        self.be.forward_layer_device(layer, x, self.y_sh, flags=self._flags(_lib.SHARED_ONLY))
+        torch.add(self.y_routed, self.y_sh, out=y)
+
+    def capture(self, steps: int):
+        """CUDA graph of `steps` consecutive steps (single GPU only)."""
+        if self.world > 1:
+            return None
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for i in range(3):
+                self.step(i)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                self.step(i)
+        torch.cuda.synchronize()
+        self._graph = g
+        return g
+
+    # ------------------------------------------------------------ accounting
+
+    def algorithmic_bytes(self, steps: int) -> int:
+        """Packed weight + router + gate-vector bytes this rank's steps must
+        read: the distinct held experts each step's tokens select, the
+        shared expert and router once per step."""
+        lw = self.lw
+        per_expert = lw.expert_bytes
+        ids = self.ids[:min(steps, self.max_steps)].cpu().numpy()
+        dl = self.be.store.layer(self.layers[0])
+        total = 0
+        for step_ids in ids:
+            sel = np.unique(step_ids[step_ids >= 0])
+            held = sel[(sel >= dl.expert_begin) & (sel < dl.expert_begin + dl.expert_count)]
+            total += len(held) * per_expert
+        total += steps * (lw.shared_bytes + lw.router.nbytes + lw.hidden * 4)
+        return int(total)
+
+    # ------------------------------------------------------------------ e2e
+
+    def e2e(self, steps: int, warmup: int) -> dict:
+        """The same steps through host memory: each step copies its token from
+        pinned host memory, decodes, and reads the result back to pinned
+        host memory, synchronising like a caller that consumes the result."""
+        H = self.lw.hidden
+        n = self.tokens.shape[0]
+        host_x = torch.empty((n, H), dtype=torch.float32).pin_memory()
+        host_x.copy_(self.tokens.cpu())
+        host_y = torch.empty((1, H), dtype=torch.float32).pin_memory()
+        xd = torch.empty((1, H), dtype=torch.float32, device=self.dev)
+        stream = torch.cuda.current_stream(self.dev)
+
+        def one(i):
+            xd.copy_(host_x[i % n].view(1, -1), non_blocking=True)
+            self.step(i, x=xd)
+            host_y.copy_(self.y, non_blocking=True)
+            stream.synchronize()
+
+        for i in range(warmup):
+            one(i)
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            one(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        t = torch.tensor([ms], device=self.dev)
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        byts = self.algorithmic_bytes(steps)
+        bt = torch.tensor([float(byts)], device=self.dev, dtype=torch.float64)
+        if self.world > 1:
+            dist.all_reduce(bt)
+        return {"value": round(float(bt.item()) / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
+                "us_per_token": round(ms * 1e3 / steps, 3),
+                "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4}
+
+    def close(self):
+        self._graph = None

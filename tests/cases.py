@@ -1,0 +1,90 @@
+"""Seeded test cases shared by the golden generator and the tests.
+
+Every case is regenerated from seeds; the golden fixtures store a digest of
+the generated inputs so that a drift of the generator is caught.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from flash_moe_b200 import synth
+from flash_moe_b200.formats import BLOCK, Q4_K, Q6_K, Q8_0
+
+import oracle as O
+
+# type triples of the reference's native test
+# (tools/test_optimized_inference.py:237-238)
+TRIPLES = [(8, 11, 12), (11, 12, 13), (12, 13, 14), (13, 14, 8), (14, 8, 11),
+           (12, 12, 14), (12, 12, 8), (11, 11, 11)]
+
+# name -> (synth.make_layer kwargs, token count)
+LAYER_SPECS = {
+    "small": (dict(seed=5, hidden=512, inter=256, n_experts=16, top_k=4, shared_inter=256), 4),
+    "small_q4": (dict(seed=6, hidden=512, inter=256, n_experts=12, top_k=3, gate_type=Q4_K,
+                      up_type=Q4_K, down_type=Q8_0, shared_inter=256,
+                      shared_types=(Q6_K, Q6_K, Q6_K)), 3),
+    "cfg2": (dict(seed=2), 2),
+}
+
+
+def small_expert_inputs(kinds, seed_stream: int):
+    """The value pattern of the reference's native test
+    (``tools/test_optimized_inference.py:239-252``): random bytes with
+    d = 0.002 (and dmin = 0.001), a 256x256 expert, x ~ N(0,1)*0.005."""
+    rng = np.random.default_rng(np.random.SeedSequence([17, seed_stream]))
+    tensors = {}
+    for name, kind in zip(("gate", "up", "down"), kinds):
+        bs, size = BLOCK[kind]
+        raw = rng.integers(0, 256, (256 * (256 // bs), size), np.uint8)
+        offset = size - 2 if kind in (11, 14) else 0
+        raw[:, offset:offset + 2] = np.frombuffer(np.float16(.002).tobytes(), np.uint8)
+        if kind in (12, 13):
+            raw[:, 2:4] = np.frombuffer(np.float16(.001).tobytes(), np.uint8)
+        tensors[name] = raw.reshape(-1)
+    x = (rng.standard_normal(256) * .005).astype(np.float32)
+    return tensors, x
+
+
+def layer_case(name: str):
+    kw, count = LAYER_SPECS[name]
+    lw = synth.make_layer(**kw)
+    xs = synth.make_tokens(kw["seed"], count, lw.hidden)
+    return lw, xs
+
+
+def layer_digest(lw, xs) -> str:
+    extra = [lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_inp] if lw.shared_inter else []
+    return synth.digest(lw.gate, lw.up, lw.down, lw.router, *extra, xs)
+
+
+def oracle_shared_weights(lib, lw):
+    """fp32 shared-expert weights as the reference loads them (binary16
+    rounding, ``shared_expert.py:380-390``), or None."""
+    if not lw.shared_inter:
+        return None
+    return O.shared_weights_from_packed(lib, lw.shared(), lw.shared_kinds, lw.hidden,
+                                        lw.shared_inter, lw.shared_gate_inp)
+
+
+def oracle_layer(lib, lw, xs, fp16_graph: int = 0, selections=None):
+    """The oracle's layer output per token: (y [T,H], ids, weights)."""
+    shared = oracle_shared_weights(lib, lw)
+    gate_he = lw.gate_he()
+    if lw.router_bias is not None:
+        raise NotImplementedError("use oracle_layer_biased")
+
+    def expert_fn(e, x):
+        rc, y = lib.expert(lw.expert(e), lw.kinds, x, lw.hidden, lw.inter, fp16_graph)
+        if rc:
+            raise RuntimeError(f"native expert failed with status {rc}")
+        return y
+
+    ys, ids, ws = [], [], []
+    for i, x in enumerate(xs):
+        sel = selections[i] if selections is not None else None
+        y, e, w = O.run_moe_layer(x, gate_he, lw.top_k, expert_fn, shared, workers=1,
+                                  selection=sel)
+        ys.append(y)
+        ids.append(e)
+        ws.append(w)
+    return np.stack(ys), np.array(ids), np.array(ws)

@@ -1,0 +1,116 @@
+"""Whole-layer decode on the GPU (moe_b200_decode through the C ABI) against
+the oracle restatement of the reference's run_moe_layer.
+
+Routing: the device's top-k ids must equal the oracle's, except where the
+k-th and (k+1)-th scores are within 1e-5 relative (a near tie that fp32
+summation order can flip); then the oracle is re-run with the device's
+selection.  Outputs: max|y - ref| / max|ref| <= 1e-3."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from cases import LAYER_SPECS, layer_case, oracle_layer
+from flash_moe_b200 import synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def _arena_backend(lw, **kw):
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    arena = ExpertArena()
+    arena.add_layer(0, lw)
+    return B200ExpertBackend(arena, **kw)
+
+
+def check_layer(oracle, lw, xs, y, ids, w, fp16_graph=0, tol=TOL):
+    want_y, want_ids, want_w = oracle_layer(oracle, lw, xs, fp16_graph)
+    sel = None
+    if not np.array_equal(np.asarray(ids), want_ids):
+        scores = np.stack([O.route(x, lw.gate_he(), lw.top_k)[2] for x in xs])
+        for t in range(len(xs)):
+            s = np.sort(scores[t])[::-1]
+            k = lw.top_k
+            assert abs(s[k - 1] - s[k]) <= 1e-5 * max(abs(s[k - 1]), 1e-30), \
+                f"token {t}: routing differs without a near tie: {ids[t]} vs {want_ids[t]}"
+        sel = [(list(map(int, ids[t])), [float(v) for v in w[t]]) for t in range(len(xs))]
+        want_y, _, want_w = oracle_layer(oracle, lw, xs, fp16_graph, selections=sel)
+    np.testing.assert_allclose(np.asarray(w), want_w, rtol=1e-6, atol=1e-7)
+    err = O.max_relative_error(y, want_y)
+    assert err <= tol, err
+    return err
+
+
+@pytest.mark.parametrize("name", list(LAYER_SPECS))
+@pytest.mark.parametrize("exact", [False, True])
+def test_decode_layer_matches_oracle(oracle, name, exact):
+    lw, xs = layer_case(name)
+    be = _arena_backend(lw, exact=exact)
+    y, (ids, w) = be.forward_layer(0, xs, return_routing=True)
+    check_layer(oracle, lw, xs, y, ids, w)
+
+
+@pytest.mark.parametrize("name", list(LAYER_SPECS))
+def test_decode_layer_matches_reference_golden(golden, name):
+    g = golden(f"layer_{name}")
+    lw, xs = layer_case(name)
+    be = _arena_backend(lw)
+    y, (ids, w) = be.forward_layer(0, xs, return_routing=True)
+    np.testing.assert_array_equal(ids, g["ids"])
+    assert O.max_relative_error(y, g["y"]) <= TOL
+
+
+def test_decode_layer_fp16_graph_matches_stock_reference(golden):
+    """Routed experts with the stock NativeExpert rounding (fp16_graph=1)."""
+    g = golden("layer_small")
+    lw, xs = layer_case("small")
+    be = _arena_backend(lw, fp16_graph=True, exact=True)
+    y = be.forward_layer(0, xs)
+    assert O.max_relative_error(y, g["y_stock"]) <= 5e-3
+
+
+@pytest.mark.parametrize("tokens", [1, 7, 64])
+def test_decode_batched_tokens(oracle, tokens):
+    lw = synth.make_layer(seed=11, hidden=512, inter=256, n_experts=32, top_k=8, shared_inter=256)
+    xs = synth.make_tokens(11, tokens, lw.hidden)
+    be = _arena_backend(lw)
+    y, (ids, w) = be.forward_layer(0, xs, return_routing=True)
+    check_layer(oracle, lw, xs, y, ids, w)
+
+
+def test_decode_run_twice_bit_identical():
+    lw, xs = layer_case("small")
+    be = _arena_backend(lw)
+    a = be.forward_layer(0, xs)
+    b = be.forward_layer(0, xs)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_run_moe_layer_drop_in_uses_fused_path(oracle):
+    from flash_moe_b200.moe_layer import run_moe_layer, run_moe_sequence
+    lw, xs = layer_case("small")
+    be = _arena_backend(lw)
+    router = type("R", (), {"top_k": lw.top_k})()
+    y = np.stack([run_moe_layer(0, x, router, be, lw.hidden, lw.inter) for x in xs])
+    ys = run_moe_sequence(0, xs, router, be, lw.hidden, lw.inter)
+    want, _, _ = oracle_layer(oracle, lw, xs)
+    assert O.max_relative_error(y, want) <= TOL
+    assert O.max_relative_error(ys, want) <= TOL
+
+
+def test_backend_per_expert_forward_matches_oracle(oracle):
+    from flash_moe_b200.key import ExpertKey
+    lw, xs = layer_case("small")
+    be = _arena_backend(lw)
+    for e in (0, 5, 15):
+        got = be.forward(ExpertKey(0, e), xs[0], lw.hidden, lw.inter)
+        _, want = oracle.expert(lw.expert(e), lw.kinds, xs[0], lw.hidden, lw.inter, 0)
+        assert O.max_relative_error(got, want) <= TOL
+    got = be.forward_batch(ExpertKey(0, 3), xs, lw.hidden, lw.inter)
+    for t in range(len(xs)):
+        _, want = oracle.expert(lw.expert(3), lw.kinds, xs[t], lw.hidden, lw.inter, 0)
+        assert O.max_relative_error(got[t], want) <= TOL
+    assert be.forward_batch(ExpertKey(0, 3), xs[:0], lw.hidden, lw.inter).shape == (0, lw.hidden)
