@@ -305,8 +305,8 @@ def run_gpu(args) -> None:
         cpu = {"value": round(step_bytes(8) / per_tok / 1e9, 4), "unit": UNIT,
                "cores": os.cpu_count() or 1, "kind": kind,
                "sample": f"{n} tokens of the same layer ({per_tok * 1e6:.0f} us/token), {cpu_model()}"}
-    if graph is not None:
-        del graph
+    used_graph = graph is not None
+    graph = None
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": UNIT, "n_gpus": world,
@@ -321,7 +321,7 @@ def run_gpu(args) -> None:
                        "l2": f"rotating {args.copies} layer copies at distinct addresses "
                              f"({args.copies * step_bytes(8) / 1e6:.0f} MB touched per rotation > 2x L2)",
                        "parallelism": f"ep{world}" if world > 1 else "single",
-                       "engine": args.engine, "cuda_graph": graph is not None or not args.no_graph,
+                       "engine": args.engine, "cuda_graph": used_graph,
                        "algorithmic_bytes_per_token": step_bytes(8)},
             "roofline": roof,
             "e2e": e2e,

@@ -121,7 +121,10 @@ typedef struct moe_b200_layer {
 #define MOE_B200_EXACT        4  /* use the exact (fp32 dequant + FMA) engine */
 #define MOE_B200_SHARED_ONLY  8  /* only the shared expert (no routing, no routed experts) */
 
-/* Bytes of workspace moe_b200_decode needs for `max_tokens` tokens. */
+/* Bytes of workspace moe_b200_decode needs for `max_tokens` tokens.  The
+ * workspace is 256-byte aligned device memory; zero it once with
+ * moe_b200_workspace_init before its first use.  Calls sharing one
+ * workspace must be ordered (same stream). */
 MOE_B200_API int moe_b200_decode_workspace(const moe_b200_layer* layer, int32_t max_tokens,
                               size_t* bytes);
 
@@ -140,10 +143,29 @@ MOE_B200_API int moe_b200_decode(const moe_b200_layer* layer, const float* x, in
                     float* y, int32_t* topk_ids, float* topk_weights,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Zero the workspace's control words (its first 256 bytes) on `stream`.
+ * Call once after allocating a decode workspace; the decode kernels leave
+ * them zero again when they finish. */
+MOE_B200_API int moe_b200_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Synchronously read (and clear) the device-side error word of a
+ * workspace: 0, or -9 when a bounded wait of a decode launch gave up. */
+MOE_B200_API int moe_b200_workspace_error(void* workspace, void* stream, int* error);
+
 /* Device-pointer dequantisation on a stream: out_dtype 0 = fp32,
  * 1 = binary16 (round to nearest even).  Same values as dequant_k. */
 MOE_B200_API int moe_b200_dequant(int type, const void* src, void* dst, int64_t n, int out_dtype,
                      void* stream);
+
+/* Phase tracing of the fused decode kernel: while set, every fused launch
+ * from this thread writes, per CTA c, 32 uint64 global-timer stamps (ns)
+ * to device_buffer[32 * c ...] at its phase boundaries (0 entry, 1 token
+ * quantised, 2 first copies landed, 3 router done, 4 shared gate/up done,
+ * 5 routing known, 6 top-k done, 7 routed gate/up done, 8 after barrier,
+ * 9 all activations published, 10 down inputs ready, 11 down done, 12 exit;
+ * 13-15 inside the top-k, 16-22 inside the routed and down phases).  capacity_ctas must cover the grid (one CTA
+ * per SM).  NULL switches tracing off. */
+MOE_B200_API int moe_b200_set_trace(void* device_buffer, int capacity_ctas);
 
 /* cudaError_t of the last failed CUDA call on this thread (0 if none). */
 MOE_B200_API int moe_b200_last_cuda_error(void);

@@ -34,7 +34,7 @@ int sm_count() {
     return cache[dev];
 }
 
-static inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+static inline size_t align256(size_t v) { return align_up(v); }
 
 // Per-thread scratch on one device: a stream and a growable device buffer.
 struct Scratch {
@@ -151,6 +151,7 @@ static DecodeWs decode_ws(const moe_b200_layer* L, int T) {
     const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate
                                                               : L->intermediate;
     Stager s;
+    s.used = 256;  // counters and error word of the fused kernel
     DecodeWs w;
     w.scores = s.take((size_t)T * L->n_experts * 4);
     w.ids = s.take((size_t)T * L->top_k * 4);
@@ -158,6 +159,8 @@ static DecodeWs decode_ws(const moe_b200_layer* L, int T) {
     w.sg = s.take((size_t)T * 4);
     w.act = s.take((size_t)T * (L->top_k + 1) * Imax * 4);
     w.total = s.used;
+    const size_t fused = fused_workspace_bytes(L);
+    if (fused > w.total) w.total = fused;
     return w;
 }
 
@@ -169,7 +172,30 @@ extern "C" {
 
 int moe_b200_version(void) { return 100; }
 
+int moe_b200_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+    if (!workspace || workspace_bytes < 256) return ST_ARG;
+    cudaError_t e = cudaMemsetAsync(workspace, 0, 256, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ST_OK : fail(e, ST_CUDA);
+}
+
+int moe_b200_workspace_error(void* workspace, void* stream, int* error) {
+    if (!workspace || !error) return ST_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int* word = reinterpret_cast<int*>(static_cast<char*>(workspace) + 32);
+    cudaError_t e = cudaMemcpyAsync(error, word, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess && *error != 0) e = cudaMemsetAsync(word, 0, sizeof(int), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? ST_OK : fail(e, ST_CUDA);
+}
+
 int moe_b200_last_cuda_error(void) { return tl_last_cuda; }
+
+int moe_b200_set_trace(void* device_buffer, int capacity_ctas) {
+    if (device_buffer && capacity_ctas < 1) return ST_ARG;
+    set_fused_trace(device_buffer, device_buffer ? capacity_ctas : 0);
+    return ST_OK;
+}
 
 int dequant_k_supported(int type) { return supported(type) ? 1 : 0; }
 
@@ -331,6 +357,14 @@ int moe_b200_decode(const moe_b200_layer* L, const float* x, int32_t T, float* y
     const bool shared_only = (L->flags & MOE_B200_SHARED_ONLY) != 0;
     const bool with_shared = L->shared_intermediate > 0 && !(L->flags & MOE_B200_NO_SHARED);
     if (shared_only && !with_shared) return ST_ARG;
+
+    if (fused_supported(L, T, L->flags)) {
+        bool launched = false;
+        cudaError_t fe = launch_decode_fused(L, L->flags, x, y, topk_ids, topk_weights, workspace, s,
+                                             &launched);
+        if (fe != cudaSuccess) return fail(fe, ST_CUDA);
+        if (launched) return ST_OK;
+    }
 
     RoutePlan r{};
     r.T = T;

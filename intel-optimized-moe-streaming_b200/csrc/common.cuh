@@ -38,7 +38,9 @@ __host__ __device__ constexpr int block_bytes(int t) {
 
 inline bool supported(int t) { return block_size(t) != 0; }
 
-inline int64_t row_bytes(int t, int cols) {
+inline size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
+
+__host__ __device__ inline int64_t row_bytes(int t, int cols) {
     return (int64_t)(cols / block_size(t)) * block_bytes(t);
 }
 

@@ -45,4 +45,14 @@ struct ExactPlan {
 };
 cudaError_t launch_exact(const ExactPlan& p, cudaStream_t stream);
 
+// Fused single-token layer decode (decode.cu).  The first 256 bytes of the
+// workspace hold its counters and error word (zero before the first launch;
+// the kernel leaves them zero).
+bool fused_supported(const moe_b200_layer* L, int T, int flags);
+size_t fused_workspace_bytes(const moe_b200_layer* L);
+cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float* x, float* y,
+                                int32_t* ids_out, float* w_out, void* ws, cudaStream_t stream,
+                                bool* launched);
+void set_fused_trace(void* buf, int capacity_ctas);
+
 }  // namespace moeb200

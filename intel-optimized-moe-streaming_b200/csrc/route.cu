@@ -14,6 +14,7 @@
 #include <math.h>
 
 #include "launch.h"
+#include "topk.cuh"
 
 namespace moeb200 {
 
@@ -44,89 +45,22 @@ __global__ void __launch_bounds__(256) k_scores(RoutePlan p) {
     }
 }
 
-// numpy's pairwise summation of n <= 128 float64 values (np.add.reduce on a
-// contiguous array): sequential below 8, eight interleaved partial sums
-// combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) from 8 on.
-__device__ double np_sum(const double* v, int n) {
-    if (n < 8) {
-        double r = 0.0;
-        for (int i = 0; i < n; ++i) r += v[i];
-        return r;
-    }
-    double r[8];
-    for (int j = 0; j < 8; ++j) r[j] = v[j];
-    int i = 8;
-    for (; i < n - (n % 8); i += 8)
-        for (int j = 0; j < 8; ++j) r[j] += v[i + j];
-    double res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
-    for (; i < n; ++i) res += v[i];
-    return res;
-}
-
-constexpr int kMaxTopK = 16;
-
 __global__ void __launch_bounds__(32) k_topk(RoutePlan p) {
     extern __shared__ float s_scores[];
     unsigned char* taken = reinterpret_cast<unsigned char*>(s_scores + p.E);
     const int t = blockIdx.x, lane = threadIdx.x;
-    for (int e = lane; e < p.E && p.K > 0; e += 32) {
-        s_scores[e] = p.scores[(size_t)t * p.E + e];
-        taken[e] = 0;
-    }
-    __syncwarp();
-    float sel_v[kMaxTopK];
-    int sel_i[kMaxTopK];
-    for (int k = 0; k < p.K; ++k) {
-        float best = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int e = lane; e < p.E; e += 32) {
-            const float v = s_scores[e];
-            if (!taken[e] && (v > best || (v == best && e < bi) || bi == 0x7fffffff)) {
-                best = v;
-                bi = e;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > best || (ov == best && oi < bi))) {
-                best = ov;
-                bi = oi;
-            }
-        }
-        if (lane == 0) taken[bi] = 1;
+    if (p.K > 0) {
+        for (int e = lane; e < p.E; e += 32) s_scores[e] = p.scores[(size_t)t * p.E + e];
         __syncwarp();
-        sel_v[k] = best;
-        sel_i[k] = bi;
-    }
-    if (lane == 0 && p.K > 0) {
-        double m = (double)sel_v[0];
-        for (int k = 1; k < p.K; ++k) m = fmax(m, (double)sel_v[k]);
-        double ex[kMaxTopK];
-        for (int k = 0; k < p.K; ++k) ex[k] = exp((double)sel_v[k] - m);
-        const double tot = np_sum(ex, p.K);
-        const bool uniform = !isfinite(tot) || tot <= 0.0;
-        for (int k = 0; k < p.K; ++k) {
-            p.ids[(size_t)t * p.K + k] = sel_i[k];
-            p.w[(size_t)t * p.K + k] = uniform ? (float)(1.0 / p.K) : (float)(ex[k] / tot);
-        }
+        topk_softmax_warp(s_scores, taken, p.E, p.K, p.ids + (size_t)t * p.K,
+                          p.w + (size_t)t * p.K);
     }
     if (p.gate_inp) {
         const float* xr = p.x + (size_t)t * p.H;
         float acc = 0.f;
         for (int i = lane; i < p.H; i += 32) acc = fmaf(xr[i], p.gate_inp[i], acc);
         acc = warp_sum(acc);
-        if (lane == 0) {
-            float g;
-            if (acc >= 0.f) {
-                g = 1.0f / (1.0f + expf(-acc));
-            } else {
-                const float e = expf(acc);
-                g = e / (1.0f + e);
-            }
-            p.sg[t] = g;
-        }
+        if (lane == 0) p.sg[t] = shared_sigmoid(acc);
     }
 }
 

@@ -77,9 +77,22 @@ class B200ExpertBackend:
                    "moe_b200_decode_workspace")
         ws = cache.get(self.device)
         if ws is None or ws.numel() < need.value:
-            ws = torch.empty(max(need.value, 256), dtype=torch.uint8, device=self.device)
+            ws = torch.zeros(max(need.value, 256), dtype=torch.uint8, device=self.device)
             cache[self.device] = ws
         return ws
+
+    def device_errors(self) -> int:
+        """Read and clear the device error word of this thread's workspace
+        (-9 when a bounded wait inside a decode kernel gave up)."""
+        cache = getattr(self._tls, "ws", None) or {}
+        ws = cache.get(self.device)
+        if ws is None:
+            return 0
+        err = C.c_int(0)
+        _lib.check(self.lib.moe_b200_workspace_error(
+            ws.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream, C.byref(err)),
+            "moe_b200_workspace_error")
+        return err.value
 
     # -------------------------------------------------------------- forward
 

@@ -121,14 +121,18 @@ class ReferenceLibrary(_KQuantLib):
 
 # ---------------------------------------------------------------- numpy layer
 
-def route(x: np.ndarray, gate_he: np.ndarray, top_k: int):
+def route(x: np.ndarray, gate_he: np.ndarray, top_k: int, bias: np.ndarray | None = None):
     """Top-k ids and softmax weights of one token.
 
     Restates ``ExpertRouter.scores/route`` (``src/flash_moe/router.py:241-271``):
     fp32 ``x @ W`` with W laid out (hidden, experts), ``argsort`` ascending,
-    the last k reversed, a float64 softmax over those k only."""
+    the last k reversed, a float64 softmax over those k only.  ``bias`` (an
+    fp32 per-expert logit offset, the popularity skew of the batched-decode
+    benchmark; the reference router has none) is added to the fp32 scores."""
     x = np.asarray(x, dtype=np.float32).reshape(-1)
     scores = (x @ np.asarray(gate_he, dtype=np.float32)).astype(np.float32)
+    if bias is not None:
+        scores = (scores + np.asarray(bias, dtype=np.float32)).astype(np.float32)
     ids = np.argsort(scores)[-top_k:][::-1].astype(np.int64).tolist()
     top = scores[ids].astype(np.float64)
     e = np.exp(top - np.max(top))
@@ -190,7 +194,7 @@ def shared_weights_from_packed(lib: _KQuantLib, packed: dict, kinds: dict,
 
 
 def run_moe_layer(x, gate_he, top_k, expert_fn, shared=None, workers: int = 4,
-                  selection=None):
+                  selection=None, bias=None):
     """One token through one MoE layer.
 
     Restates ``run_moe_layer`` (``src/flash_moe/moe_layer.py:39-107``): the k
@@ -200,7 +204,7 @@ def run_moe_layer(x, gate_he, top_k, expert_fn, shared=None, workers: int = 4,
     (ids, weights) pair, used when the device's routing resolved a near tie
     differently.  Returns (y, ids, weights)."""
     if selection is None:
-        ids, weights, _ = route(x, gate_he, top_k)
+        ids, weights, _ = route(x, gate_he, top_k, bias)
     else:
         ids, weights = selection
     combined = np.zeros(np.asarray(x).size, dtype=np.float32)

@@ -8,7 +8,7 @@ from __future__ import annotations
 import numpy as np
 
 from flash_moe_b200 import synth
-from flash_moe_b200.formats import BLOCK, Q4_K, Q6_K, Q8_0
+from flash_moe_b200.formats import BLOCK, Q3_K, Q4_K, Q5_K, Q6_K, Q8_0
 
 import oracle as O
 
@@ -24,6 +24,21 @@ LAYER_SPECS = {
                       up_type=Q4_K, down_type=Q8_0, shared_inter=256,
                       shared_types=(Q6_K, Q6_K, Q6_K)), 3),
     "cfg2": (dict(seed=2), 2),
+}
+
+# Layers whose every tensor the fused single-token kernel takes (rows a
+# multiple of 16 bytes, 256..2048 columns): every block format, each lane
+# grouping (H = 2048, 1024, 512 -> 32, 16, 8 lanes per row), a router bias.
+FUSED_SPECS = {
+    "f_q3q4q8": (dict(seed=21, n_experts=32), 3),
+    "f_q6q5q8": (dict(seed=22, n_experts=16, top_k=4, gate_type=Q6_K, up_type=Q5_K,
+                      down_type=Q8_0, shared_types=(Q4_K, Q4_K, Q5_K)), 3),
+    "f_h1024": (dict(seed=23, hidden=1024, inter=256, n_experts=16, top_k=6, gate_type=Q4_K,
+                     up_type=Q4_K, down_type=Q8_0, shared_inter=512), 3),
+    "f_h512_bias": (dict(seed=24, hidden=512, inter=512, n_experts=64, top_k=8, gate_type=Q4_K,
+                         up_type=Q8_0, down_type=Q5_K, shared_inter=256,
+                         shared_types=(Q8_0, Q4_K, Q8_0), zipf_s=1.1), 3),
+    "f_noshared": (dict(seed=25, n_experts=8, top_k=2, shared_inter=0), 2),
 }
 
 
@@ -46,7 +61,7 @@ def small_expert_inputs(kinds, seed_stream: int):
 
 
 def layer_case(name: str):
-    kw, count = LAYER_SPECS[name]
+    kw, count = LAYER_SPECS[name] if name in LAYER_SPECS else FUSED_SPECS[name]
     lw = synth.make_layer(**kw)
     xs = synth.make_tokens(kw["seed"], count, lw.hidden)
     return lw, xs
@@ -70,8 +85,6 @@ def oracle_layer(lib, lw, xs, fp16_graph: int = 0, selections=None):
     """The oracle's layer output per token: (y [T,H], ids, weights)."""
     shared = oracle_shared_weights(lib, lw)
     gate_he = lw.gate_he()
-    if lw.router_bias is not None:
-        raise NotImplementedError("use oracle_layer_biased")
 
     def expert_fn(e, x):
         rc, y = lib.expert(lw.expert(e), lw.kinds, x, lw.hidden, lw.inter, fp16_graph)
@@ -83,7 +96,7 @@ def oracle_layer(lib, lw, xs, fp16_graph: int = 0, selections=None):
     for i, x in enumerate(xs):
         sel = selections[i] if selections is not None else None
         y, e, w = O.run_moe_layer(x, gate_he, lw.top_k, expert_fn, shared, workers=1,
-                                  selection=sel)
+                                  selection=sel, bias=lw.router_bias)
         ys.append(y)
         ids.append(e)
         ws.append(w)

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from cases import LAYER_SPECS, layer_case, oracle_layer
+from cases import FUSED_SPECS, LAYER_SPECS, layer_case, oracle_layer
 from flash_moe_b200 import synth
 
 pytestmark = pytest.mark.gpu
@@ -30,7 +30,7 @@ def check_layer(oracle, lw, xs, y, ids, w, fp16_graph=0, tol=TOL):
     want_y, want_ids, want_w = oracle_layer(oracle, lw, xs, fp16_graph)
     sel = None
     if not np.array_equal(np.asarray(ids), want_ids):
-        scores = np.stack([O.route(x, lw.gate_he(), lw.top_k)[2] for x in xs])
+        scores = np.stack([O.route(x, lw.gate_he(), lw.top_k, lw.router_bias)[2] for x in xs])
         for t in range(len(xs)):
             s = np.sort(scores[t])[::-1]
             k = lw.top_k
@@ -51,6 +51,18 @@ def test_decode_layer_matches_oracle(oracle, name, exact):
     be = _arena_backend(lw, exact=exact)
     y, (ids, w) = be.forward_layer(0, xs, return_routing=True)
     check_layer(oracle, lw, xs, y, ids, w)
+
+
+@pytest.mark.parametrize("name", list(FUSED_SPECS))
+def test_fused_decode_every_format(oracle, name):
+    """One token at a time through the fused kernel (the fast engine),
+    every block format and lane grouping, against the oracle."""
+    lw, xs = layer_case(name)
+    be = _arena_backend(lw)
+    for t in range(len(xs)):
+        y, (ids, w) = be.forward_layer(0, xs[t:t + 1], return_routing=True)
+        check_layer(oracle, lw, xs[t:t + 1], y, ids, w)
+    assert be.device_errors() == 0
 
 
 @pytest.mark.parametrize("name", list(LAYER_SPECS))
@@ -81,12 +93,14 @@ def test_decode_batched_tokens(oracle, tokens):
     check_layer(oracle, lw, xs, y, ids, w)
 
 
-def test_decode_run_twice_bit_identical():
-    lw, xs = layer_case("small")
+@pytest.mark.parametrize("name", ["small", "f_q3q4q8"])
+def test_decode_run_twice_bit_identical(name):
+    lw, xs = layer_case(name)
     be = _arena_backend(lw)
-    a = be.forward_layer(0, xs)
-    b = be.forward_layer(0, xs)
-    np.testing.assert_array_equal(a, b)
+    a = [be.forward_layer(0, xs[t:t + 1]) for t in range(len(xs))]
+    b = [be.forward_layer(0, xs[t:t + 1]) for t in range(len(xs))]
+    np.testing.assert_array_equal(np.stack(a), np.stack(b))
+    assert be.device_errors() == 0
 
 
 def test_run_moe_layer_drop_in_uses_fused_path(oracle):
