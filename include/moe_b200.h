@@ -152,6 +152,11 @@ MOE_B200_API int moe_b200_workspace_init(void* workspace, size_t workspace_bytes
  * workspace: 0, or -9 when a bounded wait of a decode launch gave up. */
 MOE_B200_API int moe_b200_workspace_error(void* workspace, void* stream, int* error);
 
+/* Number of kernels one moe_b200_decode call with this layer, token count
+ * and the layer's flags launches (1 for the fused single-token path). */
+MOE_B200_API int moe_b200_decode_kernels(const moe_b200_layer* layer, int32_t tokens,
+                                         int* kernels);
+
 /* Device-pointer dequantisation on a stream: out_dtype 0 = fp32,
  * 1 = binary16 (round to nearest even).  Same values as dequant_k. */
 MOE_B200_API int moe_b200_dequant(int type, const void* src, void* dst, int64_t n, int out_dtype,

@@ -335,6 +335,19 @@ int moe_b200_dequant(int type, const void* src, void* dst, int64_t n, int out_dt
     return e == cudaSuccess ? ST_OK : fail(e, ST_CUDA);
 }
 
+int moe_b200_decode_kernels(const moe_b200_layer* L, int32_t T, int* kernels) {
+    const int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (T < 1 || !kernels) return ST_ARG;
+    if (fused_supported(L, T, L->flags)) {
+        *kernels = 1;
+    } else {
+        const bool shared_only = (L->flags & MOE_B200_SHARED_ONLY) != 0;
+        *kernels = (shared_only ? 1 : 2) + 2;  // [scores,] top-k/gate, gate/up, down
+    }
+    return ST_OK;
+}
+
 int moe_b200_decode_workspace(const moe_b200_layer* L, int32_t max_tokens, size_t* bytes) {
     const int st = check_layer(L);
     if (st != ST_OK) return st;

@@ -25,6 +25,7 @@
 // no CTA waits for another to publish it.  Exchanges through global memory:
 // E scores, the A*I + Is fp32 activations, the shared gate value.
 #include <math.h>
+#include <stdlib.h>
 
 #include "launch.h"
 #include "qdot.cuh"
@@ -57,6 +58,7 @@ struct FusedParams {
     int max_router_rows, max_sgu_rows, max_out_rows, max_rgu_rows;
     int lpr_h, lpr_i, lpr_is;
     int chunk_rows;
+    int warm;
     uint32_t o_x32, o_xq, o_router, o_sgate, o_sup, o_sdown, o_rgate, o_rup, o_rdown;
     uint32_t o_act, o_aq, o_misc, total;
 };
@@ -156,6 +158,34 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     const int lpr_h = p.lpr_h, sub_h = lane / lpr_h, pr_h = lane % lpr_h;
     XLane xl;
     load_xlane(xl, xq, pr_h >> 2, pr_h & 3);
+
+    // ---- instruction-cache warm-up while the first copies are in flight.
+    // Each kernel launch runs its critical-path code once per CTA, so every
+    // phase would otherwise start on cold instruction caches.  Here the
+    // decoders and the top-k run once on dummy data (4 warps per region, one
+    // per SM sub-partition); their results feed a store guarded by a
+    // condition that never holds (G > 0), so nothing is written.
+    if (p.warm) {
+        float dummy = 0.f;
+        const uint8_t* junk = sm + p.o_x32;
+        const int region = warp >> 2;
+        if (region == 0) {
+            dummy = qdot_t<GU>(L.gate_type, junk, 0, lane & 3, xl);
+        } else if (region == 1) {
+            dummy = qdot_t<DN>(L.down_type, junk, 0, lane & 3, xl);
+        } else if (region == 2) {
+            if (Is)
+                dummy = qdot_t<SGU>(L.shared_gate_type, junk, 0, lane & 3, xl) +
+                        qdot_t<SDN>(L.shared_down_type, junk, 0, lane & 3, xl);
+        } else if (E <= 256) {
+            int di[kMaxTopK];
+            float dw[kMaxTopK];
+            topk_softmax_warp_fast(p.scores, E, K, di, dw);
+            dummy = dw[lane % K] + (float)di[lane % K];
+        }
+        dummy = group_sum(dummy, 32);
+        if (G < 0 && dummy == 1.2345f) p.y[0] = dummy;
+    }
 
     if (!mbar_wait(&bars[0], 0, kWaitPolls) && tid == 0) set_error(p.ctr, ST_TIMEOUT);
     __syncthreads();
@@ -350,15 +380,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     __syncthreads();
     TRACE(10);
 
-    // ---- down rows [h0, h1) of every vector: item = (vector, row group)
+    // ---- down rows [h0, h1) of every vector: item = (vector, pair of row
+    // groups); the activation codes are loaded once per item
     {
         const int rpw_i = 32 / p.lpr_i, rpw_s = 32 / p.lpr_is;
         const int ng_i = (nh + rpw_i - 1) / rpw_i, ng_s = Is ? (nh + rpw_s - 1) / rpw_s : 0;
-        for (int it = warp; it < A * ng_i + ng_s; it += nw) {
-            const bool sh = it >= A * ng_i;
-            const int v = sh ? A : it / ng_i;
-            const int gi = sh ? it - A * ng_i : it % ng_i;
+        const int np_i = (ng_i + 1) / 2, np_s = (ng_s + 1) / 2;
+        for (int it = warp; it < A * np_i + np_s; it += nw) {
+            const bool sh = it >= A * np_i;
+            const int v = sh ? A : it / np_i;
+            const int gp = sh ? it - A * np_i : it % np_i;
             const int lpr = sh ? p.lpr_is : p.lpr_i;
+            const int ng = sh ? ng_s : ng_i;
             const int rpw = 32 / lpr, sub = lane / lpr, pr = lane % lpr;
             const int type = sh ? L.shared_down_type : L.down_type;
             const int64_t rb = sh ? rb_sd : rb_down;
@@ -366,13 +399,19 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             const int n = sh ? Is : I;
             XLane xa;
             load_xlane(xa, qvec_at(sm + p.o_aq + v * qb, n), pr >> 2, pr & 3);
-            const int rr = gi * rpw + sub;
-            const bool ok = rr < nh;
-            const uint8_t* rowp = rows + (ok ? rr : 0) * rb;
-            float d = sh ? qdot_t<SDN>(type, rowp, pr >> 2, pr & 3, xa)
-                         : qdot_t<DN>(type, rowp, pr >> 2, pr & 3, xa);
-            d = group_sum(d, lpr);
-            if (ok && pr == 0) s_vout[v * p.max_out_rows + rr] = d;
+#pragma unroll
+            for (int gg = 0; gg < 2; ++gg) {
+                const int gi = 2 * gp + gg;
+                if (gi < ng) {
+                    const int rr = gi * rpw + sub;
+                    const bool ok = rr < nh;
+                    const uint8_t* rowp = rows + (ok ? rr : 0) * rb;
+                    float d = sh ? qdot_t<SDN>(type, rowp, pr >> 2, pr & 3, xa)
+                                 : qdot_t<DN>(type, rowp, pr >> 2, pr & 3, xa);
+                    d = group_sum(d, lpr);
+                    if (ok && pr == 0) s_vout[v * p.max_out_rows + rr] = d;
+                }
+            }
             if (it == 0) TRACE(21);
             if (it == nw) TRACE(22);
         }
@@ -549,6 +588,8 @@ cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float*
     off += align_up((size_t)Imax * 4);
     p.sg = reinterpret_cast<float*>(base + off);
     p.trace = (tl_trace && tl_trace_cap >= G) ? tl_trace : nullptr;
+    static const bool no_warm = getenv("MOE_B200_NO_WARM") != nullptr;
+    p.warm = no_warm ? 0 : 1;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);

@@ -129,132 +129,207 @@ __device__ __forceinline__ void load_xlane(XLane& x, const QVec& v, int b, int o
     x.s = v.s[b];
 }
 
-__device__ __forceinline__ uint32_t ld32(const uint8_t* p) {
-    return *reinterpret_cast<const uint32_t*>(p);
-}
-
-// 32-bit load from a 2-byte aligned shared address.
-__device__ __forceinline__ uint32_t ld32a2(const uint8_t* p) {
-    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
-    return (uint32_t)q[0] | ((uint32_t)q[1] << 16);
-}
-
 __device__ __forceinline__ int dp4(uint32_t a, uint32_t b, int c) {
     return __dp4a((int)a, (int)b, c);
 }
 
 // ---- per-format partial dot of one lane's 64 values (block pointer bp) ----
+//
+// Shared-memory loads are the scarce resource here (one warp-wide load issue
+// per SM cycle), so every decoder reads its bytes with the widest aligned
+// loads the block layout allows and extracts fields in registers.  Blocks of
+// 110 (Q3_K) and 210 (Q6_K) bytes are only 2-byte aligned: their words are
+// read as aligned words and funnel-shifted by 0 or 16 bits.
 
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) {
+    return *reinterpret_cast<const uint32_t*>(p);
+}
+
+// Two consecutive 32-bit words starting at a 2-byte aligned address:
+// al = address rounded down to 4, sh = 8 * (address & 3) in {0, 16}.
+__device__ __forceinline__ uint2 lds64_a2(const uint8_t* al, int sh) {
+    const uint32_t w0 = lds32(al), w1 = lds32(al + 4), w2 = lds32(al + 8);
+    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+    return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu)));
+}
+
+
+// Zero-extended byte i of w (one PRMT).
+__device__ __forceinline__ int ubyte(uint32_t w, int i) { return (int)__byte_perm(w, 0u, 0x4440u | (uint32_t)i); }
+// Sign-extended byte i of w: one PRMT whose selector nibbles 1..3 have
+// their msb set, which replicates the sign bit of byte i (PTX prmt, generic
+// mode).
+__device__ __forceinline__ int sbyte(uint32_t w, int i) {
+    const uint32_t sel = (uint32_t)i | ((uint32_t)(8 | i) << 4) | ((uint32_t)(8 | i) << 8) |
+                         ((uint32_t)(8 | i) << 12);
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+    return (int)r;
+}
+
+// Q3_K: u = q + 4 in 0..7; 13 shared loads per lane.  The -4 * sum(x)
+// correction rides in the dp4a accumulator's start value.
 __device__ __forceinline__ float qdot_q3k(const uint8_t* bp, int o, const XLane& x) {
-    const uint32_t hm0 = ld32a2(bp + 8 * o), hm1 = ld32a2(bp + 8 * o + 4);
-    const uint32_t qa0 = ld32a2(bp + 32 + 8 * o), qa1 = ld32a2(bp + 36 + 8 * o);
-    const uint32_t qb0 = ld32a2(bp + 64 + 8 * o), qb1 = ld32a2(bp + 68 + 8 * o);
-    const uint8_t* s = bp + 96;
+    const uint8_t* al = reinterpret_cast<const uint8_t*>((uintptr_t)bp & ~(uintptr_t)3);
+    const int sh = 8 * (int)((uintptr_t)bp & 3);
+    const uint2 hm = lds64_a2(al + 8 * o, sh);
+    const uint2 qa = lds64_a2(al + 32 + 8 * o, sh);
+    const uint2 qb = lds64_a2(al + 64 + 8 * o, sh);
+    const uint32_t w0 = lds32(al + 96), w1 = lds32(al + 100), w2 = lds32(al + 104), w3 = lds32(al + 108);
+    const uint32_t s03 = __funnelshift_r(w0, w1, sh), s47 = __funnelshift_r(w1, w2, sh);
+    const uint32_t s811 = __funnelshift_r(w2, w3, sh);
+    const float d = h2f(w3 >> sh);
+    // six-bit scales j = 2G + jo (reference dequant_q3_k, cpp/dequant_k.cpp:284-289),
+    // as signed bytes (scale - 32)
     const int jo = o >> 1;
-    int ah = 0, al = 0;
+    const uint32_t bq = __byte_perm(s03, s47, jo | ((2 + jo) << 4) | ((4 + jo) << 8) | ((6 + jo) << 12));
+    const uint32_t t = __byte_perm(s811, 0u, jo | ((2 + jo) << 4) | (jo << 8) | ((2 + jo) << 12));
+    const uint32_t hiA = (t & 0x00000303u) | ((t >> 2) & 0x03030000u);
+    const uint32_t hiB = ((t >> 4) & 0x00000303u) | ((t >> 6) & 0x03030000u);
+    uint32_t scA = ((bq & 0x0F0F0F0Fu) | (hiA << 4)) ^ 0x20202020u;          // 6-bit two's complement
+    uint32_t scB = (((bq >> 4) & 0x0F0F0F0Fu) | (hiB << 4)) ^ 0x20202020u;
+    scA |= (scA & 0x20202020u) * 6u;                                          // sign-extend to 8 bits
+    scB |= (scB & 0x20202020u) * 6u;
+    int ah = 0, alo = 0;
 #pragma unroll
     for (int G = 0; G < 8; ++G) {
-        const uint32_t q0 = G < 4 ? qa0 : qb0, q1 = G < 4 ? qa1 : qb1;
-        const int sh = 2 * (G & 3);
-        const uint32_t u0 = ((q0 >> sh) & 0x03030303u) | (((hm0 >> G) & 0x01010101u) << 2);
-        const uint32_t u1 = ((q1 >> sh) & 0x03030303u) | (((hm1 >> G) & 0x01010101u) << 2);
+        const uint32_t q0 = G < 4 ? qa.x : qb.x, q1 = G < 4 ? qa.y : qb.y;
+        const int s2 = 2 * (G & 3);
+        // hmask bit G of each byte moved to bit 2 (one shift, one mask)
+        const uint32_t hb0 = (G >= 2 ? hm.x >> (G - 2) : hm.x << (2 - G)) & 0x04040404u;
+        const uint32_t hb1 = (G >= 2 ? hm.y >> (G - 2) : hm.y << (2 - G)) & 0x04040404u;
+        const uint32_t u0 = ((q0 >> s2) & 0x03030303u) | hb0;
+        const uint32_t u1 = ((q1 >> s2) & 0x03030303u) | hb1;
         const uint2 xh = x.h2(G), xl = x.l2(G);
-        const int h = dp4(u1, xh.y, dp4(u0, xh.x, 0));
-        const int l = dp4(u1, xl.y, dp4(u0, xl.x, 0));
-        const int sc = q3_scale(s, 2 * G + jo);
-        ah += sc * (h - 4 * x.sh(G));
-        al += sc * (l - 4 * x.sl(G));
+        const int h = dp4(u1, xh.y, dp4(u0, xh.x, -4 * x.sh(G)));
+        const int l = dp4(u1, xl.y, dp4(u0, xl.x, -4 * x.sl(G)));
+        const int sc = sbyte(G < 4 ? scA : scB, G & 3);
+        ah += sc * h;
+        alo += sc * l;
     }
-    return ld_f16(bp + 108) * x.s * fmaf(256.f, (float)ah, (float)al);
+    return d * x.s * fmaf(256.f, (float)ah, (float)alo);
 }
 
+// (scale, min) bytes of Q4_K/Q5_K sub-blocks 0..3 and 4..7 from the 12
+// packed bytes (reference unpack_scale_min_k4, cpp/dequant_k.cpp:166-175):
+// y = bytes 0..3, z = bytes 4..7, w = bytes 8..11.
+__device__ __forceinline__ void k4_scales_words(uint32_t y, uint32_t z, uint32_t w, uint32_t& sc03,
+                                                uint32_t& mn03, uint32_t& sc47, uint32_t& mn47) {
+    sc03 = y & 0x3F3F3F3Fu;
+    mn03 = z & 0x3F3F3F3Fu;
+    sc47 = (w & 0x0F0F0F0Fu) | ((y >> 2) & 0x30303030u);
+    mn47 = ((w >> 4) & 0x0F0F0F0Fu) | ((z >> 2) & 0x30303030u);
+}
+
+// Q4_K: 16-byte aligned blocks; 5 shared loads per lane.
 __device__ __forceinline__ float qdot_q4k(const uint8_t* bp, int o, const XLane& x) {
-    int ah = 0, al = 0, mh = 0, ml = 0;
+    const uint4 hd = *reinterpret_cast<const uint4*>(bp);
+    uint32_t sc03, mn03, sc47, mn47;
+    k4_scales_words(hd.y, hd.z, hd.w, sc03, mn03, sc47, mn47);
+    int ah = 0, alo = 0, mh = 0, ml = 0;
 #pragma unroll
     for (int pp = 0; pp < 4; ++pp) {
-        const uint32_t w0 = ld32(bp + 16 + 32 * pp + 8 * o), w1 = ld32(bp + 20 + 32 * pp + 8 * o);
+        const uint2 w = *reinterpret_cast<const uint2*>(bp + 16 + 32 * pp + 8 * o);
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
             const int G = 2 * pp + hf;
-            const uint32_t u0 = (w0 >> (4 * hf)) & 0x0F0F0F0Fu, u1 = (w1 >> (4 * hf)) & 0x0F0F0F0Fu;
+            const uint32_t u0 = (w.x >> (4 * hf)) & 0x0F0F0F0Fu, u1 = (w.y >> (4 * hf)) & 0x0F0F0F0Fu;
             const uint2 xh = x.h2(G), xl = x.l2(G);
             const int h = dp4(u1, xh.y, dp4(u0, xh.x, 0));
             const int l = dp4(u1, xl.y, dp4(u0, xl.x, 0));
-            int sc, mn;
-            k4_scale_min(bp + 4, G, sc, mn);
+            const int sc = ubyte(G < 4 ? sc03 : sc47, G & 3);
+            const int mn = ubyte(G < 4 ? mn03 : mn47, G & 3);
             ah += sc * h;
-            al += sc * l;
+            alo += sc * l;
             mh += mn * x.sh(G);
             ml += mn * x.sl(G);
         }
     }
-    const float a = fmaf(256.f, (float)ah, (float)al);
+    const float a = fmaf(256.f, (float)ah, (float)alo);
     const float m = fmaf(256.f, (float)mh, (float)ml);
-    return x.s * (ld_f16(bp) * a - ld_f16(bp + 2) * m);
+    return x.s * (h2f(hd.x) * a - h2f(hd.x >> 16) * m);
 }
 
+// Q5_K: 16-byte aligned blocks; 6 shared loads per lane.
 __device__ __forceinline__ float qdot_q5k(const uint8_t* bp, int o, const XLane& x) {
-    const uint32_t qh0 = ld32(bp + 16 + 8 * o), qh1 = ld32(bp + 20 + 8 * o);
-    int ah = 0, al = 0, mh = 0, ml = 0;
+    const uint4 hd = *reinterpret_cast<const uint4*>(bp);
+    uint32_t sc03, mn03, sc47, mn47;
+    k4_scales_words(hd.y, hd.z, hd.w, sc03, mn03, sc47, mn47);
+    const uint2 qh = *reinterpret_cast<const uint2*>(bp + 16 + 8 * o);
+    int ah = 0, alo = 0, mh = 0, ml = 0;
 #pragma unroll
     for (int pp = 0; pp < 4; ++pp) {
-        const uint32_t w0 = ld32(bp + 48 + 32 * pp + 8 * o), w1 = ld32(bp + 52 + 32 * pp + 8 * o);
+        const uint2 w = *reinterpret_cast<const uint2*>(bp + 48 + 32 * pp + 8 * o);
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
             const int G = 2 * pp + hf;
-            const uint32_t u0 = ((w0 >> (4 * hf)) & 0x0F0F0F0Fu) | (((qh0 >> G) & 0x01010101u) << 4);
-            const uint32_t u1 = ((w1 >> (4 * hf)) & 0x0F0F0F0Fu) | (((qh1 >> G) & 0x01010101u) << 4);
+            const uint32_t u0 = ((w.x >> (4 * hf)) & 0x0F0F0F0Fu) | (((qh.x >> G) & 0x01010101u) << 4);
+            const uint32_t u1 = ((w.y >> (4 * hf)) & 0x0F0F0F0Fu) | (((qh.y >> G) & 0x01010101u) << 4);
             const uint2 xh = x.h2(G), xl = x.l2(G);
             const int h = dp4(u1, xh.y, dp4(u0, xh.x, 0));
             const int l = dp4(u1, xl.y, dp4(u0, xl.x, 0));
-            int sc, mn;
-            k4_scale_min(bp + 4, G, sc, mn);
+            const int sc = ubyte(G < 4 ? sc03 : sc47, G & 3);
+            const int mn = ubyte(G < 4 ? mn03 : mn47, G & 3);
             ah += sc * h;
-            al += sc * l;
+            alo += sc * l;
             mh += mn * x.sh(G);
             ml += mn * x.sl(G);
         }
     }
-    const float a = fmaf(256.f, (float)ah, (float)al);
+    const float a = fmaf(256.f, (float)ah, (float)alo);
     const float m = fmaf(256.f, (float)mh, (float)ml);
-    return x.s * (ld_f16(bp) * a - ld_f16(bp + 2) * m);
+    return x.s * (h2f(hd.x) * a - h2f(hd.x >> 16) * m);
 }
 
+// Q6_K: 2-byte aligned blocks; 24 shared loads per lane.
 __device__ __forceinline__ float qdot_q6k(const uint8_t* bp, int o, const XLane& x) {
-    const uint32_t ha0 = ld32a2(bp + 128 + 8 * o), ha1 = ld32a2(bp + 132 + 8 * o);
-    const uint32_t hb0 = ld32a2(bp + 160 + 8 * o), hb1 = ld32a2(bp + 164 + 8 * o);
-    const int8_t* sc = reinterpret_cast<const int8_t*>(bp + 192);
+    const uint8_t* al = reinterpret_cast<const uint8_t*>((uintptr_t)bp & ~(uintptr_t)3);
+    const int sh = 8 * (int)((uintptr_t)bp & 3);
+    const uint2 ha = lds64_a2(al + 128 + 8 * o, sh), hb = lds64_a2(al + 160 + 8 * o, sh);
+    const uint32_t v0 = lds32(al + 192), v1 = lds32(al + 196), v2 = lds32(al + 200),
+                   v3 = lds32(al + 204), v4 = lds32(al + 208);
+    const uint32_t sw[4] = {__funnelshift_r(v0, v1, sh), __funnelshift_r(v1, v2, sh),
+                            __funnelshift_r(v2, v3, sh), __funnelshift_r(v3, v4, sh)};
+    const float d = h2f(__funnelshift_r(v4, v4, sh));
     const int jo = o >> 1;
-    int ah = 0, al = 0;
+    int ah = 0, alo = 0;
 #pragma unroll
     for (int G = 0; G < 8; ++G) {
-        const uint8_t* lp = bp + 64 * (G >> 2) + 32 * (G & 1) + 8 * o;
-        const uint32_t w0 = ld32a2(lp), w1 = ld32a2(lp + 4);
+        const uint2 w = lds64_a2(al + 64 * (G >> 2) + 32 * (G & 1) + 8 * o, sh);
         const int ns = 4 * ((G >> 1) & 1), hs = 2 * (G & 3);
-        const uint32_t h0 = G < 4 ? ha0 : hb0, h1 = G < 4 ? ha1 : hb1;
-        const uint32_t u0 = ((w0 >> ns) & 0x0F0F0F0Fu) | (((h0 >> hs) & 0x03030303u) << 4);
-        const uint32_t u1 = ((w1 >> ns) & 0x0F0F0F0Fu) | (((h1 >> hs) & 0x03030303u) << 4);
+        const uint32_t h0 = G < 4 ? ha.x : hb.x, h1 = G < 4 ? ha.y : hb.y;
+        const uint32_t u0 = ((w.x >> ns) & 0x0F0F0F0Fu) | (((h0 >> hs) & 0x03030303u) << 4);
+        const uint32_t u1 = ((w.y >> ns) & 0x0F0F0F0Fu) | (((h1 >> hs) & 0x03030303u) << 4);
         const uint2 xh = x.h2(G), xl = x.l2(G);
-        const int h = dp4(u1, xh.y, dp4(u0, xh.x, 0));
-        const int l = dp4(u1, xl.y, dp4(u0, xl.x, 0));
-        const int s8 = sc[2 * G + jo];
-        ah += s8 * (h - 32 * x.sh(G));
-        al += s8 * (l - 32 * x.sl(G));
+        const int h = dp4(u1, xh.y, dp4(u0, xh.x, -32 * x.sh(G)));
+        const int l = dp4(u1, xl.y, dp4(u0, xl.x, -32 * x.sl(G)));
+        const int si = 2 * G + jo;  // int8 scale byte si of bytes 192..207
+        const int s8 = sbyte(sw[si >> 2], si & 3);
+        ah += s8 * h;
+        alo += s8 * l;
     }
-    return ld_f16(bp + 208) * x.s * fmaf(256.f, (float)ah, (float)al);
+    return d * x.s * fmaf(256.f, (float)ah, (float)alo);
 }
 
-// Q8_0: bp points at 8 consecutive 34-byte blocks (256 values).
+// Q8_0: bp points at 8 consecutive 34-byte blocks (256 values, 16-byte
+// aligned); block G starts at 34*G (2-byte aligned).
 __device__ __forceinline__ float qdot_q8_0(const uint8_t* bp, int o, const XLane& x) {
     float acc = 0.f;
 #pragma unroll
     for (int G = 0; G < 8; ++G) {
         const uint8_t* qb = bp + 34 * G;
-        const uint32_t q0 = ld32a2(qb + 2 + 8 * o), q1 = ld32a2(qb + 6 + 8 * o);
+        // bytes qb[0..1] = d, qb[2 + 8o .. 10 + 8o) = quants
+        const uint8_t* al = reinterpret_cast<const uint8_t*>((uintptr_t)(qb + 2 + 8 * o) & ~(uintptr_t)3);
+        const int sh = 8 * (int)((uintptr_t)(qb + 2 + 8 * o) & 3);
+        const uint2 q = lds64_a2(al, sh);
+        const float dg = h2f(*reinterpret_cast<const uint16_t*>(qb));
         const uint2 xh = x.h2(G), xl = x.l2(G);
-        const int h = dp4(q1, xh.y, dp4(q0, xh.x, 0));
-        const int l = dp4(q1, xl.y, dp4(q0, xl.x, 0));
-        acc = fmaf(ld_f16(qb), fmaf(256.f, (float)h, (float)l), acc);
+        const int h = dp4(q.y, xh.y, dp4(q.x, xh.x, 0));
+        const int l = dp4(q.y, xl.y, dp4(q.x, xl.x, 0));
+        acc = fmaf(dg, fmaf(256.f, (float)h, (float)l), acc);
     }
     return x.s * acc;
 }

@@ -51,6 +51,7 @@ def _bind(lib: C.CDLL) -> None:
         "dequant_k": (i, [i, vp, vp, i64, i]),
         "moe_quant_expert": (i, [i, vp, i64] * 3 + [vp, i, i, vp, i]),
         "moe_b200_decode_workspace": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_size_t)]),
+        "moe_b200_decode_kernels": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_int)]),
         "moe_b200_decode": (i, [C.POINTER(Layer), vp, C.c_int32, vp, vp, vp, vp, C.c_size_t, vp]),
         "moe_b200_dequant": (i, [i, vp, vp, i64, i, vp]),
         "moe_b200_last_cuda_error": (i, []),

@@ -81,6 +81,15 @@ class B200ExpertBackend:
             cache[self.device] = ws
         return ws
 
+    def kernels_per_call(self, layer: int, tokens: int, flags: int | None = None) -> int:
+        """Kernels one forward_layer_device call launches (from the library)."""
+        dl = self.store.layer(layer)
+        s = dl.with_flags(self.flags if flags is None else flags)
+        n = C.c_int(0)
+        _lib.check(self.lib.moe_b200_decode_kernels(C.byref(s), tokens, C.byref(n)),
+                   "moe_b200_decode_kernels")
+        return n.value
+
     def device_errors(self) -> int:
         """Read and clear the device error word of this thread's workspace
         (-9 when a bounded wait inside a decode kernel gave up)."""

@@ -44,7 +44,6 @@ class DecodeRunner:
     Step i decodes token ``i % len(tokens)`` of this rank through layer
     ``layers[i % len(layers)]``."""
 
-    kernel_name = "moe_b200_decode"
 
     def __init__(self, backend, layers, tokens: torch.Tensor, world: int = 1, rank: int = 0,
                  max_steps: int = 4096):
@@ -64,7 +63,14 @@ class DecodeRunner:
             self.y_part = torch.empty((world, H), dtype=torch.float32, device=self.dev)
             self.y_routed = torch.empty((1, H), dtype=torch.float32, device=self.dev)
             self.y_sh = torch.empty((1, H), dtype=torch.float32, device=self.dev)
-        self.launches_per_step = 4 if world == 1 else 7
+        if world == 1:
+            self.launches_per_step = backend.kernels_per_call(self.layers[0], 1)
+        else:
+            self.launches_per_step = (
+                backend.kernels_per_call(self.layers[0], world, backend.flags | _lib.NO_SHARED)
+                + backend.kernels_per_call(self.layers[0], 1, backend.flags | _lib.SHARED_ONLY))
+        self.kernel_name = ("k_decode_fused (1 launch per step)" if self.launches_per_step == 1
+                            else f"moe_b200_decode ({self.launches_per_step} kernels per step)")
         self.recorded = 0
         self._graph = None
 
