@@ -157,6 +157,33 @@ MOE_B200_API int moe_b200_workspace_error(void* workspace, void* stream, int* er
 MOE_B200_API int moe_b200_decode_kernels(const moe_b200_layer* layer, int32_t tokens,
                                          int* kernels);
 
+/* Largest `intermediate` moe_b200_expert_noalloc accepts. */
+#define MOE_B200_NOALLOC_MAX_INTERMEDIATE 16384
+
+/* moe_quant_expert for callers that cannot allocate device memory -- a
+ * serving process that reserved all of it up front for its own pool, or a
+ * thread that must not enter the CUDA allocator while other work runs
+ * (freeing, and allocating when memory has to be returned first,
+ * synchronise the device).  No counterpart in the reference.
+ *
+ * Same arguments, arithmetic and argument checks as moe_quant_expert, but
+ * every pointer must be device memory (input and output 16-byte aligned),
+ * the call is asynchronous on `stream` (a cudaStream_t), and it allocates
+ * nothing: its scratch (the intermediate activations) is a fixed array
+ * inside the library, 2 x MOE_B200_NOALLOC_MAX_INTERMEDIATE floats that
+ * every GPU loading the library holds until the process exits.  Returns -1
+ * also when intermediate exceeds MOE_B200_NOALLOC_MAX_INTERMEDIATE.  A
+ * non-finite output is not reported (use moe_quant_expert for status -4).
+ * The first call on a device looks up the array's device address (once per
+ * device); make that first call before any stream capture.  All calls on a
+ * device share the array: calls whose kernels overlap on the GPU race, so
+ * order them on one stream. */
+MOE_B200_API int moe_b200_expert_noalloc(int gate_type, const uint8_t* gate, int64_t gate_bytes,
+                                         int up_type, const uint8_t* up, int64_t up_bytes,
+                                         int down_type, const uint8_t* down, int64_t down_bytes,
+                                         const float* input, int hidden, int intermediate,
+                                         float* output, int fp16_graph, void* stream);
+
 /* Device-pointer dequantisation on a stream: out_dtype 0 = fp32,
  * 1 = binary16 (round to nearest even).  Same values as dequant_k. */
 MOE_B200_API int moe_b200_dequant(int type, const void* src, void* dst, int64_t n, int out_dtype,

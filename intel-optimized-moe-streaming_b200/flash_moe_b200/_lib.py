@@ -54,6 +54,7 @@ def _bind(lib: C.CDLL) -> None:
         "moe_b200_decode_kernels": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_int)]),
         "moe_b200_decode": (i, [C.POINTER(Layer), vp, C.c_int32, vp, vp, vp, vp, C.c_size_t, vp]),
         "moe_b200_dequant": (i, [i, vp, vp, i64, i, vp]),
+        "moe_b200_expert_noalloc": (i, [i, vp, i64] * 3 + [vp, i, i, vp, i, vp]),
         "moe_b200_last_cuda_error": (i, []),
         "moe_b200_workspace_init": (i, [vp, C.c_size_t, vp]),
         "moe_b200_set_trace": (i, [vp, i]),
