@@ -149,13 +149,56 @@ MOE_B200_API int moe_b200_decode(const moe_b200_layer* layer, const float* x, in
 MOE_B200_API int moe_b200_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
 
 /* Synchronously read (and clear) the device-side error word of a
- * workspace: 0, or -9 when a bounded wait of a decode launch gave up. */
+ * workspace: 0; -9 when a bounded wait of a decode or prefill launch gave
+ * up; -10 when a prefill SwiGLU activation fell outside the fp16 range
+ * (that call's output is not valid; moe_b200_decode computes the same
+ * tokens in fp32). */
 MOE_B200_API int moe_b200_workspace_error(void* workspace, void* stream, int* error);
 
 /* Number of kernels one moe_b200_decode call with this layer, token count
  * and the layer's flags launches (1 for the fused single-token path). */
 MOE_B200_API int moe_b200_decode_kernels(const moe_b200_layer* layer, int32_t tokens,
                                          int* kernels);
+
+/* Many-token layer forward on the tcgen05 tensor cores: the prefill form of
+ * run_moe_sequence (reference src/flash_moe/moe_layer.py:110-195, whose
+ * per-expert batches go through ExpertBackend.forward_batch,
+ * src/flash_moe/backend_ov.py:357-431, and SharedExpert.forward_batch,
+ * src/flash_moe/shared_expert.py:395-414).  No single reference function
+ * has this signature: it is the device-resident prefill export the B200
+ * library adds beside the per-expert ones.
+ *
+ * x: device [tokens x hidden], fp32 (x_dtype 0) or bf16 (x_dtype 1).
+ * y: device fp32 [tokens x hidden], written in full.  topk_ids /
+ * topk_weights: device [tokens x top_k] or NULL.  The expert weights are
+ * dequantised to fp16 (the value of dequant_k with want_f16 = 1) and the
+ * products accumulate in fp32; the result matches the fp32 reference
+ * within 1e-3 relative (max |y - ref| / max |ref|).  Flags: NO_SHARED and
+ * SHARED_ONLY as for moe_b200_decode; EXACT and FP16_GRAPH are not
+ * available here (-2).  Returns -2 when a shape or block format is outside
+ * this path (moe_b200_prefill_supported), -8 for a short workspace.
+ * Asynchronous on `stream`; calls sharing a workspace must be ordered on
+ * one stream. */
+MOE_B200_API int moe_b200_prefill(const moe_b200_layer* layer, const void* x, int32_t x_dtype,
+                                  int32_t tokens, float* y, int32_t* topk_ids,
+                                  float* topk_weights, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
+/* Workspace bytes of moe_b200_prefill for up to max_tokens tokens (device
+ * memory, 256-byte aligned; its first 256 bytes are the control words
+ * that moe_b200_workspace_init clears). */
+MOE_B200_API int moe_b200_prefill_workspace(const moe_b200_layer* layer, int32_t max_tokens,
+                                            size_t* bytes);
+
+/* 1 when moe_b200_prefill handles this layer and its flags: hidden,
+ * intermediate and shared_intermediate multiples of 256; Q8_0, Q3_K,
+ * Q4_K, Q5_K or Q6_K weights whose rows are multiples of 16 bytes; gate
+ * and up of one format; at most 1024 held experts. */
+MOE_B200_API int moe_b200_prefill_supported(const moe_b200_layer* layer);
+
+/* Number of kernels one moe_b200_prefill call launches (7, or 3 with
+ * MOE_B200_SHARED_ONLY). */
+MOE_B200_API int moe_b200_prefill_kernels(const moe_b200_layer* layer, int* kernels);
 
 /* Largest `intermediate` moe_b200_expert_noalloc accepts. */
 #define MOE_B200_NOALLOC_MAX_INTERMEDIATE 16384

@@ -87,16 +87,6 @@ static bool on_device(const void* p) {
     return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
-// Lays out host->device staging regions inside one scratch buffer.
-struct Stager {
-    size_t used = 0;
-    size_t take(size_t bytes) {
-        const size_t at = used;
-        used += align256(bytes);
-        return at;
-    }
-};
-
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 static int check_qmat(int type, const void* base, int rows, int cols) {
@@ -429,6 +419,46 @@ int moe_b200_decode(const moe_b200_layer* L, const float* x, int32_t T, float* y
         e = cudaMemcpyAsync(topk_weights, r.w, (size_t)T * L->top_k * 4, cudaMemcpyDeviceToDevice, s);
         if (e != cudaSuccess) return fail(e, ST_CUDA);
     }
+    return ST_OK;
+}
+
+int moe_b200_prefill_supported(const moe_b200_layer* L) {
+    if (check_layer(L) != ST_OK) return 0;
+    return prefill_supported(L, L->flags) ? 1 : 0;
+}
+
+int moe_b200_prefill_workspace(const moe_b200_layer* L, int32_t max_tokens, size_t* bytes) {
+    const int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (max_tokens < 1 || !bytes) return ST_ARG;
+    *bytes = prefill_workspace_bytes(L, max_tokens);
+    return ST_OK;
+}
+
+int moe_b200_prefill(const moe_b200_layer* L, const void* x, int32_t x_dtype, int32_t T,
+                     float* y, int32_t* topk_ids, float* topk_weights, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+    int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (T < 1 || !x || !y || !workspace || (x_dtype != 0 && x_dtype != 1)) return ST_ARG;
+    if (!aligned16(x) || !aligned16(y) || ((uintptr_t)workspace & 255u)) return ST_ALIGN;
+    const bool shared_only = (L->flags & MOE_B200_SHARED_ONLY) != 0;
+    const bool with_shared = L->shared_intermediate > 0 && !(L->flags & MOE_B200_NO_SHARED);
+    if (shared_only && !with_shared) return ST_ARG;
+    if (!prefill_supported(L, L->flags)) return ST_TYPE;
+    if (workspace_bytes < prefill_workspace_bytes(L, T)) return ST_WORKSPACE;
+    cudaError_t ce = cudaSuccess;
+    st = prefill_run(L, x, x_dtype, T, y, topk_ids, topk_weights, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream), &ce);
+    if (st == ST_CUDA) return fail(ce, ST_CUDA);
+    return st;
+}
+
+int moe_b200_prefill_kernels(const moe_b200_layer* L, int* kernels) {
+    const int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (!kernels) return ST_ARG;
+    *kernels = prefill_kernels(L);
     return ST_OK;
 }
 

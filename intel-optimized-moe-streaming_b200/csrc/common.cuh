@@ -25,6 +25,7 @@ enum : int {
     ST_ALIGN = -7,      // a device pointer is not 16-byte aligned
     ST_WORKSPACE = -8,  // workspace too small
     ST_TIMEOUT = -9,    // a bounded device-side wait gave up
+    ST_RANGE = -10,     // a prefill activation outside the fp16 range
 };
 
 __host__ __device__ constexpr int block_size(int t) {
@@ -58,6 +59,12 @@ struct QMat {
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
 

@@ -529,6 +529,11 @@ void set_fused_trace(void* buf, int capacity_ctas) {
     tl_trace_cap = capacity_ctas;
 }
 
+uint64_t* trace_buffer(int* capacity_ctas) {
+    *capacity_ctas = tl_trace_cap;
+    return tl_trace;
+}
+
 cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float* x, float* y,
                                 int32_t* ids_out, float* w_out, void* ws, cudaStream_t stream,
                                 bool* launched) {

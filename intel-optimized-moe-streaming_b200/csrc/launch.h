@@ -8,6 +8,16 @@ namespace moeb200 {
 
 int sm_count();  // multiprocessors of the current device (cached per device)
 
+// Lays out regions (256-byte aligned) inside one buffer.
+struct Stager {
+    size_t used = 0;
+    size_t take(size_t bytes) {
+        const size_t at = used;
+        used += align_up(bytes);
+        return at;
+    }
+};
+
 cudaError_t launch_dequant(int type, const void* src, void* dst, int64_t n, bool f16,
                            cudaStream_t stream);
 
@@ -54,5 +64,15 @@ cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float*
                                 int32_t* ids_out, float* w_out, void* ws, cudaStream_t stream,
                                 bool* launched);
 void set_fused_trace(void* buf, int capacity_ctas);
+uint64_t* trace_buffer(int* capacity_ctas);  // the buffer set above (this thread)
+
+// Many-token layer on the tcgen05 tensor cores (prefill.cu).  x is fp32 or
+// (x_bf16) bf16 [T x H]; y is written in full.
+bool prefill_supported(const moe_b200_layer* L, int flags);
+size_t prefill_workspace_bytes(const moe_b200_layer* L, int T);
+int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float* y,
+                int32_t* ids_out, float* w_out, void* ws, size_t ws_bytes, cudaStream_t s,
+                cudaError_t* ce);
+int prefill_kernels(const moe_b200_layer* L);
 
 }  // namespace moeb200

@@ -54,12 +54,6 @@ __device__ __forceinline__ QVec qvec_at(uint8_t* base, int n) {
     return q;
 }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-
 // Quantise 256-value block b of an fp32 vector in shared memory with one
 // warp: lane l takes values 8l..8l+7 (octet l).  No block-wide barrier; the
 // caller synchronises before the codes are read.

@@ -20,6 +20,7 @@ STATUS = {
     -3: "byte count does not match shape", -4: "non-finite output",
     -5: "host-side failure", -6: "CUDA call failed", -7: "device pointer not 16-byte aligned",
     -8: "workspace too small", -9: "device wait timed out",
+    -10: "prefill activation outside the fp16 range",
 }
 
 FP16_GRAPH = 1
@@ -53,6 +54,11 @@ def _bind(lib: C.CDLL) -> None:
         "moe_b200_decode_workspace": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_size_t)]),
         "moe_b200_decode_kernels": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_int)]),
         "moe_b200_decode": (i, [C.POINTER(Layer), vp, C.c_int32, vp, vp, vp, vp, C.c_size_t, vp]),
+        "moe_b200_prefill": (i, [C.POINTER(Layer), vp, C.c_int32, C.c_int32, vp, vp, vp, vp,
+                                 C.c_size_t, vp]),
+        "moe_b200_prefill_workspace": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_size_t)]),
+        "moe_b200_prefill_supported": (i, [C.POINTER(Layer)]),
+        "moe_b200_prefill_kernels": (i, [C.POINTER(Layer), C.POINTER(C.c_int)]),
         "moe_b200_dequant": (i, [i, vp, vp, i64, i, vp]),
         "moe_b200_expert_noalloc": (i, [i, vp, i64] * 3 + [vp, i, i, vp, i, vp]),
         "moe_b200_last_cuda_error": (i, []),

@@ -35,7 +35,8 @@ class B200ExpertBackend:
     the fp32 arithmetic of ``fp16_graph=0``."""
 
     def __init__(self, arena: ExpertArena, expert_workers: int = 4,
-                 fp16_graph: bool = False, exact: bool = False):
+                 fp16_graph: bool = False, exact: bool = False,
+                 prefill_min_tokens: int = 32):
         if expert_workers < 1:
             raise ValueError("thread and worker counts must be positive")
         self.lib = _lib.load()
@@ -47,6 +48,9 @@ class B200ExpertBackend:
         self._moe_executor = ThreadPoolExecutor(max_workers=expert_workers)
         self._native_enabled = False
         self._tls = threading.local()
+        # forward_layer uses the tensor-core prefill kernels from this many
+        # tokens on (when the layer's shapes and formats allow it)
+        self.prefill_min_tokens = int(prefill_min_tokens)
 
     # ---------------------------------------------------------------- policy
 
@@ -80,6 +84,62 @@ class B200ExpertBackend:
             ws = torch.zeros(max(need.value, 256), dtype=torch.uint8, device=self.device)
             cache[self.device] = ws
         return ws
+
+    def _prefill_workspace(self, s, tokens: int) -> torch.Tensor:
+        cache = getattr(self._tls, "pf_ws", None)
+        if cache is None:
+            cache = self._tls.pf_ws = {}
+        need = C.c_size_t(0)
+        _lib.check(self.lib.moe_b200_prefill_workspace(C.byref(s), tokens, C.byref(need)),
+                   "moe_b200_prefill_workspace")
+        ws = cache.get(self.device)
+        if ws is None or ws.numel() < need.value:
+            ws = torch.zeros(max(need.value, 256), dtype=torch.uint8, device=self.device)
+            cache[self.device] = ws
+        return ws
+
+    def prefill_supported(self, layer: int, flags: int | None = None) -> bool:
+        """Whether the tensor-core prefill path takes this layer and flags."""
+        s = self.store.layer(layer).with_flags(self.flags if flags is None else flags)
+        return bool(self.lib.moe_b200_prefill_supported(C.byref(s)))
+
+    def prefill_device(self, layer: int, x: torch.Tensor, y: torch.Tensor,
+                       topk_ids: torch.Tensor | None = None,
+                       topk_weights: torch.Tensor | None = None,
+                       flags: int | None = None, stream=None) -> None:
+        """Asynchronous many-token layer on the tensor cores: x fp32 or bf16
+        [T, H], y fp32 [T, H] (``moe_b200_prefill``)."""
+        dl = self.store.layer(layer)
+        t = x.shape[0]
+        s = dl.with_flags(self.flags if flags is None else flags)
+        if x.dtype == torch.float32:
+            xdt = 0
+        elif x.dtype == torch.bfloat16:
+            xdt = 1
+        else:
+            raise TypeError("prefill input must be fp32 or bf16")
+        ws = self._prefill_workspace(s, t)
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        st = self.lib.moe_b200_prefill(
+            C.byref(s), x.data_ptr(), xdt, t, y.data_ptr(),
+            topk_ids.data_ptr() if topk_ids is not None else None,
+            topk_weights.data_ptr() if topk_weights is not None else None,
+            ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        _lib.check(st, "moe_b200_prefill")
+
+    def prefill_errors(self) -> int:
+        """Read and clear the device error word of this thread's prefill
+        workspace (-9 wait timeout, -10 activation outside fp16)."""
+        cache = getattr(self._tls, "pf_ws", None) or {}
+        ws = cache.get(self.device)
+        if ws is None:
+            return 0
+        err = C.c_int(0)
+        _lib.check(self.lib.moe_b200_workspace_error(
+            ws.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream, C.byref(err)),
+            "moe_b200_workspace_error")
+        return err.value
 
     def kernels_per_call(self, layer: int, tokens: int, flags: int | None = None) -> int:
         """Kernels one forward_layer_device call launches (from the library)."""
@@ -134,7 +194,15 @@ class B200ExpertBackend:
             k = self.store.layer(layer).weights.top_k
             ids = torch.empty((x.shape[0], k), dtype=torch.int32, device=self.device)
             w = torch.empty((x.shape[0], k), dtype=torch.float32, device=self.device)
-            self.forward_layer_device(layer, xd, yd, ids, w)
+            if x.shape[0] >= self.prefill_min_tokens and self.prefill_supported(layer):
+                self.prefill_device(layer, xd, yd, ids, w)
+                err = self.prefill_errors()
+                if err == -10:   # an activation outside fp16: fp32 engine instead
+                    self.forward_layer_device(layer, xd, yd, ids, w)
+                elif err:
+                    _lib.check(err, "moe_b200_prefill")
+            else:
+                self.forward_layer_device(layer, xd, yd, ids, w)
             y = yd.cpu().numpy()
             routing = (ids.cpu().numpy(), w.cpu().numpy())
         y = y[0] if squeeze else y
