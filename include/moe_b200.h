@@ -196,7 +196,7 @@ MOE_B200_API int moe_b200_prefill_workspace(const moe_b200_layer* layer, int32_t
  * and up of one format; at most 1024 held experts. */
 MOE_B200_API int moe_b200_prefill_supported(const moe_b200_layer* layer);
 
-/* Number of kernels one moe_b200_prefill call launches (7, or 3 with
+/* Number of kernels one moe_b200_prefill call launches (8, or 3 with
  * MOE_B200_SHARED_ONLY). */
 MOE_B200_API int moe_b200_prefill_kernels(const moe_b200_layer* layer, int* kernels);
 

@@ -25,6 +25,7 @@
 //   k_pf_gemm<ROUTER> logits = x . router^T (+ bias)
 //   k_pf_topk        per token: top-k + softmax (topk.cuh), pair counts
 //   k_pf_scatter     per expert: its (token, weight) pairs in token order
+//   k_pf_permute     x rows in pair order (contiguous B rows per expert)
 //   k_pf_gemm<GATEUP> act = silu(x Wg^T) * (x Wu^T) per pair, fp16
 //   k_pf_gemm<DOWN>  y[token] += w * (act Wd^T) per pair (fp32 reductions)
 //
@@ -90,8 +91,9 @@ struct PfSide {
 
 struct __align__(64) PfParams {
     CUtensorMap wmap[2][2];  // [routed, shared][gate or down, up]: raw weight bytes
-    CUtensorMap bmap;        // B rows: fp16 x hi (ROUTER, GATEUP) or act (DOWN)
-    CUtensorMap bmap2;       // ROUTER: fp16 x lo
+    CUtensorMap bmap[2][2];  // [routed, shared][box of 128 rows, of 16 rows]: B rows
+                             // (gate/up: x in pair order / x; down: act)
+    CUtensorMap rbmap[2];    // ROUTER B: fp16 x hi, lo (boxes of 16 rows)
     CUtensorMap rmap[2];     // ROUTER A: router rows hi, lo
     PfSide side[2];
     int n_routed;            // routed experts held (units on side 0)
@@ -415,7 +417,8 @@ __device__ __forceinline__ bool dq_unit(const PfParams& p, const PfUnit& un, uin
             src[4 * k + 2] = v.z;
             src[4 * k + 3] = v.w;
         }
-        mbar_arrive(&rempty[slot]);
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&rempty[slot]);
         ++it_r;
         // normalise: word i = bytes o + 4i .. o + 4i + 3 of the window
         const int o = (g * GB) & 15;
@@ -439,7 +442,8 @@ __device__ __forceinline__ bool dq_unit(const PfParams& p, const PfUnit& un, uin
             if (!pf_wait_t(&empty[st], ph ^ 1u, abort, p.err, t_empty)) return false;
             dq_store<T>(smem + (size_t)st * p.stage_bytes, trow, h, w, s_c);
             fence_async_smem();
-            mbar_arrive(&full[st]);
+            __syncwarp();
+            if ((threadIdx.x & 31) == 0) mbar_arrive(&full[st]);
             ++it_s;
             return true;
         };
@@ -507,18 +511,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     // --- set-up
     if (warp == kPfMmaWarp) tmem_alloc(s_tmem, 512);
     if (tid == 0) {
-        const uint32_t fcount = (MODE == PF_ROUTER) ? 1u : 1u + kPfDqThreads;
+        // stage full: the B producer (its expect_tx arrival) and one arrival
+        // per dequantisation warp
+        const uint32_t fcount = (MODE == PF_ROUTER) ? 1u : 1u + kPfDqThreads / 32;
         for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], fcount);
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < R; ++i) {
             mbar_init(&rfull[i], 1);
-            mbar_init(&rempty[i], kPfDqThreads);
+            mbar_init(&rempty[i], kPfDqThreads / 32);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], kPfEpiWarps * 32);
+            mbar_init(&acc_empty[i], kPfEpiWarps);
         }
         *s_abort = 0;
         mbar_fence_init();
@@ -593,23 +599,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                     ok = __shfl_sync(0xffffffffu, good, 0) != 0;
                     if (ok && 16 * lane < N16)
                         tma_load_2d(smem + (size_t)st * p.stage_bytes + p.a_bytes + 16 * lane * 128,
-                                    seg == 2 ? &p.bmap2 : &p.bmap, kk, un.tok0 + 16 * lane,
+                                    &p.rbmap[seg == 2], kk, un.tok0 + 16 * lane,
                                     &full[st]);
                     ++it_s;
                 }
                 continue;
             }
-            // B: token rows of x by tile::gather4 (gate/up) or act rows by
-            // 2-D boxes (down), kept in L2 (evict-last) across the row tiles
-            int tok[8];
-            if (MODE == PF_GATEUP) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int r = (j < 4 ? 0 : 128) + 4 * lane + (j & 3);
-                    const int rr = min(r, un.n - 1);
-                    tok[j] = un.side == 0 ? p.pair_tok[un.prow + rr] : un.tok0 + rr;
-                }
-            }
+            // B: the unit's pair rows are consecutive rows of x in pair order
+            // (gate/up, routed), of x (gate/up, shared) or of act (down):
+            // one 128-row box and 16-row boxes per stage, kept in L2
+            // (evict-last) across the row tiles of the expert
+            const CUtensorMap* b128 = &p.bmap[un.side][0];
+            const CUtensorMap* b16 = &p.bmap[un.side][1];
+            const int row0 = (MODE == PF_GATEUP && un.side == 1) ? un.tok0 : un.prow;
+            const int nb = N16 >> 7, n16 = (N16 & 127) >> 4;
             const uint64_t keep = l2_evict_last();
             const int nk = p.side[un.side].K / 64;
             for (int k = 0; k < nk && ok; ++k) {
@@ -623,16 +626,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 if (!ok) break;
                 uint8_t* b = smem + (size_t)st * p.stage_bytes + p.a_bytes;
                 const int k0 = 64 * k;
-                if (MODE == PF_GATEUP) {
-                    if (4 * lane < N16)
-                        tma_gather4_hint(b + 4 * lane * 128, &p.bmap, k0, tok[0], tok[1], tok[2],
-                                         tok[3], &full[st], keep);
-                    if (128 + 4 * lane < N16)
-                        tma_gather4_hint(b + (128 + 4 * lane) * 128, &p.bmap, k0, tok[4], tok[5],
-                                         tok[6], tok[7], &full[st], keep);
-                } else if (16 * lane < N16) {
-                    tma_load_2d_hint(b + 16 * lane * 128, &p.bmap, k0, un.prow + 16 * lane,
-                                     &full[st], keep);
+                if (lane < nb) {
+                    tma_load_2d_hint(b + lane * 128 * 128, b128, k0, row0 + 128 * lane, &full[st],
+                                     keep);
+                } else if (lane < nb + n16) {
+                    const int r = 128 * nb + 16 * (lane - nb);
+                    tma_load_2d_hint(b + r * 128, b16, k0, row0 + r, &full[st], keep);
                 }
                 ++it_s;
             }
@@ -799,15 +798,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                         if (col < un.n) {
                             const float xs = s_cw[col];
                             const float gg = __fmul_rn(g, xs), uu = __fmul_rn(uu0, xs);
-                            float a;
-                            if (un.side == 0) {
-                                const float sg = 1.0f / (1.0f + expf(-gg));
-                                a = (gg * sg) * uu;
-                            } else {
-                                a = (gg * shared_sigmoid(gg)) * uu;
-                            }
+                            // silu(g) * u with the fast exponential and divide:
+                            // their ~1e-6 relative error is far below the fp16
+                            // rounding of the stored activation
+                            const float a = __fdividef(gg * uu, 1.0f + __expf(-gg));
                             ah = __float2half_rn(a);
-                            if (__hisinf(ah) && isfinite(a)) atomicCAS(p.err, 0u, (uint32_t)ST_RANGE);
+                            if (!(fabsf(a) <= 65504.0f)) atomicCAS(p.err, 0u, (uint32_t)ST_RANGE);
                         }
                         th[cl * 16 + jl] = ah;
                     }
@@ -845,7 +841,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 }
             }
             tc_fence_before();
-            mbar_arrive(&acc_empty[b]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
             ++it_acc;
             if (tr_lane) c1 += clock64() - tb0;
         }
@@ -1079,6 +1076,17 @@ __global__ void __launch_bounds__(256) k_pf_scatter(PfRoute p) {
         }
         off += total;
     }
+    if (e == p.n_routed - 1 && tid == 0) p.counts[p.n_routed] = off;  // pairs in total
+}
+
+// x rows in pair order (one warp per pair row), the gate/up GEMM's B rows
+__global__ void __launch_bounds__(256) k_pf_permute(const int32_t* npairs, const int32_t* pair_tok,
+                                                    const __half* xh, __half* xperm, int H) {
+    const int pr = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (pr >= *npairs) return;
+    const uint4* src = reinterpret_cast<const uint4*>(xh + (size_t)pair_tok[pr] * H);
+    uint4* dst = reinterpret_cast<uint4*>(xperm + (size_t)pr * H);
+    for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -1147,7 +1155,7 @@ bool prefill_supported(const moe_b200_layer* L, int flags) {
 }
 
 struct PfWs {
-    size_t counts, xs_inv, sg, xh, xl, rh, rl, rs_inv, logits, ids, w, ptok, pw, act, total;
+    size_t counts, xs_inv, sg, xh, xl, rh, rl, rs_inv, logits, ids, w, ptok, pw, act, xperm, total;
 };
 
 static PfWs pf_ws(const moe_b200_layer* L, int T) {
@@ -1171,6 +1179,7 @@ static PfWs pf_ws(const moe_b200_layer* L, int T) {
     w.ptok = s.take((size_t)T * K * 4);
     w.pw = s.take((size_t)T * K * 4);
     w.act = s.take(((size_t)T * K + T) * Imax * 2);
+    w.xperm = s.take((size_t)T * K * H * 2);
     w.total = s.used;
     return w;
 }
@@ -1301,8 +1310,8 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
         PfParams rp2 = gp;
         bool ok = make_map(&rp2.rmap[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.rh, H, E, (uint64_t)H * 2, 64, 128, true) &&
                   make_map(&rp2.rmap[1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.rl, H, E, (uint64_t)H * 2, 64, 128, true) &&
-                  make_map(&rp2.bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.xh, H, T, (uint64_t)H * 2, 64, 16, true) &&
-                  make_map(&rp2.bmap2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.xl, H, T, (uint64_t)H * 2, 64, 16, true);
+                  make_map(&rp2.rbmap[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.xh, H, T, (uint64_t)H * 2, 64, 16, true) &&
+                  make_map(&rp2.rbmap[1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.xl, H, T, (uint64_t)H * 2, 64, 16, true);
         if (!ok) return ST_INTERNAL;
         rp2.segs = 3;
         rp2.stages = 6;
@@ -1319,6 +1328,9 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
         k_pf_scatter<<<n_routed, 256, 0, s>>>(rp);
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
+        k_pf_permute<<<(T * K + 7) / 8, 256, 0, s>>>(pp.counts + n_routed, rp.pair_tok, pp.xh,
+                                                     reinterpret_cast<__half*>(base + W.xperm), H);
+        if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
     }
 
     // expert GEMMs
@@ -1329,7 +1341,12 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     // gate/up
     {
         PfParams g = gp;
-        bool ok = make_map(&g.bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.xh, H, T, (uint64_t)H * 2, 64, 1, true);
+        __half* xperm = reinterpret_cast<__half*>(base + W.xperm);
+        const uint64_t prows = (uint64_t)T * K;
+        bool ok = make_map(&g.bmap[0][0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xperm, H, prows, (uint64_t)H * 2, 64, 128, true) &&
+                  make_map(&g.bmap[0][1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xperm, H, prows, (uint64_t)H * 2, 64, 16, true) &&
+                  make_map(&g.bmap[1][0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.xh, H, T, (uint64_t)H * 2, 64, 128, true) &&
+                  make_map(&g.bmap[1][1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.xh, H, T, (uint64_t)H * 2, 64, 16, true);
         if (routed) {
             const int t0 = L->gate_type, t1 = L->up_type;
             const uint64_t rb0 = row_bytes(t0, H), rb1 = row_bytes(t1, H);
@@ -1362,7 +1379,10 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     // down
     {
         PfParams g = gp;
-        bool ok = make_map(&g.bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, gp.act, Imax, act_rows, (uint64_t)Imax * 2, 64, 16, true);
+        bool ok = make_map(&g.bmap[0][0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, gp.act, Imax, act_rows, (uint64_t)Imax * 2, 64, 128, true) &&
+                  make_map(&g.bmap[0][1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, gp.act, Imax, act_rows, (uint64_t)Imax * 2, 64, 16, true);
+        g.bmap[1][0] = g.bmap[0][0];
+        g.bmap[1][1] = g.bmap[0][1];
         if (routed) {
             const int tw = pf_w(L->down_type);
             const uint64_t rb = row_bytes(L->down_type, L->intermediate);
@@ -1393,7 +1413,7 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
 
 int prefill_kernels(const moe_b200_layer* L) {
     const bool routed = !(L->flags & MOE_B200_SHARED_ONLY);
-    return routed ? 7 : 3;
+    return routed ? 8 : 3;
 }
 
 }  // namespace moeb200

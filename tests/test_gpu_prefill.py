@@ -211,4 +211,4 @@ def test_prefill_kernel_count():
     s = be.store.layer(0).with_flags(0)
     n = C.c_int(0)
     assert be.lib.moe_b200_prefill_kernels(C.byref(s), C.byref(n)) == 0
-    assert n.value == 7
+    assert n.value == 8
