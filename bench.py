@@ -20,6 +20,10 @@ step on the host cores: the reference's AVX2 moe_quant_expert (compiled from
 its sources into oracle/_ref) for the 8 routed experts on a thread pool, and
 the numpy router / combine / shared expert of its Python layer.
 
+At N = 1 the line also carries "prefill" (config 4: 4096 bf16 tokens on the
+tensor cores, TFLOP/s against the measured bf16 peak) and "batched_decode"
+(config 3: 64 tokens with a Zipf(1.1) router bias).
+
 Prints one JSON line (rank 0).
 """
 from __future__ import annotations
@@ -206,6 +210,84 @@ def run_reference_arm(args) -> None:
 
 # --------------------------------------------------------------------- GPU arm
 
+PREFILL_FLOPS_PER_TOKEN = 8 * 3 * 2 * 2048 * 512 + 3 * 2 * 2048 * 512 + 2 * 2048 * 256
+
+
+def _time_calls(fn, n: int, warmup: int = 3) -> float:
+    """Mean device milliseconds of fn() over n calls (CUDA events)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
+def bench_prefill(backend, layer: int, dev, peaks: dict, peak_kind: str) -> dict:
+    """Config 4: 4096 bf16 tokens through the config-2 layer on the tensor
+    cores (moe_b200_prefill).  The packed weights (382 MB) exceed L2, so each
+    call streams them from HBM."""
+    import torch
+    from flash_moe_b200 import synth
+    T = 4096
+    lw = backend.store.layer(layer).weights
+    x = torch.from_numpy(synth.make_tokens(404, T, lw.hidden)).to(dev).to(torch.bfloat16)
+    y = torch.empty((T, lw.hidden), dtype=torch.float32, device=dev)
+    ms = _time_calls(lambda: backend.prefill_device(layer, x, y), 10)
+    err = backend.prefill_errors()
+    flops = PREFILL_FLOPS_PER_TOKEN * T
+    tf = flops / (ms / 1e3) / 1e12
+    peak = peaks.get("bf16_tflops", 1590.0)
+    return {"config": "config 4: 4096 bf16 tokens, config-2 layer (256 experts top-8, Q3_K/Q4_K + "
+                      "Q8_0 shared), fp16 operands on tcgen05 with fp32 accumulation",
+            "us_per_layer": round(ms * 1e3, 1), "tokens_per_s": round(T / (ms / 1e3)),
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(tf / peak, 4),
+                         "flops_per_layer": flops,
+                         "peak_source": f"{peak_kind} bf16_tflops (dense fp16 runs at the same rate)"},
+            "kernels_per_call": backend.prefill_kernels(layer), "device_error": err}
+
+
+def bench_batched(dev, peaks: dict, peak_kind: str) -> dict:
+    """Config 3: 64 concurrent tokens on the config-2 layer with a Zipf(1.1)
+    router bias, one GPU: the fp32 decode engine and the tensor-core path."""
+    import torch
+    from flash_moe_b200 import synth
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    lw = synth.make_layer(seed=0, zipf_s=1.1)
+    arena = ExpertArena(dev)
+    arena.add_layer(0, lw)
+    be = B200ExpertBackend(arena)
+    T = 64
+    x = torch.from_numpy(synth.make_tokens(3000, T, lw.hidden)).to(dev)
+    y = torch.empty_like(x)
+    ids = torch.empty((T, lw.top_k), dtype=torch.int32, device=dev)
+    ms_dec = _time_calls(lambda: be.forward_layer_device(0, x, y, ids), 20)
+    uniq = int(np.unique(ids.cpu().numpy()).size)
+    ms_pf = _time_calls(lambda: be.prefill_device(0, x, y, ids), 20)
+    err = be.prefill_errors()
+    algo = uniq * EXPERT_BYTES + SHARED_BYTES + ROUTER_BYTES + T * 2 * lw.hidden * 4
+    best = min(ms_dec, ms_pf)
+    gbs = algo / (best / 1e3) / 1e9
+    out = {"config": "config 3: 64 tokens/step, Zipf(s=1.1) router bias, 1 GPU",
+           "unique_experts": uniq, "algorithmic_bytes_per_step": algo,
+           "us_per_step_decode_engine": round(ms_dec * 1e3, 1),
+           "us_per_step_tensor_core_path": round(ms_pf * 1e3, 1),
+           "tokens_per_s": round(T / (best / 1e3)),
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                        "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                        "peak_source": f"{peak_kind} hbm_gbs"},
+           "device_error": err}
+    be.close()
+    return out
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -307,6 +389,10 @@ def run_gpu(args) -> None:
                "sample": f"{n} tokens of the same layer ({per_tok * 1e6:.0f} us/token), {cpu_model()}"}
     used_graph = graph is not None
     graph = None
+    extra = {}
+    if rank == 0 and world == 1 and not args.no_extra:
+        extra["prefill"] = bench_prefill(backend, 0, dev, peaks, peak_kind)
+        extra["batched_decode"] = bench_batched(dev, peaks, peak_kind)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": UNIT, "n_gpus": world,
@@ -330,6 +416,7 @@ def run_gpu(args) -> None:
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        line.update(extra)
         print(json.dumps(line), flush=True)
     runner.close()
     if world > 1:
@@ -349,6 +436,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak", type=float, default=0.5)
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the prefill and batched-decode measurements (N = 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

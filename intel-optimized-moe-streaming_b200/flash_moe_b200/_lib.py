@@ -26,6 +26,7 @@ STATUS = {
 FP16_GRAPH = 1
 NO_SHARED = 2
 EXACT = 4
+SHARED_ONLY = 8
 
 
 class Layer(C.Structure):

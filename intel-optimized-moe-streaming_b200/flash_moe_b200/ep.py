@@ -28,6 +28,31 @@ import torch
 
 from . import _lib
 
+def expert_range(n_experts: int, world: int, rank: int) -> tuple[int, int]:
+    """(first, count) of the routed experts rank `rank` of `world` holds."""
+    if n_experts % world:
+        raise ValueError(f"{n_experts} experts do not split over {world} ranks")
+    per = n_experts // world
+    return rank * per, per
+
+
+def ep_exchange_step(x, routed_fn, shared_fn, x_all, y_part, y_routed, y_sh, y,
+                     group=None) -> None:
+    """One expert-parallel layer step of this rank's tokens ``x`` [t, H].
+
+    ``routed_fn(x_all, y_part)`` writes, for all ``world * t`` gathered
+    tokens, the weighted sum of the outputs of the experts this rank holds;
+    ``shared_fn(x, y_sh)`` writes the gated shared expert of the own tokens.
+    The collectives are the same on every rank and in the same order
+    (all-gather, then reduce-scatter), whatever the device or backend."""
+    import torch.distributed as dist
+    dist.all_gather_into_tensor(x_all, x, group=group)
+    routed_fn(x_all, y_part)
+    dist.reduce_scatter_tensor(y_routed, y_part, group=group)
+    shared_fn(x, y_sh)
+    torch.add(y_routed, y_sh, out=y)
+
+
 def profiled_traffic(root: Path, name: str = "decode_layer") -> float | None:
     """DRAM bytes per launch of the decode kernel from the committed ncu
     summary (``profiles/<name>*.txt`` line ``traffic_bytes_per_launch: N``)."""
@@ -88,13 +113,13 @@ class DecodeRunner:
         if self.world == 1:
             self.be.forward_layer_device(layer, x, y, topk_ids=self.ids[slot])
             return
-        import torch.distributed as dist
-        dist.all_gather_into_tensor(self.x_all, x)
-        self.be.forward_layer_device(layer, self.x_all, self.y_part, topk_ids=self.ids[slot],
-                                     flags=self._flags(_lib.NO_SHARED))
-        dist.reduce_scatter_tensor(self.y_routed, self.y_part)
-        self.be.forward_layer_device(layer, x, self.y_sh, flags=self._flags(_lib.SHARED_ONLY))
-        torch.add(self.y_routed, self.y_sh, out=y)
+        ep_exchange_step(
+            x,
+            lambda xa, yp: self.be.forward_layer_device(layer, xa, yp, topk_ids=self.ids[slot],
+                                                        flags=self._flags(_lib.NO_SHARED)),
+            lambda xo, ys: self.be.forward_layer_device(layer, xo, ys,
+                                                        flags=self._flags(_lib.SHARED_ONLY)),
+            self.x_all, self.y_part, self.y_routed, self.y_sh, y)
 
     def capture(self, steps: int):
         """CUDA graph of `steps` consecutive steps (single GPU only)."""
