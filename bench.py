@@ -329,19 +329,30 @@ def run_gpu(args) -> None:
     torch.cuda.synchronize()
 
     graph = None
-    if not args.no_graph:
+    tables = None
+    if world == 1 and not args.single_launch:
+        # all K steps in one launch of the fused kernel (moe_b200_decode_steps)
+        tables = runner.step_tables(args.steps)
+        runner.run_tables(tables, args.steps)
+        torch.cuda.synchronize()
+    elif not args.no_graph:
         graph = runner.capture(args.steps)
+
+    def timed_steps():
+        if tables is not None:
+            runner.run_tables(tables, args.steps)
+        elif graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                runner.step(i)
 
     peaks, peak_kind = measured_peaks()
     with ClockSampler(local) as clk:
         # soak ~0.5 s so the clock sampler sees the GPU under this load
         t_end = time.perf_counter() + args.soak
         while time.perf_counter() < t_end:
-            if graph is not None:
-                graph.replay()
-            else:
-                for i in range(args.steps):
-                    runner.step(i)
+            timed_steps()
             torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -349,11 +360,7 @@ def run_gpu(args) -> None:
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
-        if graph is not None:
-            graph.replay()
-        else:
-            for i in range(args.steps):
-                runner.step(i)
+        timed_steps()
         ev1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -370,12 +377,16 @@ def run_gpu(args) -> None:
     per_step_ms = ms_max / args.steps
     gbs = total_bytes / (ms_max / 1e3) / 1e9
 
+    launch_mode = ("one launch of all steps" if tables is not None
+                   else "CUDA graph of per-step launches" if graph is not None else "per-step launches")
     # roofline of the decode kernel chain on this rank (one launch sequence
     # per step), from the same timed region
     ach = bytes_local / (ms / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": EP.profiled_traffic(ROOT),
-            "peak_source": f"{peak_kind} hbm_gbs", "kernel": runner.kernel_name}
+            "peak_source": f"{peak_kind} hbm_gbs",
+            "kernel": ("k_decode_fused (all steps in one launch)" if launch_mode.startswith("one")
+                       else runner.kernel_name)}
 
     # end to end through the public API: pinned host token in, host result out
     e2e = runner.e2e(args.steps, args.warmup)
@@ -387,8 +398,9 @@ def run_gpu(args) -> None:
         cpu = {"value": round(step_bytes(8) / per_tok / 1e9, 4), "unit": UNIT,
                "cores": os.cpu_count() or 1, "kind": kind,
                "sample": f"{n} tokens of the same layer ({per_tok * 1e6:.0f} us/token), {cpu_model()}"}
-    used_graph = graph is not None
+    launches = 1 if tables is not None else runner.launches_per_step * args.steps
     graph = None
+    tables = None
     extra = {}
     if rank == 0 and world == 1 and not args.no_extra:
         extra["prefill"] = bench_prefill(backend, 0, dev, peaks, peak_kind)
@@ -407,11 +419,11 @@ def run_gpu(args) -> None:
                        "l2": f"rotating {args.copies} layer copies at distinct addresses "
                              f"({args.copies * step_bytes(8) / 1e6:.0f} MB touched per rotation > 2x L2)",
                        "parallelism": f"ep{world}" if world > 1 else "single",
-                       "engine": args.engine, "cuda_graph": used_graph,
+                       "engine": args.engine, "launch": launch_mode,
                        "algorithmic_bytes_per_token": step_bytes(8)},
             "roofline": roof,
             "e2e": e2e,
-            "gpu_launches": runner.launches_per_step * args.steps,
+            "gpu_launches": launches,
             "clocks": clk.summary(),
         }
         if cpu is not None:
@@ -433,6 +445,8 @@ def main() -> None:
     ap.add_argument("--copies", type=int, default=16)
     ap.add_argument("--engine", choices=["fast", "exact"], default="fast")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--single-launch", action="store_true",
+                    help="one kernel launch per step (CUDA graph) instead of one for all steps")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak", type=float, default=0.5)

@@ -200,6 +200,38 @@ MOE_B200_API int moe_b200_prefill_supported(const moe_b200_layer* layer);
  * MOE_B200_SHARED_ONLY). */
 MOE_B200_API int moe_b200_prefill_kernels(const moe_b200_layer* layer, int* kernels);
 
+/* One step of a multi-step decode launch (moe_b200_decode_steps). */
+typedef struct moe_b200_step {
+    int32_t layer;            /* index into the layer table */
+    int32_t flags;            /* MOE_B200_STEP_* */
+    const float* x;           /* device [hidden] token (not read with CHAIN) */
+    float* y;                 /* device [hidden] output */
+    int32_t* topk_ids;        /* device [top_k] or NULL */
+    float* topk_weights;      /* device [top_k] or NULL */
+} moe_b200_step;
+
+#define MOE_B200_STEP_CHAIN 1 /* the input is the previous step's output */
+#define MOE_B200_STEP_BLOCK 2 /* transformer block with an identity mixer:
+                                 h = x + rmsnorm16(x), y = h + f16(MoE(rmsnorm16(h))),
+                                 RMSNorm weight 1 (src/flash_moe/transformer.py:229-247,
+                                 norm.py:21-30) */
+
+/* n_steps single-token layer steps in ONE cooperative launch of the fused
+ * decode kernel: the whole decode of a token through a stack of layers
+ * (CHAIN | BLOCK steps), or independent tokens.  No reference function has
+ * this signature: it replaces the per-layer loop of Qwen3MoEModel.forward
+ * (src/flash_moe/model.py) over run_moe_layer (moe_layer.py:39-107) for a
+ * decode step.  layer0 (host) gives the shapes and block formats that every
+ * layer of the device table layers_dev shares, and the flags (NO_SHARED
+ * allowed); steps_dev is a device array of n_steps entries.  The workspace
+ * is the one moe_b200_decode_workspace(layer0, 1, ...) sizes.  Returns -2
+ * when the fused kernel does not take these shapes or formats. */
+MOE_B200_API int moe_b200_decode_steps(const moe_b200_layer* layer0,
+                                       const moe_b200_layer* layers_dev,
+                                       const moe_b200_step* steps_dev, int32_t n_steps,
+                                       float eps, void* workspace, size_t workspace_bytes,
+                                       void* stream);
+
 /* Largest `intermediate` moe_b200_expert_noalloc accepts. */
 #define MOE_B200_NOALLOC_MAX_INTERMEDIATE 16384
 

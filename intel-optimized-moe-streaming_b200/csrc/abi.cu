@@ -422,6 +422,23 @@ int moe_b200_decode(const moe_b200_layer* L, const float* x, int32_t T, float* y
     return ST_OK;
 }
 
+int moe_b200_decode_steps(const moe_b200_layer* L0, const moe_b200_layer* layers,
+                          const moe_b200_step* steps, int32_t n_steps, float eps, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    int st = check_layer(L0);
+    if (st != ST_OK) return st;
+    if (!layers || !steps || n_steps < 1 || !workspace || !(eps >= 0.f)) return ST_ARG;
+    if (((uintptr_t)workspace & 255u) || ((uintptr_t)steps & 15u) || ((uintptr_t)layers & 15u))
+        return ST_ALIGN;
+    if (!fused_supported(L0, 1, L0->flags)) return ST_TYPE;
+    if (workspace_bytes < decode_ws(L0, 1).total) return ST_WORKSPACE;
+    bool launched = false;
+    cudaError_t e = launch_decode_steps(L0, layers, steps, n_steps, eps, workspace,
+                                        static_cast<cudaStream_t>(stream), &launched);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    return launched ? ST_OK : ST_TYPE;
+}
+
 int moe_b200_prefill_supported(const moe_b200_layer* L) {
     if (check_layer(L) != ST_OK) return 0;
     return prefill_supported(L, L->flags) ? 1 : 0;

@@ -39,27 +39,30 @@ constexpr uint32_t kWaitPolls = 1u << 21;
 constexpr int kTraceSlots = 32;
 constexpr int kMaxChunks = 8;  // routed gate/up copy chunks (mbarriers 3..10)
 
-enum { C_ROUTER = 0, C_SHARED = 1, C_GATEUP = 2, C_EXIT = 3, C_ERROR = 8 };
+enum { C_ROUTER = 0, C_SHARED = 1, C_GATEUP = 2, C_EXIT = 3, C_DONE = 4, C_ERROR = 8 };
 
 struct FusedParams {
-    moe_b200_layer L;
-    const float* x;
+    moe_b200_layer L;        // shapes and block formats of every step's layer
+    const float* x;          // single-step launch: the token
     float* y;
     int32_t* ids_out;
     float* w_out;
-    uint32_t* ctr;   // counters, error word at ctr[C_ERROR]
-    float* scores;   // [E]
-    float* act_r;    // [K x I]
-    float* act_s;    // [Is]
-    float* sg;       // [1]
-    uint64_t* trace; // [G x 16] phase timestamps (ns), or null
+    const moe_b200_layer* layers;  // multi-step launch: layer table (device)
+    const moe_b200_step* steps;    // step table (device), or null
+    int n_steps;
+    float eps;               // RMSNorm epsilon of MOE_B200_STEP_BLOCK steps
+    uint32_t* ctr;           // counters, error word at ctr[C_ERROR]
+    float* scores;           // [2][E]       (buffer = step parity)
+    float* act_r;            // [2][K x I]
+    float* act_s;            // [2][Imax]
+    float* sg;               // [2]
+    uint64_t* trace;         // [G x 32] phase timestamps of the first step (ns), or null
     int G;
     int with_shared;
     int max_router_rows, max_sgu_rows, max_out_rows, max_rgu_rows;
     int lpr_h, lpr_i, lpr_is;
     int chunk_rows;
-    int warm;
-    uint32_t o_x32, o_xq, o_router, o_sgate, o_sup, o_sdown, o_rgate, o_rup, o_rdown;
+    uint32_t o_x32, o_h32, o_xq, o_router, o_sgate, o_sup, o_sdown, o_rgate, o_rup, o_rdown;
     uint32_t o_act, o_aq, o_misc, total;
 };
 
@@ -84,23 +87,38 @@ __device__ __forceinline__ float dot_f32_warp(const float* row, const float* x, 
     return warp_sum(acc);
 }
 
+// Sum of v over the CTA in a fixed order (warp trees, then warps in order);
+// every thread gets the result.  `part` holds 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* part) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) part[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < kFusedThreads / 32; ++i) t += part[i];
+    return t;
+}
+
 // GU: gate and up type, DN: routed down type, SGU: shared gate and up type,
 // SDN: shared down type -- each a ggml type id fixed at compile time, or -1
 // to dispatch on the layer's runtime types (the generic instance).
 template <int GU, int DN, int SGU, int SDN>
 __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_constant__ FusedParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
-    const moe_b200_layer& L = p.L;
+    const moe_b200_layer& L0 = p.L;
     const int c = blockIdx.x, G = p.G, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nw = kFusedThreads / 32;
-    const int H = L.hidden, I = L.intermediate, E = L.n_experts, K = L.top_k;
-    const int Is = p.with_shared ? L.shared_intermediate : 0;
-    const int64_t rb_gate = row_bytes(L.gate_type, H), rb_up = row_bytes(L.up_type, H);
-    const int64_t rb_down = row_bytes(L.down_type, I);
+    const int H = L0.hidden, I = L0.intermediate, E = L0.n_experts, K = L0.top_k;
+    const int Is = p.with_shared ? L0.shared_intermediate : 0;
+    const int ebeg = L0.expert_begin, ecnt = L0.expert_count;
+    const int64_t rb_gate = row_bytes(L0.gate_type, H), rb_up = row_bytes(L0.up_type, H);
+    const int64_t rb_down = row_bytes(L0.down_type, I);
     const int64_t st_gate = rb_gate * I, st_up = rb_up * I, st_down = rb_down * H;
-    const int64_t rb_sg = Is ? row_bytes(L.shared_gate_type, H) : 0;
-    const int64_t rb_su = Is ? row_bytes(L.shared_up_type, H) : 0;
-    const int64_t rb_sd = Is ? row_bytes(L.shared_down_type, Is) : 0;
+    const int64_t rb_sg = Is ? row_bytes(L0.shared_gate_type, H) : 0;
+    const int64_t rb_su = Is ? row_bytes(L0.shared_up_type, H) : 0;
+    const int64_t rb_sd = Is ? row_bytes(L0.shared_down_type, Is) : 0;
+    const int Imax = max(I, Is);
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + p.o_misc);       // [3 + kMaxChunks]
     int* s_ids = reinterpret_cast<int*>(sm + p.o_misc + 128);          // [16]
@@ -108,333 +126,390 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     int* s_act = reinterpret_cast<int*>(sm + p.o_misc + 256);          // [16] active slots
     int* s_nact = reinterpret_cast<int*>(sm + p.o_misc + 320);
     float* s_sg = reinterpret_cast<float*>(sm + p.o_misc + 324);
-    float* s_part = reinterpret_cast<float*>(sm + p.o_misc + 384);     // [32] router partials
+    float* s_part = reinterpret_cast<float*>(sm + p.o_misc + 384);     // [32] partial sums
     float* s_scores = reinterpret_cast<float*>(sm + p.o_misc + 512);   // [E]
     unsigned char* s_taken = reinterpret_cast<unsigned char*>(s_scores + E);
     float* s_vout = reinterpret_cast<float*>(sm + p.o_misc + 512 + ((5 * E + 15) & ~15));
+    float* x32 = reinterpret_cast<float*>(sm + p.o_x32);
+    float* h32 = reinterpret_cast<float*>(sm + p.o_h32);
 
     const int r0 = part(E, c, G), r1 = part(E, c + 1, G);
     const int s0 = part(Is, c, G), s1 = part(Is, c + 1, G);
     const int h0 = part(H, c, G), h1 = part(H, c + 1, G);
     const int nh = h1 - h0;
-    uint64_t* trace = p.trace ? p.trace + (size_t)c * kTraceSlots : nullptr;
-#define TRACE(i) do { if (trace && tid == 0) trace[i] = global_ns(); } while (0)
-    TRACE(0);
+    const int lpr_h = p.lpr_h, sub_h = lane / lpr_h, pr_h = lane % lpr_h;
+    const QVec xq = qvec_at(sm + p.o_xq, H);
+
+    auto step_layer = [&](int s) -> const moe_b200_layer* {
+        return p.steps ? p.layers + p.steps[s].layer : &p.L;
+    };
+    // router rows of step s on bars[0], its shared-expert rows on bars[1]
+    auto issue_phase0 = [&](const moe_b200_layer* Ls) {
+        const float* router = Ls->router;
+        mbar_arrive_expect_tx(&bars[0], (uint32_t)((r1 - r0) * H * 4));
+        if (r1 > r0)
+            bulk_g2s(sm + p.o_router, router + (size_t)r0 * H, (uint32_t)((r1 - r0) * H * 4), &bars[0]);
+        if (Is) {
+            const uint8_t* sgp = Ls->shared_gate;
+            const uint8_t* sup = Ls->shared_up;
+            const uint8_t* sdp = Ls->shared_down;
+            mbar_arrive_expect_tx(&bars[1], (uint32_t)((s1 - s0) * (rb_sg + rb_su) + nh * rb_sd));
+            if (s1 > s0) {
+                bulk_g2s(sm + p.o_sgate, sgp + s0 * rb_sg, (uint32_t)((s1 - s0) * rb_sg), &bars[1]);
+                bulk_g2s(sm + p.o_sup, sup + s0 * rb_su, (uint32_t)((s1 - s0) * rb_su), &bars[1]);
+            }
+            if (nh > 0)
+                bulk_g2s(sm + p.o_sdown, sdp + h0 * rb_sd, (uint32_t)(nh * rb_sd), &bars[1]);
+        }
+    };
 
     if (tid == 0) {
         for (int i = 0; i < 3 + kMaxChunks; ++i) mbar_init(&bars[i], 1);
         mbar_fence_init();
     }
     __syncthreads();
-    // ---- phase-0 copies: router rows, shared gate/up rows, shared down rows
-    if (tid == 0) {
-        uint32_t bytes = (uint32_t)((r1 - r0) * H * 4);
-        if (Is) bytes += (uint32_t)((s1 - s0) * (rb_sg + rb_su) + nh * rb_sd);
-        mbar_arrive_expect_tx(&bars[0], bytes);
-        if (r1 > r0)
-            bulk_g2s(sm + p.o_router, L.router + (size_t)r0 * H, (uint32_t)((r1 - r0) * H * 4), &bars[0]);
-        if (Is && s1 > s0) {
-            bulk_g2s(sm + p.o_sgate, L.shared_gate + s0 * rb_sg, (uint32_t)((s1 - s0) * rb_sg), &bars[0]);
-            bulk_g2s(sm + p.o_sup, L.shared_up + s0 * rb_su, (uint32_t)((s1 - s0) * rb_su), &bars[0]);
+    if (tid == 0) issue_phase0(step_layer(0));
+    uint32_t ph = 0;  // parity of the phase each mbarrier is in
+
+    for (int s = 0; s < p.n_steps; ++s) {
+        uint64_t* trace = (p.trace && s == 0) ? p.trace + (size_t)c * kTraceSlots : nullptr;
+#define TRACE(i) do { if (trace && tid == 0) trace[i] = global_ns(); } while (0)
+        TRACE(0);
+        const moe_b200_layer* Ls = step_layer(s);
+        const uint32_t gen = (uint32_t)G * (uint32_t)(s + 1);  // counter value once step s is done
+        int sflags = 0;
+        const float* xin = p.x;
+        float* yout = p.y;
+        int32_t* ids_out = p.ids_out;
+        float* w_out = p.w_out;
+        if (p.steps) {
+            const moe_b200_step& st = p.steps[s];
+            sflags = st.flags;
+            xin = (sflags & MOE_B200_STEP_CHAIN) && s > 0 ? p.steps[s - 1].y : st.x;
+            yout = st.y;
+            ids_out = st.topk_ids;
+            w_out = st.topk_weights;
         }
-        if (Is && nh > 0)
-            bulk_g2s(sm + p.o_sdown, L.shared_down + h0 * rb_sd, (uint32_t)(nh * rb_sd), &bars[0]);
-    }
-    // ---- the token, fp32 and quantised
-    float* x32 = reinterpret_cast<float*>(sm + p.o_x32);
-    for (int i = tid; i < H; i += kFusedThreads) x32[i] = p.x[i];
-    __syncthreads();
-    const QVec xq = qvec_at(sm + p.o_xq, H);
-    for (int b = warp; b < H / 256; b += nw) quantize_block_warp(x32, xq, b);
-    __syncthreads();
-    TRACE(1);
-    if (Is && c == 0 && warp == 0) {
-        float acc = 0.f;
-        for (int i = lane; i < H; i += 32) acc = fmaf(x32[i], L.shared_gate_inp[i], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) p.sg[0] = shared_sigmoid(acc);
-    }
-    // lane -> (row-in-warp, pair) for H-long rows
-    const int lpr_h = p.lpr_h, sub_h = lane / lpr_h, pr_h = lane % lpr_h;
-    XLane xl;
-    load_xlane(xl, xq, pr_h >> 2, pr_h & 3);
+        const int buf = s & 1;
+        float* scores = p.scores + (size_t)buf * E;
+        float* act_r = p.act_r + (size_t)buf * K * I;
+        float* act_s = p.act_s + (size_t)buf * Imax;
+        float* sgp = p.sg + buf;
+        const bool chain = (sflags & MOE_B200_STEP_CHAIN) && s > 0;
+        const bool block = (sflags & MOE_B200_STEP_BLOCK) != 0;
 
-    // ---- instruction-cache warm-up while the first copies are in flight.
-    // Each kernel launch runs its critical-path code once per CTA, so every
-    // phase would otherwise start on cold instruction caches.  Here the
-    // decoders and the top-k run once on dummy data (4 warps per region, one
-    // per SM sub-partition); their results feed a store guarded by a
-    // condition that never holds (G > 0), so nothing is written.
-    if (p.warm) {
-        float dummy = 0.f;
-        const uint8_t* junk = sm + p.o_x32;
-        const int region = warp >> 2;
-        if (region == 0) {
-            dummy = qdot_t<GU>(L.gate_type, junk, 0, lane & 3, xl);
-        } else if (region == 1) {
-            dummy = qdot_t<DN>(L.down_type, junk, 0, lane & 3, xl);
-        } else if (region == 2) {
-            if (Is)
-                dummy = qdot_t<SGU>(L.shared_gate_type, junk, 0, lane & 3, xl) +
-                        qdot_t<SDN>(L.shared_down_type, junk, 0, lane & 3, xl);
-        } else if (E <= 256) {
-            int di[kMaxTopK];
-            float dw[kMaxTopK];
-            topk_softmax_warp_fast(p.scores, E, K, di, dw);
-            dummy = dw[lane % K] + (float)di[lane % K];
-        }
-        dummy = group_sum(dummy, 32);
-        if (G < 0 && dummy == 1.2345f) p.y[0] = dummy;
-    }
-
-    if (!mbar_wait(&bars[0], 0, kWaitPolls) && tid == 0) set_error(p.ctr, ST_TIMEOUT);
-    __syncthreads();
-    TRACE(2);
-
-    // ---- router scores: each of the CTA's R rows is split over nw/R warps,
-    // partial sums combined in a fixed order (deterministic)
-    {
-        const float* router_s = reinterpret_cast<const float*>(sm + p.o_router);
-        const int R = r1 - r0;
-        if (R > 0 && R <= nw) {
-            const int spr = nw / R;
-            const int row = warp / spr, sl = warp % spr;
-            if (row < R) {
-                const int cw = (H / spr) & ~3;  // 16-byte aligned slices
-                const int c0 = sl * cw, cn = (sl == spr - 1) ? H - c0 : cw;
-                float acc = dot_f32_warp(router_s + (size_t)row * H + c0, x32 + c0, cn, lane);
-                if (lane == 0) s_part[warp] = acc;
-            }
+        // ---- the token (after the previous step, whose output it is, when chained)
+        if (chain) {
+            if (tid == 0 && !wait_flag(p.ctr + C_DONE, (uint32_t)G * (uint32_t)s, kWaitPolls))
+                set_error(p.ctr, ST_TIMEOUT);
             __syncthreads();
-            if (tid < R) {
-                float acc = 0.f;
-                for (int q = 0; q < spr; ++q) acc += s_part[tid * spr + q];
-                if (L.router_bias) acc = __fadd_rn(acc, L.router_bias[r0 + tid]);
-                p.scores[r0 + tid] = acc;
-            }
+            for (int i = tid; i < H; i += kFusedThreads) x32[i] = __ldcg(xin + i);
         } else {
-            for (int rr = warp; rr < R; rr += nw) {
-                float acc = dot_f32_warp(router_s + (size_t)rr * H, x32, H, lane);
-                if (lane == 0) {
-                    if (L.router_bias) acc = __fadd_rn(acc, L.router_bias[r0 + rr]);
-                    p.scores[r0 + rr] = acc;
-                }
-            }
+            for (int i = tid; i < H; i += kFusedThreads) x32[i] = xin[i];
         }
-    }
-    __syncthreads();
-    if (tid == 0) red_release_add(p.ctr + C_ROUTER, 1);
-    TRACE(3);
-
-    // ---- shared expert gate/up (x is the token)
-    if (Is) {
-        const int rpw = 32 / lpr_h;
-        for (int rb = warp * rpw; rb < s1 - s0; rb += nw * rpw) {
-            const int rr = rb + sub_h;
-            const bool ok = rr < s1 - s0;
-            const int rs = ok ? rr : 0;
-            float g = qdot_t<SGU>(L.shared_gate_type, sm + p.o_sgate + rs * rb_sg, pr_h >> 2, pr_h & 3, xl);
-            float u = qdot_t<SGU>(L.shared_up_type, sm + p.o_sup + rs * rb_su, pr_h >> 2, pr_h & 3, xl);
-            g = group_sum(g, lpr_h);
-            u = group_sum(u, lpr_h);
-            if (ok && pr_h == 0) p.act_s[s0 + rr] = (g * shared_sigmoid(g)) * u;
-        }
-    }
-    __syncthreads();
-    if (tid == 0) red_release_add(p.ctr + C_SHARED, 1);
-    TRACE(4);
-
-    // ---- routing (every CTA, identically)
-    if (tid == 0 && !wait_flag(p.ctr + C_ROUTER, (uint32_t)G, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
-    __syncthreads();
-    TRACE(5);
-    if (E > 256) {
-        for (int e = tid; e < E; e += kFusedThreads) s_scores[e] = __ldcg(p.scores + e);
         __syncthreads();
-    }
-    if (warp == 0) {
-        if (E <= 256)
-            topk_softmax_warp_fast(p.scores, E, K, s_ids, s_w, trace);
-        else
-            topk_softmax_warp(s_scores, s_taken, E, K, s_ids, s_w);
-        if (lane == 0) {
-            int na = 0;
-            for (int k = 0; k < K; ++k) {
-                const int e = s_ids[k];
-                if (e >= L.expert_begin && e < L.expert_begin + L.expert_count) s_act[na++] = k;
+        if (block) {
+            // h = x + rmsnorm16(x); the MoE input is rmsnorm16(h)
+            // (reference TransformerBlock.forward with an identity mixer,
+            // src/flash_moe/transformer.py:229-247; RMSNorm norm.py:28-30)
+            float ss = 0.f;
+            for (int i = tid; i < H; i += kFusedThreads) ss = fmaf(x32[i], x32[i], ss);
+            ss = block_sum(ss, s_part);
+            const float rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)H), p.eps));
+            float ss2 = 0.f;
+            for (int i = tid; i < H; i += kFusedThreads) {
+                const float hv = __fadd_rn(x32[i], round16(__fdiv_rn(x32[i], rms)));
+                h32[i] = hv;
+                ss2 = fmaf(hv, hv, ss2);
             }
-            *s_nact = na;
-            if (c == 0) {
+            ss2 = block_sum(ss2, s_part);
+            const float rms2 = sqrtf(__fadd_rn(__fdiv_rn(ss2, (float)H), p.eps));
+            for (int i = tid; i < H; i += kFusedThreads) x32[i] = round16(__fdiv_rn(h32[i], rms2));
+            __syncthreads();
+        }
+        TRACE(1);
+
+        // ---- router scores (rows [r0, r1)): each row split over nw/R warps,
+        // partial sums combined in a fixed order (deterministic)
+        if (tid == 0 && !mbar_wait(&bars[0], ph & 1u, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+        ph ^= 1u;
+        __syncthreads();
+        TRACE(2);
+        {
+            const float* router_s = reinterpret_cast<const float*>(sm + p.o_router);
+            const float* bias = Ls->router_bias;
+            const int R = r1 - r0;
+            if (R > 0 && R <= nw) {
+                const int spr = nw / R;
+                const int row = warp / spr, sl = warp % spr;
+                if (row < R) {
+                    const int cw = (H / spr) & ~3;  // 16-byte aligned slices
+                    const int cc0 = sl * cw, cn = (sl == spr - 1) ? H - cc0 : cw;
+                    float acc = dot_f32_warp(router_s + (size_t)row * H + cc0, x32 + cc0, cn, lane);
+                    if (lane == 0) s_part[warp] = acc;
+                }
+                __syncthreads();
+                if (tid < R) {
+                    float acc = 0.f;
+                    for (int q = 0; q < spr; ++q) acc += s_part[tid * spr + q];
+                    if (bias) acc = __fadd_rn(acc, bias[r0 + tid]);
+                    scores[r0 + tid] = acc;
+                }
+            } else {
+                for (int rr = warp; rr < R; rr += nw) {
+                    float acc = dot_f32_warp(router_s + (size_t)rr * H, x32, H, lane);
+                    if (lane == 0) {
+                        if (bias) acc = __fadd_rn(acc, bias[r0 + rr]);
+                        scores[r0 + rr] = acc;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (tid == 0) red_release_add(p.ctr + C_ROUTER, 1);
+        TRACE(3);
+
+        // ---- the token quantised for the integer dot products; shared gate
+        for (int b = warp; b < H / 256; b += nw) quantize_block_warp(x32, xq, b);
+        if (Is && c == 0 && warp == nw - 1) {
+            const float* ginp = Ls->shared_gate_inp;
+            float acc = 0.f;
+            for (int i = lane; i < H; i += 32) acc = fmaf(x32[i], ginp[i], acc);
+            acc = warp_sum(acc);
+            if (lane == 0) *sgp = shared_sigmoid(acc);
+        }
+        __syncthreads();
+        XLane xl;
+        load_xlane(xl, xq, pr_h >> 2, pr_h & 3);
+
+        // ---- shared expert gate/up (x is the token)
+        if (Is) {
+            if (tid == 0 && !mbar_wait(&bars[1], (ph >> 1) & 1u, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+            ph ^= 2u;
+            __syncthreads();
+            const int rpw = 32 / lpr_h;
+            for (int rb = warp * rpw; rb < s1 - s0; rb += nw * rpw) {
+                const int rr = rb + sub_h;
+                const bool ok = rr < s1 - s0;
+                const int rs = ok ? rr : 0;
+                float g = qdot_t<SGU>(L0.shared_gate_type, sm + p.o_sgate + rs * rb_sg, pr_h >> 2, pr_h & 3, xl);
+                float u = qdot_t<SGU>(L0.shared_up_type, sm + p.o_sup + rs * rb_su, pr_h >> 2, pr_h & 3, xl);
+                g = group_sum(g, lpr_h);
+                u = group_sum(u, lpr_h);
+                if (ok && pr_h == 0) act_s[s0 + rr] = (g * shared_sigmoid(g)) * u;
+            }
+        }
+        __syncthreads();
+        if (tid == 0) red_release_add(p.ctr + C_SHARED, 1);
+        TRACE(4);
+
+        // ---- routing (every CTA, identically)
+        if (tid == 0 && !wait_flag(p.ctr + C_ROUTER, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+        __syncthreads();
+        TRACE(5);
+        if (E > 256) {
+            for (int e = tid; e < E; e += kFusedThreads) s_scores[e] = __ldcg(scores + e);
+            __syncthreads();
+        }
+        if (warp == 0) {
+            if (E <= 256)
+                topk_softmax_warp_fast(scores, E, K, s_ids, s_w, trace);
+            else
+                topk_softmax_warp(s_scores, s_taken, E, K, s_ids, s_w);
+            if (lane == 0) {
+                int na = 0;
                 for (int k = 0; k < K; ++k) {
-                    if (p.ids_out) p.ids_out[k] = s_ids[k];
-                    if (p.w_out) p.w_out[k] = s_w[k];
+                    const int e = s_ids[k];
+                    if (e >= ebeg && e < ebeg + ecnt) s_act[na++] = k;
+                }
+                *s_nact = na;
+                if (c == 0) {
+                    for (int k = 0; k < K; ++k) {
+                        if (ids_out) ids_out[k] = s_ids[k];
+                        if (w_out) w_out[k] = s_w[k];
+                    }
                 }
             }
         }
-    }
-    __syncthreads();
-    TRACE(6);
-    const int A = *s_nact;
-    const int f0 = part(A * I, c, G), f1 = part(A * I, c + 1, G);
+        __syncthreads();
+        TRACE(6);
+        const int A = *s_nact;
+        const int f0 = part(A * I, c, G), f1 = part(A * I, c + 1, G);
 
-    // ---- phase-1 copies: routed gate/up rows of [f0, f1) in chunks of CR
-    // rows (one mbarrier each, issued in order so compute can start on the
-    // first chunk), then the routed down rows
-    const int nrows = f1 - f0;
-    const int CR = p.chunk_rows;
-    if (tid == 0) {
-        for (int q = 0; q * CR < nrows; ++q) {
-            const int q0 = q * CR, q1 = min(nrows, q0 + CR);
-            mbar_arrive_expect_tx(&bars[3 + q], (uint32_t)((q1 - q0) * (rb_gate + rb_up)));
-            for (int f = f0 + q0; f < f0 + q1;) {
-                const int a = f / I, r = f % I;
-                const int n = min(f0 + q1 - f, I - r);
-                const int64_t e = s_ids[s_act[a]] - L.expert_begin;
-                bulk_g2s(sm + p.o_rgate + (int64_t)(f - f0) * rb_gate, L.gate + e * st_gate + r * rb_gate,
-                         (uint32_t)(n * rb_gate), &bars[3 + q]);
-                bulk_g2s(sm + p.o_rup + (int64_t)(f - f0) * rb_up, L.up + e * st_up + r * rb_up,
-                         (uint32_t)(n * rb_up), &bars[3 + q]);
-                f += n;
+        // ---- phase-1 copies: routed gate/up rows of [f0, f1) in chunks of CR
+        // rows (one mbarrier each, issued in order so compute can start on the
+        // first chunk), then the routed down rows
+        const int nrows = f1 - f0;
+        const int CR = p.chunk_rows;
+        const int nchunks = (nrows + CR - 1) / CR;
+        if (tid == 0) {
+            const uint8_t* gate = Ls->gate;
+            const uint8_t* up = Ls->up;
+            const uint8_t* down = Ls->down;
+            for (int q = 0; q < nchunks; ++q) {
+                const int q0 = q * CR, q1 = min(nrows, q0 + CR);
+                mbar_arrive_expect_tx(&bars[3 + q], (uint32_t)((q1 - q0) * (rb_gate + rb_up)));
+                for (int f = f0 + q0; f < f0 + q1;) {
+                    const int a = f / I, r = f % I;
+                    const int n = min(f0 + q1 - f, I - r);
+                    const int64_t e = s_ids[s_act[a]] - ebeg;
+                    bulk_g2s(sm + p.o_rgate + (int64_t)(f - f0) * rb_gate, gate + e * st_gate + r * rb_gate,
+                             (uint32_t)(n * rb_gate), &bars[3 + q]);
+                    bulk_g2s(sm + p.o_rup + (int64_t)(f - f0) * rb_up, up + e * st_up + r * rb_up,
+                             (uint32_t)(n * rb_up), &bars[3 + q]);
+                    f += n;
+                }
+            }
+            mbar_arrive_expect_tx(&bars[2], (uint32_t)(A * nh * rb_down));
+            if (nh > 0) {
+                for (int a = 0; a < A; ++a) {
+                    const int64_t e = s_ids[s_act[a]] - ebeg;
+                    bulk_g2s(sm + p.o_rdown + (int64_t)a * p.max_out_rows * rb_down,
+                             down + e * st_down + h0 * rb_down, (uint32_t)(nh * rb_down), &bars[2]);
+                }
             }
         }
-        mbar_arrive_expect_tx(&bars[2], (uint32_t)(A * nh * rb_down));
-        if (nh > 0) {
-            for (int a = 0; a < A; ++a) {
-                const int64_t e = s_ids[s_act[a]] - L.expert_begin;
-                bulk_g2s(sm + p.o_rdown + (int64_t)a * p.max_out_rows * rb_down,
-                         L.down + e * st_down + h0 * rb_down, (uint32_t)(nh * rb_down), &bars[2]);
+
+        // ---- routed gate/up, chunk by chunk
+        {
+            const int rpw = 32 / lpr_h;
+            int waited = -1;
+            for (int rb = warp * rpw; rb < nrows; rb += nw * rpw) {
+                const int qlast = min(rb + rpw - 1, nrows - 1) / CR;
+                while (waited < qlast) {
+                    ++waited;
+                    if (!mbar_wait(&bars[3 + waited], (ph >> (3 + waited)) & 1u, kWaitPolls) && lane == 0)
+                        set_error(p.ctr, ST_TIMEOUT);
+                    if (waited < 2) TRACE(16 + waited);
+                }
+                const int rr = rb + sub_h;
+                const bool ok = rr < nrows;
+                const int rs = ok ? rr : 0;
+                float g = qdot_t<GU>(L0.gate_type, sm + p.o_rgate + rs * rb_gate, pr_h >> 2, pr_h & 3, xl);
+                float u = qdot_t<GU>(L0.up_type, sm + p.o_rup + rs * rb_up, pr_h >> 2, pr_h & 3, xl);
+                g = group_sum(g, lpr_h);
+                u = group_sum(u, lpr_h);
+                if (ok && pr_h == 0) {
+                    const float sgm = 1.0f / (1.0f + expf(-g));
+                    act_r[f0 + rr] = (g * sgm) * u;
+                }
+                if (rb == 0) TRACE(18);
+            }
+            // every chunk barrier must have completed before the CTA moves on
+            // (its copies write shared memory)
+            for (int q = waited + 1; q < nchunks; ++q)
+                if (!mbar_wait(&bars[3 + q], (ph >> (3 + q)) & 1u, kWaitPolls) && lane == 0)
+                    set_error(p.ctr, ST_TIMEOUT);
+            ph ^= ((1u << nchunks) - 1u) << 3;
+        }
+        TRACE(7);
+        __syncthreads();
+        TRACE(8);
+        if (tid == 0) {
+            red_release_add(p.ctr + C_GATEUP, 1);
+            if (Is && !wait_flag(p.ctr + C_SHARED, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+            if (!wait_flag(p.ctr + C_GATEUP, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+        }
+        __syncthreads();
+        TRACE(9);
+
+        // ---- activations of the A routed experts (+ shared), quantised
+        float* act32 = reinterpret_cast<float*>(sm + p.o_act);
+        for (int i = tid; i < (A * I) / 4; i += kFusedThreads) {
+            const int e = 4 * i;
+            *reinterpret_cast<float4*>(act32 + (e / I) * Imax + (e % I)) =
+                __ldcg(reinterpret_cast<const float4*>(act_r) + i);
+        }
+        if (Is) {
+            for (int i = tid; i < Is / 4; i += kFusedThreads)
+                *reinterpret_cast<float4*>(act32 + A * Imax + 4 * i) =
+                    __ldcg(reinterpret_cast<const float4*>(act_s) + i);
+            if (tid == 0) *s_sg = __ldcg(sgp);
+        }
+        __syncthreads();
+        TRACE(19);
+        const uint32_t qb = qvec_bytes(Imax);
+        {
+            const int bi = I / 256, bs = Is / 256;
+            for (int it = warp; it < A * bi + bs; it += nw) {
+                const int v = it < A * bi ? it / bi : A;
+                const int b = it < A * bi ? it % bi : it - A * bi;
+                const int n = v < A ? I : Is;
+                quantize_block_warp(act32 + v * Imax, qvec_at(sm + p.o_aq + v * qb, n), b);
             }
         }
-    }
+        __syncthreads();
+        TRACE(20);
+        if (tid == 0 && !mbar_wait(&bars[2], (ph >> 2) & 1u, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+        ph ^= 4u;
+        __syncthreads();
+        TRACE(10);
 
-    // ---- routed gate/up, chunk by chunk
-    {
-        const int rpw = 32 / lpr_h;
-        int waited = -1;
-        for (int rb = warp * rpw; rb < nrows; rb += nw * rpw) {
-            const int qlast = min(rb + rpw - 1, nrows - 1) / CR;
-            while (waited < qlast) {
-                ++waited;
-                if (!mbar_wait(&bars[3 + waited], 0, kWaitPolls) && lane == 0) set_error(p.ctr, ST_TIMEOUT);
-                if (waited < 2) TRACE(16 + waited);
-            }
-            const int rr = rb + sub_h;
-            const bool ok = rr < nrows;
-            const int rs = ok ? rr : 0;
-            float g = qdot_t<GU>(L.gate_type, sm + p.o_rgate + rs * rb_gate, pr_h >> 2, pr_h & 3, xl);
-            float u = qdot_t<GU>(L.up_type, sm + p.o_rup + rs * rb_up, pr_h >> 2, pr_h & 3, xl);
-            g = group_sum(g, lpr_h);
-            u = group_sum(u, lpr_h);
-            if (ok && pr_h == 0) {
-                const float sgm = 1.0f / (1.0f + expf(-g));
-                p.act_r[f0 + rr] = (g * sgm) * u;
-            }
-            if (rb == 0) TRACE(18);
-        }
-        // every chunk barrier must have completed before the CTA moves on
-        // (its copies write shared memory)
-        for (int q = waited + 1; q * CR < nrows; ++q)
-            if (!mbar_wait(&bars[3 + q], 0, kWaitPolls) && lane == 0) set_error(p.ctr, ST_TIMEOUT);
-    }
-    TRACE(7);
-    __syncthreads();
-    TRACE(8);
-    if (tid == 0) {
-        red_release_add(p.ctr + C_GATEUP, 1);
-        if (Is && !wait_flag(p.ctr + C_SHARED, (uint32_t)G, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
-        if (!wait_flag(p.ctr + C_GATEUP, (uint32_t)G, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
-    }
-    __syncthreads();
-    TRACE(9);
-
-    // ---- activations of the A routed experts (+ shared), quantised
-    const int nvec = A + (Is ? 1 : 0);
-    const int Imax = max(I, Is);
-    float* act32 = reinterpret_cast<float*>(sm + p.o_act);
-    for (int i = tid; i < (A * I) / 4; i += kFusedThreads) {
-        const int e = 4 * i;
-        *reinterpret_cast<float4*>(act32 + (e / I) * Imax + (e % I)) =
-            __ldcg(reinterpret_cast<const float4*>(p.act_r) + i);
-    }
-    if (Is) {
-        for (int i = tid; i < Is / 4; i += kFusedThreads)
-            *reinterpret_cast<float4*>(act32 + A * Imax + 4 * i) =
-                __ldcg(reinterpret_cast<const float4*>(p.act_s) + i);
-        if (tid == 0) *s_sg = __ldcg(p.sg);
-    }
-    __syncthreads();
-    TRACE(19);
-    const uint32_t qb = qvec_bytes(Imax);
-    {
-        const int bi = I / 256, bs = Is / 256;
-        for (int it = warp; it < A * bi + bs; it += nw) {
-            const int v = it < A * bi ? it / bi : A;
-            const int b = it < A * bi ? it % bi : it - A * bi;
-            const int n = v < A ? I : Is;
-            quantize_block_warp(act32 + v * Imax, qvec_at(sm + p.o_aq + v * qb, n), b);
-        }
-    }
-    __syncthreads();
-    TRACE(20);
-    if (!mbar_wait(&bars[2], 0, kWaitPolls) && tid == 0) set_error(p.ctr, ST_TIMEOUT);
-    __syncthreads();
-    TRACE(10);
-
-    // ---- down rows [h0, h1) of every vector: item = (vector, pair of row
-    // groups); the activation codes are loaded once per item
-    {
-        const int rpw_i = 32 / p.lpr_i, rpw_s = 32 / p.lpr_is;
-        const int ng_i = (nh + rpw_i - 1) / rpw_i, ng_s = Is ? (nh + rpw_s - 1) / rpw_s : 0;
-        const int np_i = (ng_i + 1) / 2, np_s = (ng_s + 1) / 2;
-        for (int it = warp; it < A * np_i + np_s; it += nw) {
-            const bool sh = it >= A * np_i;
-            const int v = sh ? A : it / np_i;
-            const int gp = sh ? it - A * np_i : it % np_i;
-            const int lpr = sh ? p.lpr_is : p.lpr_i;
-            const int ng = sh ? ng_s : ng_i;
-            const int rpw = 32 / lpr, sub = lane / lpr, pr = lane % lpr;
-            const int type = sh ? L.shared_down_type : L.down_type;
-            const int64_t rb = sh ? rb_sd : rb_down;
-            const uint8_t* rows = sh ? sm + p.o_sdown : sm + p.o_rdown + (int64_t)v * p.max_out_rows * rb_down;
-            const int n = sh ? Is : I;
-            XLane xa;
-            load_xlane(xa, qvec_at(sm + p.o_aq + v * qb, n), pr >> 2, pr & 3);
+        // ---- down rows [h0, h1) of every vector: item = (vector, pair of row
+        // groups); the activation codes are loaded once per item
+        {
+            const int rpw_i = 32 / p.lpr_i, rpw_s = 32 / p.lpr_is;
+            const int ng_i = (nh + rpw_i - 1) / rpw_i, ng_s = Is ? (nh + rpw_s - 1) / rpw_s : 0;
+            const int np_i = (ng_i + 1) / 2, np_s = (ng_s + 1) / 2;
+            for (int it = warp; it < A * np_i + np_s; it += nw) {
+                const bool sh = it >= A * np_i;
+                const int v = sh ? A : it / np_i;
+                const int gp = sh ? it - A * np_i : it % np_i;
+                const int lpr = sh ? p.lpr_is : p.lpr_i;
+                const int ng = sh ? ng_s : ng_i;
+                const int rpw = 32 / lpr, sub = lane / lpr, pr = lane % lpr;
+                const int type = sh ? L0.shared_down_type : L0.down_type;
+                const int64_t rb = sh ? rb_sd : rb_down;
+                const uint8_t* rows = sh ? sm + p.o_sdown : sm + p.o_rdown + (int64_t)v * p.max_out_rows * rb_down;
+                const int n = sh ? Is : I;
+                XLane xa;
+                load_xlane(xa, qvec_at(sm + p.o_aq + v * qb, n), pr >> 2, pr & 3);
 #pragma unroll
-            for (int gg = 0; gg < 2; ++gg) {
-                const int gi = 2 * gp + gg;
-                if (gi < ng) {
-                    const int rr = gi * rpw + sub;
-                    const bool ok = rr < nh;
-                    const uint8_t* rowp = rows + (ok ? rr : 0) * rb;
-                    float d = sh ? qdot_t<SDN>(type, rowp, pr >> 2, pr & 3, xa)
-                                 : qdot_t<DN>(type, rowp, pr >> 2, pr & 3, xa);
-                    d = group_sum(d, lpr);
-                    if (ok && pr == 0) s_vout[v * p.max_out_rows + rr] = d;
+                for (int gg = 0; gg < 2; ++gg) {
+                    const int gi = 2 * gp + gg;
+                    if (gi < ng) {
+                        const int rr = gi * rpw + sub;
+                        const bool ok = rr < nh;
+                        const uint8_t* rowp = rows + (ok ? rr : 0) * rb;
+                        float d = sh ? qdot_t<SDN>(type, rowp, pr >> 2, pr & 3, xa)
+                                     : qdot_t<DN>(type, rowp, pr >> 2, pr & 3, xa);
+                        d = group_sum(d, lpr);
+                        if (ok && pr == 0) s_vout[v * p.max_out_rows + rr] = d;
+                    }
+                }
+                if (it == 0) TRACE(21);
+                if (it == nw) TRACE(22);
+            }
+        }
+        __syncthreads();
+        TRACE(11);
+        // ---- weighted sum in top-k order, + shared (moe_layer.py:85-86, 102-105);
+        // block steps add the residual h to the binary16-rounded MoE output
+        // (transformer.py:192-204, 229-247)
+        for (int rr = tid; rr < nh; rr += kFusedThreads) {
+            float comb = 0.f;
+            int a = 0;
+            for (int k = 0; k < K; ++k) {
+                if (a < A && s_act[a] == k) {
+                    comb = __fadd_rn(comb, __fmul_rn(s_w[k], s_vout[a * p.max_out_rows + rr]));
+                    ++a;
                 }
             }
-            if (it == 0) TRACE(21);
-            if (it == nw) TRACE(22);
+            if (Is) comb = __fadd_rn(comb, __fmul_rn(*s_sg, s_vout[A * p.max_out_rows + rr]));
+            if (block) comb = __fadd_rn(h32[h0 + rr], round16(comb));
+            yout[h0 + rr] = comb;
         }
-    }
-    __syncthreads();
-    TRACE(11);
-    // ---- weighted sum in top-k order, + shared (moe_layer.py:85-86, 102-105)
-    for (int rr = tid; rr < nh; rr += kFusedThreads) {
-        float comb = 0.f;
-        int a = 0;
-        for (int k = 0; k < K; ++k) {
-            if (a < A && s_act[a] == k) {
-                comb = __fadd_rn(comb, __fmul_rn(s_w[k], s_vout[a * p.max_out_rows + rr]));
-                ++a;
-            }
+        __syncthreads();
+        TRACE(12);
+#undef TRACE
+        if (tid == 0) {
+            red_release_add(p.ctr + C_DONE, 1);
+            // the router and shared-expert regions are free: the next step's
+            // rows load while this CTA waits for the others
+            if (s + 1 < p.n_steps) issue_phase0(step_layer(s + 1));
         }
-        if (Is) comb = __fadd_rn(comb, __fmul_rn(*s_sg, s_vout[A * p.max_out_rows + rr]));
-        p.y[h0 + rr] = comb;
     }
     // ---- exit: the last CTA resets the counters for the next launch
-    __syncthreads();
-    TRACE(12);
-#undef TRACE
     if (tid == 0) {
         __threadfence();
         const uint32_t t = atomicAdd(p.ctr + C_EXIT, 1u);
@@ -442,6 +517,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             p.ctr[C_ROUTER] = 0;
             p.ctr[C_SHARED] = 0;
             p.ctr[C_GATEUP] = 0;
+            p.ctr[C_DONE] = 0;
             p.ctr[C_EXIT] = 0;
             __threadfence();
         }
@@ -480,8 +556,10 @@ bool fused_supported(const moe_b200_layer* L, int T, int flags) {
 
 size_t fused_workspace_bytes(const moe_b200_layer* L) {
     const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate : L->intermediate;
-    return 256 + align_up((size_t)L->n_experts * 4) + align_up((size_t)L->top_k * L->intermediate * 4) +
-           align_up((size_t)Imax * 4) + 256;
+    // counters, then two buffers (step parity) of scores, routed and shared
+    // activations and the shared gate
+    return 256 + align_up((size_t)2 * L->n_experts * 4) +
+           align_up((size_t)2 * L->top_k * L->intermediate * 4) + align_up((size_t)2 * Imax * 4) + 256;
 }
 
 static bool fused_plan(const moe_b200_layer* L, bool shared, int G, FusedParams& p) {
@@ -506,6 +584,7 @@ static bool fused_plan(const moe_b200_layer* L, bool shared, int G, FusedParams&
         return at;
     };
     p.o_x32 = take((uint64_t)H * 4);
+    p.o_h32 = take((uint64_t)H * 4);
     p.o_xq = take(qvec_bytes(H));
     p.o_router = take((uint64_t)p.max_router_rows * H * 4);
     p.o_sgate = take(Is ? (uint64_t)p.max_sgu_rows * row_bytes(L->shared_gate_type, H) : 0);
@@ -534,9 +613,12 @@ uint64_t* trace_buffer(int* capacity_ctas) {
     return tl_trace;
 }
 
-cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float* x, float* y,
-                                int32_t* ids_out, float* w_out, void* ws, cudaStream_t stream,
-                                bool* launched) {
+// One cooperative launch of the fused kernel: a single step (steps null:
+// the token x through layer *L) or n_steps steps from the device tables.
+static cudaError_t fused_launch(const moe_b200_layer* L, int flags, const float* x, float* y,
+                                int32_t* ids_out, float* w_out, const moe_b200_layer* layers,
+                                const moe_b200_step* steps, int n_steps, float eps, void* ws,
+                                cudaStream_t stream, bool* launched) {
     *launched = false;
     const bool shared = L->shared_intermediate > 0 && !(flags & MOE_B200_NO_SHARED);
     FusedParams p{};
@@ -582,19 +664,21 @@ cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float*
     p.y = y;
     p.ids_out = ids_out;
     p.w_out = w_out;
+    p.layers = layers;
+    p.steps = steps;
+    p.n_steps = steps ? n_steps : 1;
+    p.eps = eps;
     p.ctr = reinterpret_cast<uint32_t*>(base);
+    const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate : L->intermediate;
     size_t off = 256;
     p.scores = reinterpret_cast<float*>(base + off);
-    off += align_up((size_t)L->n_experts * 4);
+    off += align_up((size_t)2 * L->n_experts * 4);
     p.act_r = reinterpret_cast<float*>(base + off);
-    off += align_up((size_t)L->top_k * L->intermediate * 4);
+    off += align_up((size_t)2 * L->top_k * L->intermediate * 4);
     p.act_s = reinterpret_cast<float*>(base + off);
-    const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate : L->intermediate;
-    off += align_up((size_t)Imax * 4);
+    off += align_up((size_t)2 * Imax * 4);
     p.sg = reinterpret_cast<float*>(base + off);
     p.trace = (tl_trace && tl_trace_cap >= G) ? tl_trace : nullptr;
-    static const bool no_warm = getenv("MOE_B200_NO_WARM") != nullptr;
-    p.warm = no_warm ? 0 : 1;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
@@ -609,6 +693,20 @@ cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float*
     cudaError_t e = cudaLaunchKernelEx(&cfg, kInstances[pick].fn, p);
     if (e == cudaSuccess) *launched = true;
     return e;
+}
+
+cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float* x, float* y,
+                                int32_t* ids_out, float* w_out, void* ws, cudaStream_t stream,
+                                bool* launched) {
+    return fused_launch(L, flags, x, y, ids_out, w_out, nullptr, nullptr, 1, 0.f, ws, stream,
+                        launched);
+}
+
+cudaError_t launch_decode_steps(const moe_b200_layer* L0, const moe_b200_layer* layers,
+                                const moe_b200_step* steps, int n_steps, float eps, void* ws,
+                                cudaStream_t stream, bool* launched) {
+    return fused_launch(L0, L0->flags, nullptr, nullptr, nullptr, nullptr, layers, steps, n_steps,
+                        eps, ws, stream, launched);
 }
 
 }  // namespace moeb200

@@ -63,6 +63,11 @@ size_t fused_workspace_bytes(const moe_b200_layer* L);
 cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float* x, float* y,
                                 int32_t* ids_out, float* w_out, void* ws, cudaStream_t stream,
                                 bool* launched);
+// n_steps single-token steps from device tables in one launch (every layer
+// shares L0's shapes and block formats; L0's flags apply to all).
+cudaError_t launch_decode_steps(const moe_b200_layer* L0, const moe_b200_layer* layers,
+                                const moe_b200_step* steps, int n_steps, float eps, void* ws,
+                                cudaStream_t stream, bool* launched);
 void set_fused_trace(void* buf, int capacity_ctas);
 uint64_t* trace_buffer(int* capacity_ctas);  // the buffer set above (this thread)
 

@@ -27,6 +27,8 @@ FP16_GRAPH = 1
 NO_SHARED = 2
 EXACT = 4
 SHARED_ONLY = 8
+STEP_CHAIN = 1
+STEP_BLOCK = 2
 
 
 class Layer(C.Structure):
@@ -45,6 +47,15 @@ class Layer(C.Structure):
     ]
 
 
+class Step(C.Structure):
+    """Mirror of ``struct moe_b200_step``."""
+
+    _fields_ = [
+        ("layer", C.c_int32), ("flags", C.c_int32), ("x", C.c_void_p), ("y", C.c_void_p),
+        ("topk_ids", C.c_void_p), ("topk_weights", C.c_void_p),
+    ]
+
+
 def _bind(lib: C.CDLL) -> None:
     i, i64, vp, f = C.c_int, C.c_int64, C.c_void_p, C.c_float
     sigs = {
@@ -58,6 +69,8 @@ def _bind(lib: C.CDLL) -> None:
         "moe_b200_prefill": (i, [C.POINTER(Layer), vp, C.c_int32, C.c_int32, vp, vp, vp, vp,
                                  C.c_size_t, vp]),
         "moe_b200_prefill_workspace": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_size_t)]),
+        "moe_b200_decode_steps": (i, [C.POINTER(Layer), vp, vp, C.c_int32, C.c_float, vp,
+                                      C.c_size_t, vp]),
         "moe_b200_prefill_supported": (i, [C.POINTER(Layer)]),
         "moe_b200_prefill_kernels": (i, [C.POINTER(Layer), C.POINTER(C.c_int)]),
         "moe_b200_dequant": (i, [i, vp, vp, i64, i, vp]),

@@ -191,6 +191,61 @@ class B200ExpertBackend:
             ws.data_ptr(), ws.numel(), stream.cuda_stream)
         _lib.check(st, "moe_b200_decode")
 
+    # ---------------------------------------------------- multi-step decode
+
+    def layer_table(self, layers) -> torch.Tensor:
+        """Device copy of the ``moe_b200_layer`` structs of `layers` (cached
+        per tuple of layer ids and flags)."""
+        key = (tuple(layers), self.flags)
+        cache = getattr(self, "_layer_tables", None)
+        if cache is None:
+            cache = self._layer_tables = {}
+        t = cache.get(key)
+        if t is None:
+            raw = b"".join(bytes(self.store.layer(l).with_flags(self.flags)) for l in layers)
+            t = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.device)
+            cache[key] = t
+        return t
+
+    def step_table(self, steps) -> torch.Tensor:
+        """Device array of ``moe_b200_step`` for `steps`, a list of
+        (table index, flags, x, y, topk_ids, topk_weights) with device
+        tensors (or None)."""
+        arr = (_lib.Step * len(steps))()
+        ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+        for i, (li, fl, x, y, ids, w) in enumerate(steps):
+            arr[i] = _lib.Step(li, fl, ptr(x), ptr(y), ptr(ids), ptr(w))
+        return torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(self.device)
+
+    def decode_steps_device(self, layer_table: torch.Tensor, step_table: torch.Tensor,
+                            n_steps: int, layer0: int, eps: float = 1e-6, stream=None) -> None:
+        """All steps of the tables in one launch (``moe_b200_decode_steps``)."""
+        dl = self.store.layer(layer0)
+        s = dl.with_flags(self.flags)
+        ws = self._workspace(dl, 1)
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        st = self.lib.moe_b200_decode_steps(C.byref(s), layer_table.data_ptr(),
+                                            step_table.data_ptr(), n_steps, eps, ws.data_ptr(),
+                                            ws.numel(), stream.cuda_stream)
+        _lib.check(st, "moe_b200_decode_steps")
+
+    def decode_stack(self, layers, x: torch.Tensor, y: torch.Tensor, eps: float = 1e-6) -> None:
+        """One token through a stack of blocks with identity mixers (the
+        40-layer configuration): h = x + rmsnorm16(x); out = h +
+        f16(MoE(rmsnorm16(h))), layer after layer, in one launch."""
+        H = x.shape[-1]
+        tmp = torch.empty((2, H), dtype=torch.float32, device=self.device)
+        steps = []
+        for i, _ in enumerate(layers):
+            out = y.view(-1) if i == len(layers) - 1 else tmp[i % 2]
+            fl = _lib.STEP_BLOCK | (_lib.STEP_CHAIN if i else 0)
+            steps.append((i, fl, x.view(-1) if i == 0 else None, out, None, None))
+        lt = self.layer_table(layers)
+        stt = self.step_table(steps)
+        self.decode_steps_device(lt, stt, len(steps), layers[0], eps)
+        self._keep = (tmp, stt)  # alive until the stream has run the launch
+
     def forward_layer(self, layer: int, activations, return_routing: bool = False):
         """Whole MoE layer for T tokens (host arrays in, host array out)."""
         x = np.ascontiguousarray(activations, dtype=np.float32)

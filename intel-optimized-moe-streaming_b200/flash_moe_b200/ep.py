@@ -121,6 +121,23 @@ class DecodeRunner:
                                                         flags=self._flags(_lib.SHARED_ONLY)),
             self.x_all, self.y_part, self.y_routed, self.y_sh, y)
 
+    def step_tables(self, steps: int):
+        """(layer table, step table) running `steps` consecutive steps in one
+        launch (single GPU): step i decodes token i % n through layer i % L."""
+        if self.world > 1:
+            raise ValueError("multi-step launches run on one GPU")
+        n = self.tokens.shape[0]
+        rows = []
+        for i in range(steps):
+            slot = i % self.max_steps
+            rows.append((i % len(self.layers), 0, self.tokens[i % n], self.y.view(-1),
+                         self.ids[slot], None))
+        self.recorded = max(self.recorded, min(steps, self.max_steps))
+        return self.be.layer_table(self.layers), self.be.step_table(rows)
+
+    def run_tables(self, tables, steps: int) -> None:
+        self.be.decode_steps_device(tables[0], tables[1], steps, self.layers[0])
+
     def capture(self, steps: int):
         """CUDA graph of `steps` consecutive steps (single GPU only)."""
         if self.world > 1:

@@ -1,0 +1,118 @@
+"""Many decode steps in one launch (moe_b200_decode_steps through the C ABI).
+
+Independent steps must give exactly the outputs of one moe_b200_decode call
+per step (same kernel arithmetic).  Chained transformer-block steps (the
+40-layer stack configuration: h = x + rmsnorm16(x), y = h +
+f16(MoE(rmsnorm16(h)))) are checked layer by layer against the oracle's
+stack_block, fed with the device's own input to that layer."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from cases import oracle_layer
+from flash_moe_b200 import synth
+from flash_moe_b200.formats import Q4_K, Q8_0
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+TIE = 1e-5
+
+SPEC = dict(hidden=1024, inter=256, n_experts=16, top_k=6, gate_type=Q4_K, up_type=Q4_K,
+            down_type=Q8_0, shared_inter=512)
+
+
+def _arena(n_layers, seed0=70, **extra):
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    arena = ExpertArena()
+    lws = []
+    for l in range(n_layers):
+        lw = synth.make_layer(seed=seed0 + l, **dict(SPEC, **extra))
+        arena.add_layer(l, lw)
+        lws.append(lw)
+    return B200ExpertBackend(arena), lws
+
+
+def test_independent_steps_equal_single_calls():
+    import torch
+    from flash_moe_b200 import _lib
+    be, lws = _arena(3)
+    H, K = lws[0].hidden, lws[0].top_k
+    n = 7
+    xs = torch.from_numpy(synth.make_tokens(71, n, H)).to(be.device)
+    ys = torch.empty((n, H), dtype=torch.float32, device=be.device)
+    ids = torch.empty((n, K), dtype=torch.int32, device=be.device)
+    ws = torch.empty((n, K), dtype=torch.float32, device=be.device)
+    rows = [(i % 3, 0, xs[i], ys[i], ids[i], ws[i]) for i in range(n)]
+    be.decode_steps_device(be.layer_table([0, 1, 2]), be.step_table(rows), n, 0)
+    torch.cuda.synchronize()
+    for i in range(n):
+        y1 = torch.empty((1, H), dtype=torch.float32, device=be.device)
+        i1 = torch.empty((1, K), dtype=torch.int32, device=be.device)
+        be.forward_layer_device(i % 3, xs[i:i + 1], y1, i1)
+        torch.cuda.synchronize()
+        assert torch.equal(ids[i], i1[0]), i
+        assert torch.equal(ys[i], y1[0]), i
+    assert be.device_errors() == 0
+
+
+def _check_block(oracle, lw, x, y_dev, ids_dev, w_dev):
+    """One block against the oracle; a near tie resolved differently by the
+    device is re-routed with the device's selection."""
+    h = x + O.rmsnorm_f16(x).astype(np.float32)
+    n2 = O.rmsnorm_f16(h).astype(np.float32)
+    want_moe, want_ids, _ = oracle_layer(oracle, lw, n2[None])
+    if not np.array_equal(ids_dev, want_ids[0]):
+        s = np.sort(O.route(n2, lw.gate_he(), lw.top_k, lw.router_bias)[2])[::-1]
+        k = lw.top_k
+        assert abs(s[k - 1] - s[k]) <= TIE * max(abs(s[k - 1]), 1e-30), (ids_dev, want_ids[0])
+        sel = [(list(map(int, ids_dev)), [float(v) for v in w_dev])]
+        want_moe, _, _ = oracle_layer(oracle, lw, n2[None], selections=sel)
+    want = h + want_moe[0].astype(np.float16).astype(np.float32)
+    err = O.max_relative_error(y_dev, want)
+    assert err <= TOL, err
+
+
+@pytest.mark.parametrize("n_layers", [1, 4])
+def test_block_chain_matches_oracle_layer_by_layer(oracle, n_layers):
+    import torch
+    from flash_moe_b200 import _lib
+    be, lws = _arena(n_layers)
+    H, K = lws[0].hidden, lws[0].top_k
+    x0 = torch.from_numpy(synth.make_tokens(72, 1, H)).to(be.device)
+    ys = torch.empty((n_layers, H), dtype=torch.float32, device=be.device)
+    ids = torch.empty((n_layers, K), dtype=torch.int32, device=be.device)
+    ws = torch.empty((n_layers, K), dtype=torch.float32, device=be.device)
+    rows = []
+    for l in range(n_layers):
+        fl = _lib.STEP_BLOCK | (_lib.STEP_CHAIN if l else 0)
+        rows.append((l, fl, x0[0] if l == 0 else None, ys[l], ids[l], ws[l]))
+    be.decode_steps_device(be.layer_table(list(range(n_layers))), be.step_table(rows), n_layers, 0)
+    torch.cuda.synchronize()
+    assert be.device_errors() == 0
+    yh, ih, wh = ys.cpu().numpy(), ids.cpu().numpy(), ws.cpu().numpy()
+    x = x0[0].cpu().numpy()
+    for l in range(n_layers):
+        _check_block(oracle, lws[l], x, yh[l], ih[l], wh[l])
+        x = yh[l]
+
+
+def test_decode_stack_api_matches_step_tables():
+    """backend.decode_stack (ping-pong buffers) equals the same chain with
+    one output buffer per layer."""
+    import torch
+    from flash_moe_b200 import _lib
+    be, lws = _arena(3, seed0=90)
+    H = lws[0].hidden
+    x0 = torch.from_numpy(synth.make_tokens(73, 1, H)).to(be.device)
+    y = torch.empty((1, H), dtype=torch.float32, device=be.device)
+    be.decode_stack([0, 1, 2], x0, y)
+    ys = torch.empty((3, H), dtype=torch.float32, device=be.device)
+    rows = [(l, _lib.STEP_BLOCK | (_lib.STEP_CHAIN if l else 0), x0[0] if l == 0 else None, ys[l],
+             None, None) for l in range(3)]
+    be.decode_steps_device(be.layer_table([0, 1, 2]), be.step_table(rows), 3, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(y[0], ys[2])
+    assert be.device_errors() == 0
