@@ -21,8 +21,9 @@ its sources into oracle/_ref) for the 8 routed experts on a thread pool, and
 the numpy router / combine / shared expert of its Python layer.
 
 At N = 1 the line also carries "prefill" (config 4: 4096 bf16 tokens on the
-tensor cores, TFLOP/s against the measured bf16 peak) and "batched_decode"
-(config 3: 64 tokens with a Zipf(1.1) router bias).
+tensor cores, TFLOP/s against the measured bf16 peak), "batched_decode"
+(config 3: 64 tokens with a Zipf(1.1) router bias) and "stack" (config 5:
+40 identity-mixer blocks, batch 1 in one launch and batch 32).
 
 Prints one JSON line (rank 0).
 """
@@ -288,6 +289,52 @@ def bench_batched(dev, peaks: dict, peak_kind: str) -> dict:
     return out
 
 
+def bench_stack(backend, base_layer: int, dev, peaks: dict, peak_kind: str) -> dict:
+    """Config 5: 40 identity-mixer blocks (RMSNorm f16 + residual around each
+    MoE layer), 40 distinct resident layers (15.3 GB of packed weights), batch
+    1 (one launch of 40 chained block steps) and batch 32 (block kernels
+    around the tensor-core path per layer)."""
+    import torch
+    from flash_moe_b200 import synth
+    arena = backend.store
+    base = arena.layer(base_layer)
+    ids = []
+    for l in range(40):
+        lid = 1000 + l
+        arena.add_device_layer(lid, base.reshuffled(5000 + l) if l else base)
+        ids.append(lid)
+    H = base.weights.hidden
+    x1 = torch.from_numpy(synth.make_tokens(7000, 1, H)).to(dev)
+    y1 = torch.empty_like(x1)
+    lt = backend.layer_table(ids)
+    tmp = torch.empty((2, H), dtype=torch.float32, device=dev)
+    rows = [(i, 2 | (1 if i else 0), x1[0] if i == 0 else None,
+             y1[0] if i == 39 else tmp[i % 2], None, None) for i in range(40)]
+    st = backend.step_table(rows)
+    ms1 = _time_calls(lambda: backend.decode_steps_device(lt, st, 40, ids[0]), 10)
+    x32 = torch.from_numpy(synth.make_tokens(7001, 32, H)).to(dev)
+    y32 = torch.empty_like(x32)
+    ms32 = _time_calls(lambda: backend.decode_stack_batch(ids, x32, y32), 3, warmup=1)
+    err = backend.device_errors() or backend.prefill_errors()
+    per_tok_bytes = 40 * step_bytes(8)
+    gbs = per_tok_bytes / (ms1 / 1e3) / 1e9
+    for lid in ids:
+        arena.drop_layer(lid)
+    return {"config": "config 5: 40 blocks (identity mixer + RMSNorm f16 eps 1e-6 + residual), "
+                      "40 distinct resident layers (layer 0 seeded, 1..39 seeded row permutations "
+                      "with their own routers), 1 GPU",
+            "batch1_us_per_token": round(ms1 * 1e3, 1),
+            "batch1_us_per_layer": round(ms1 * 1e3 / 40, 2),
+            "batch1_roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                                "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                                "algorithmic_bytes_per_token": per_tok_bytes,
+                                "peak_source": f"{peak_kind} hbm_gbs"},
+            "batch1_launches": 1,
+            "batch32_ms_per_step": round(ms32, 3),
+            "batch32_tokens_per_s": round(32 / (ms32 / 1e3)),
+            "device_error": err}
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -405,6 +452,7 @@ def run_gpu(args) -> None:
     if rank == 0 and world == 1 and not args.no_extra:
         extra["prefill"] = bench_prefill(backend, 0, dev, peaks, peak_kind)
         extra["batched_decode"] = bench_batched(dev, peaks, peak_kind)
+        extra["stack"] = bench_stack(backend, 0, dev, peaks, peak_kind)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": UNIT, "n_gpus": world,

@@ -232,6 +232,18 @@ MOE_B200_API int moe_b200_decode_steps(const moe_b200_layer* layer0,
                                        float eps, void* workspace, size_t workspace_bytes,
                                        void* stream);
 
+/* The transformer block with an identity mixer around a many-token MoE
+ * call, for T tokens of H values (device fp32, row-major):
+ *   moe_b200_block_prepare: h = x + f16(rmsnorm(x)), n = f16(rmsnorm(h))
+ *   moe_b200_block_finish:  y = h + f16(m), m the MoE output of n
+ * RMSNorm with weight 1: v / sqrt(mean(v^2) + eps) (src/flash_moe/norm.py:21-30;
+ * the block, src/flash_moe/transformer.py:229-247).  Single-token stacks run
+ * the same block inside moe_b200_decode_steps (MOE_B200_STEP_BLOCK). */
+MOE_B200_API int moe_b200_block_prepare(const float* x, float* h, float* n, int32_t tokens,
+                                        int32_t hidden, float eps, void* stream);
+MOE_B200_API int moe_b200_block_finish(const float* h, const float* m, float* y, int32_t tokens,
+                                       int32_t hidden, void* stream);
+
 /* Largest `intermediate` moe_b200_expert_noalloc accepts. */
 #define MOE_B200_NOALLOC_MAX_INTERMEDIATE 16384
 

@@ -422,6 +422,20 @@ int moe_b200_decode(const moe_b200_layer* L, const float* x, int32_t T, float* y
     return ST_OK;
 }
 
+int moe_b200_block_prepare(const float* x, float* h, float* n, int32_t T, int32_t H, float eps,
+                           void* stream) {
+    if (!x || !h || !n || T < 1 || H < 1 || !(eps >= 0.f)) return ST_ARG;
+    cudaError_t e = launch_block_prepare(x, h, n, T, H, eps, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ST_OK : fail(e, ST_CUDA);
+}
+
+int moe_b200_block_finish(const float* h, const float* m, float* y, int32_t T, int32_t H,
+                          void* stream) {
+    if (!h || !m || !y || T < 1 || H < 1) return ST_ARG;
+    cudaError_t e = launch_block_finish(h, m, y, T, H, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ST_OK : fail(e, ST_CUDA);
+}
+
 int moe_b200_decode_steps(const moe_b200_layer* L0, const moe_b200_layer* layers,
                           const moe_b200_step* steps, int32_t n_steps, float eps, void* workspace,
                           size_t workspace_bytes, void* stream) {

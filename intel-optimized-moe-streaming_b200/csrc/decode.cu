@@ -56,7 +56,7 @@ struct FusedParams {
     float* act_r;            // [2][K x I]
     float* act_s;            // [2][Imax]
     float* sg;               // [2]
-    uint64_t* trace;         // [G x 32] phase timestamps of the first step (ns), or null
+    uint64_t* trace;         // [G x 32] phase timestamps of step n_steps / 2 (ns), or null
     int G;
     int with_shared;
     int max_router_rows, max_sgu_rows, max_out_rows, max_rgu_rows;
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     uint32_t ph = 0;  // parity of the phase each mbarrier is in
 
     for (int s = 0; s < p.n_steps; ++s) {
-        uint64_t* trace = (p.trace && s == 0) ? p.trace + (size_t)c * kTraceSlots : nullptr;
+        uint64_t* trace = (p.trace && s == p.n_steps / 2) ? p.trace + (size_t)c * kTraceSlots : nullptr;
 #define TRACE(i) do { if (trace && tid == 0) trace[i] = global_ns(); } while (0)
         TRACE(0);
         const moe_b200_layer* Ls = step_layer(s);

@@ -80,4 +80,10 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
                 cudaError_t* ce);
 int prefill_kernels(const moe_b200_layer* L);
 
+// Identity-mixer transformer block around a many-token MoE call (block.cu).
+cudaError_t launch_block_prepare(const float* x, float* h, float* n, int T, int H, float eps,
+                                 cudaStream_t s);
+cudaError_t launch_block_finish(const float* h, const float* m, float* y, int T, int H,
+                                cudaStream_t s);
+
 }  // namespace moeb200

@@ -376,10 +376,9 @@ __device__ __forceinline__ PfUnit pf_unit(const PfParams& p, const PfShared& sh,
 // chunks 4h..4h+3 of it per stage; its raw block row starts `rofs` bytes
 // into the raw slot.
 
-template <int T>
+template <int T, int S>
 __device__ __forceinline__ void dq_store(uint8_t* a, int trow, int h,
-                                         const uint32_t (&w)[PfNW<T>::n], auto s_c) {
-    constexpr int S = decltype(s_c)::value;
+                                         const uint32_t (&w)[PfNW<T>::n]) {
     if (h == 0) {
         *reinterpret_cast<uint4*>(a + sw128_offset(trow, 0)) = dq_chunk<T, S, 0>(w);
         *reinterpret_cast<uint4*>(a + sw128_offset(trow, 1)) = dq_chunk<T, S, 1>(w);
@@ -440,7 +439,7 @@ __device__ __forceinline__ bool dq_unit(const PfParams& p, const PfUnit& un, uin
         auto stage = [&](auto s_c) -> bool {
             const uint32_t st = it_s % p.stages, ph = (it_s / p.stages) & 1u;
             if (!pf_wait_t(&empty[st], ph ^ 1u, abort, p.err, t_empty)) return false;
-            dq_store<T>(smem + (size_t)st * p.stage_bytes, trow, h, w, s_c);
+            dq_store<T, decltype(s_c)::value>(smem + (size_t)st * p.stage_bytes, trow, h, w);
             fence_async_smem();
             __syncwarp();
             if ((threadIdx.x & 31) == 0) mbar_arrive(&full[st]);

@@ -246,6 +246,30 @@ class B200ExpertBackend:
         self.decode_steps_device(lt, stt, len(steps), layers[0], eps)
         self._keep = (tmp, stt)  # alive until the stream has run the launch
 
+    def decode_stack_batch(self, layers, x: torch.Tensor, y: torch.Tensor, eps: float = 1e-6,
+                           prefill: bool = True) -> None:
+        """T tokens through the identity-mixer block stack: per layer
+        moe_b200_block_prepare, the MoE layer (tensor-core prefill path, or
+        the decode engines), moe_b200_block_finish."""
+        T, H = x.shape
+        dev = self.device
+        h = torch.empty((T, H), dtype=torch.float32, device=dev)
+        n = torch.empty_like(h)
+        m = torch.empty_like(h)
+        scratch = torch.empty_like(h)  # layer outputs between layers
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        for i, layer in enumerate(layers):
+            src = x if i == 0 else scratch
+            dst = y if i == len(layers) - 1 else scratch
+            _lib.check(self.lib.moe_b200_block_prepare(src.data_ptr(), h.data_ptr(), n.data_ptr(),
+                                                       T, H, eps, stream), "moe_b200_block_prepare")
+            if prefill:
+                self.prefill_device(layer, n, m)
+            else:
+                self.forward_layer_device(layer, n, m)
+            _lib.check(self.lib.moe_b200_block_finish(h.data_ptr(), m.data_ptr(), dst.data_ptr(),
+                                                      T, H, stream), "moe_b200_block_finish")
+
     def forward_layer(self, layer: int, activations, return_routing: bool = False):
         """Whole MoE layer for T tokens (host arrays in, host array out)."""
         x = np.ascontiguousarray(activations, dtype=np.float32)

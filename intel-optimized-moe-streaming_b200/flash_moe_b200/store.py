@@ -97,6 +97,42 @@ class DeviceLayer:
         other.struct = other._make_struct(self.struct.flags)
         return other
 
+    def reshuffled(self, seed: int) -> "DeviceLayer":
+        """Another layer of the same construction, made on the device: the
+        rows of every packed tensor permuted by a seeded permutation (each row
+        keeps its blocks, so every block keeps its drawn scales and quants)
+        and a fresh N(0, 0.02) router and shared-gate vector.  Used to fill a
+        deep stack of distinct resident layers without generating gigabytes
+        on the host; the values are not those of synth.make_layer(seed)."""
+        lw = self.weights
+        g = torch.Generator(device=self.device)
+        g.manual_seed(int(seed))
+
+        def rows(t: torch.Tensor, row_bytes: int) -> torch.Tensor:
+            r = t.view(-1, row_bytes)
+            return r[torch.randperm(r.shape[0], generator=g, device=self.device)].reshape(-1)
+
+        other = object.__new__(DeviceLayer)
+        other.weights = lw
+        other.device = self.device
+        other.expert_begin, other.expert_count = self.expert_begin, self.expert_count
+        other.gate = rows(self.gate, lw.gate_stride // lw.inter)
+        other.up = rows(self.up, lw.up_stride // lw.inter)
+        other.down = rows(self.down, lw.down_stride // lw.hidden)
+        other.router = torch.randn(self.router.shape, generator=g, device=self.device) * 0.02
+        other.router_bias = self.router_bias.clone() if self.router_bias is not None else None
+        other.shared = None
+        if self.shared is not None:
+            sh = self.shared
+            other.shared = {
+                "gate": rows(sh["gate"], sh["gate"].numel() // lw.shared_inter),
+                "up": rows(sh["up"], sh["up"].numel() // lw.shared_inter),
+                "down": rows(sh["down"], sh["down"].numel() // lw.hidden),
+                "gate_inp": torch.randn(sh["gate_inp"].shape, generator=g, device=self.device) * 0.02,
+            }
+        other.struct = other._make_struct(self.struct.flags)
+        return other
+
     def with_flags(self, flags: int) -> _lib.Layer:
         s = _lib.Layer.from_buffer_copy(self.struct)
         s.flags = flags
@@ -162,6 +198,13 @@ class ExpertArena:
         self.stats.resident_bytes += dl.resident_bytes
         self.stats.layers += 1
         return dl
+
+    def drop_layer(self, index: int) -> None:
+        """Release a resident layer (its device memory returns to the pool)."""
+        old = self.layers.pop(index, None)
+        if old is not None:
+            self.stats.resident_bytes -= old.resident_bytes
+            self.stats.layers -= 1
 
     def layer(self, index: int) -> DeviceLayer:
         try:
