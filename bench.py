@@ -335,6 +335,20 @@ def bench_stack(backend, base_layer: int, dev, peaks: dict, peak_kind: str) -> d
             "device_error": err}
 
 
+def run_prefill_only(args) -> None:
+    """The config-4 prefill measurement alone (one GPU), for profiling."""
+    import torch
+    from flash_moe_b200 import synth
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    dev = torch.device("cuda", 0)
+    arena = ExpertArena(dev)
+    arena.add_layer(0, synth.make_layer(seed=0))
+    backend = B200ExpertBackend(arena)
+    peaks, peak_kind = measured_peaks()
+    print(json.dumps({"prefill": bench_prefill(backend, 0, dev, peaks, peak_kind)}), flush=True)
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -498,6 +512,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak", type=float, default=0.5)
+    ap.add_argument("--only", choices=["prefill"], default=None,
+                    help="run only the config-4 prefill measurement (for profiling)")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the prefill and batched-decode measurements (N = 1)")
     args = ap.parse_args()
@@ -505,6 +521,8 @@ def main() -> None:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.only == "prefill":
+        run_prefill_only(args)
     else:
         run_gpu(args)
 
