@@ -38,6 +38,7 @@ constexpr int kFusedThreads = 512;
 constexpr uint32_t kWaitPolls = 1u << 21;
 constexpr int kTraceSlots = 32;
 constexpr int kMaxChunks = 8;  // routed gate/up copy chunks (mbarriers 3..10)
+constexpr int kXBar = 3 + kMaxChunks;  // mbarrier of the prefetched token
 
 enum { C_ROUTER = 0, C_SHARED = 1, C_GATEUP = 2, C_EXIT = 3, C_DONE = 4, C_ERROR = 8 };
 
@@ -120,7 +121,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     const int64_t rb_sd = Is ? row_bytes(L0.shared_down_type, Is) : 0;
     const int Imax = max(I, Is);
 
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + p.o_misc);       // [3 + kMaxChunks]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + p.o_misc);       // [kXBar + 1]
     int* s_ids = reinterpret_cast<int*>(sm + p.o_misc + 128);          // [16]
     float* s_w = reinterpret_cast<float*>(sm + p.o_misc + 192);        // [16]
     int* s_act = reinterpret_cast<int*>(sm + p.o_misc + 256);          // [16] active slots
@@ -163,12 +164,27 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         }
     };
 
+    // A step's token comes by TMA (issued before the step begins) unless it
+    // is the previous step's output or not 16-byte aligned.
+    auto step_x = [&](int s) -> const float* { return p.steps ? p.steps[s].x : p.x; };
+    auto x_by_copy = [&](int s) -> bool {
+        const bool chain = p.steps && (p.steps[s].flags & MOE_B200_STEP_CHAIN) && s > 0;
+        return !chain && (((uintptr_t)step_x(s)) & 15u) == 0;
+    };
+    auto issue_x = [&](int s) {
+        mbar_arrive_expect_tx(&bars[kXBar], (uint32_t)(H * 4));
+        bulk_g2s(x32, step_x(s), (uint32_t)(H * 4), &bars[kXBar]);
+    };
+
     if (tid == 0) {
-        for (int i = 0; i < 3 + kMaxChunks; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i <= kXBar; ++i) mbar_init(&bars[i], 1);
         mbar_fence_init();
     }
     __syncthreads();
-    if (tid == 0) issue_phase0(step_layer(0));
+    if (tid == 0) {
+        issue_phase0(step_layer(0));
+        if (x_by_copy(0)) issue_x(0);
+    }
     uint32_t ph = 0;  // parity of the phase each mbarrier is in
 
     for (int s = 0; s < p.n_steps; ++s) {
@@ -204,6 +220,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                 set_error(p.ctr, ST_TIMEOUT);
             __syncthreads();
             for (int i = tid; i < H; i += kFusedThreads) x32[i] = __ldcg(xin + i);
+        } else if (x_by_copy(s)) {
+            if (tid == 0 && !mbar_wait(&bars[kXBar], (ph >> kXBar) & 1u, kWaitPolls))
+                set_error(p.ctr, ST_TIMEOUT);
+            ph ^= 1u << kXBar;
         } else {
             for (int i = tid; i < H; i += kFusedThreads) x32[i] = xin[i];
         }
@@ -282,27 +302,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         XLane xl;
         load_xlane(xl, xq, pr_h >> 2, pr_h & 3);
 
-        // ---- shared expert gate/up (x is the token)
-        if (Is) {
-            if (tid == 0 && !mbar_wait(&bars[1], (ph >> 1) & 1u, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
-            ph ^= 2u;
-            __syncthreads();
-            const int rpw = 32 / lpr_h;
-            for (int rb = warp * rpw; rb < s1 - s0; rb += nw * rpw) {
-                const int rr = rb + sub_h;
-                const bool ok = rr < s1 - s0;
-                const int rs = ok ? rr : 0;
-                float g = qdot_t<SGU>(L0.shared_gate_type, sm + p.o_sgate + rs * rb_sg, pr_h >> 2, pr_h & 3, xl);
-                float u = qdot_t<SGU>(L0.shared_up_type, sm + p.o_sup + rs * rb_su, pr_h >> 2, pr_h & 3, xl);
-                g = group_sum(g, lpr_h);
-                u = group_sum(u, lpr_h);
-                if (ok && pr_h == 0) act_s[s0 + rr] = (g * shared_sigmoid(g)) * u;
-            }
-        }
-        __syncthreads();
-        if (tid == 0) red_release_add(p.ctr + C_SHARED, 1);
-        TRACE(4);
-
         // ---- routing (every CTA, identically)
         if (tid == 0 && !wait_flag(p.ctr + C_ROUTER, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
         __syncthreads();
@@ -342,12 +341,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         const int nrows = f1 - f0;
         const int CR = p.chunk_rows;
         const int nchunks = (nrows + CR - 1) / CR;
-        if (tid == 0) {
+        // issued by the lanes of warp 0 in parallel: lane q < nchunks chunk q,
+        // lanes 16.. the down rows of expert 16 - lane
+        if (warp == 0) {
             const uint8_t* gate = Ls->gate;
             const uint8_t* up = Ls->up;
             const uint8_t* down = Ls->down;
-            for (int q = 0; q < nchunks; ++q) {
-                const int q0 = q * CR, q1 = min(nrows, q0 + CR);
+            if (lane < nchunks) {
+                const int q = lane, q0 = q * CR, q1 = min(nrows, q0 + CR);
                 mbar_arrive_expect_tx(&bars[3 + q], (uint32_t)((q1 - q0) * (rb_gate + rb_up)));
                 for (int f = f0 + q0; f < f0 + q1;) {
                     const int a = f / I, r = f % I;
@@ -360,15 +361,34 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                     f += n;
                 }
             }
-            mbar_arrive_expect_tx(&bars[2], (uint32_t)(A * nh * rb_down));
-            if (nh > 0) {
-                for (int a = 0; a < A; ++a) {
-                    const int64_t e = s_ids[s_act[a]] - ebeg;
-                    bulk_g2s(sm + p.o_rdown + (int64_t)a * p.max_out_rows * rb_down,
-                             down + e * st_down + h0 * rb_down, (uint32_t)(nh * rb_down), &bars[2]);
-                }
+            if (lane == 16) mbar_arrive_expect_tx(&bars[2], (uint32_t)(A * nh * rb_down));
+            if (lane >= 16 && lane - 16 < A && nh > 0) {
+                const int a = lane - 16;
+                const int64_t e = s_ids[s_act[a]] - ebeg;
+                bulk_g2s(sm + p.o_rdown + (int64_t)a * p.max_out_rows * rb_down,
+                         down + e * st_down + h0 * rb_down, (uint32_t)(nh * rb_down), &bars[2]);
             }
         }
+
+        // ---- shared expert gate/up (x is the token), while the routed rows
+        // are in flight; rows go to the last warps first (warp 0 issues the
+        // copies).  Its counter is released with the gate/up one.
+        if (Is) {
+            if (!mbar_wait(&bars[1], (ph >> 1) & 1u, kWaitPolls) && lane == 0) set_error(p.ctr, ST_TIMEOUT);
+            ph ^= 2u;
+            const int rpw = 32 / lpr_h;
+            for (int rb = (nw - 1 - warp) * rpw; rb < s1 - s0; rb += nw * rpw) {
+                const int rr = rb + sub_h;
+                const bool ok = rr < s1 - s0;
+                const int rs = ok ? rr : 0;
+                float g = qdot_t<SGU>(L0.shared_gate_type, sm + p.o_sgate + rs * rb_sg, pr_h >> 2, pr_h & 3, xl);
+                float u = qdot_t<SGU>(L0.shared_up_type, sm + p.o_sup + rs * rb_su, pr_h >> 2, pr_h & 3, xl);
+                g = group_sum(g, lpr_h);
+                u = group_sum(u, lpr_h);
+                if (ok && pr_h == 0) act_s[s0 + rr] = (g * shared_sigmoid(g)) * u;
+            }
+        }
+        TRACE(4);
 
         // ---- routed gate/up, chunk by chunk
         {
@@ -406,6 +426,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         __syncthreads();
         TRACE(8);
         if (tid == 0) {
+            if (Is) red_release_add(p.ctr + C_SHARED, 1);
             red_release_add(p.ctr + C_GATEUP, 1);
             if (Is && !wait_flag(p.ctr + C_SHARED, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
             if (!wait_flag(p.ctr + C_GATEUP, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
@@ -506,7 +527,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             red_release_add(p.ctr + C_DONE, 1);
             // the router and shared-expert regions are free: the next step's
             // rows load while this CTA waits for the others
-            if (s + 1 < p.n_steps) issue_phase0(step_layer(s + 1));
+            if (s + 1 < p.n_steps) {
+                issue_phase0(step_layer(s + 1));
+                if (x_by_copy(s + 1)) issue_x(s + 1);
+            }
         }
     }
     // ---- exit: the last CTA resets the counters for the next launch
