@@ -156,7 +156,8 @@ MOE_B200_API int moe_b200_workspace_init(void* workspace, size_t workspace_bytes
 MOE_B200_API int moe_b200_workspace_error(void* workspace, void* stream, int* error);
 
 /* Number of kernels one moe_b200_decode call with this layer, token count
- * and the layer's flags launches (1 for the fused single-token path). */
+ * and the layer's flags launches (1 for the fused paths: one token, or up
+ * to 8 tokens and SHARED_ONLY calls of up to 8 tokens). */
 MOE_B200_API int moe_b200_decode_kernels(const moe_b200_layer* layer, int32_t tokens,
                                          int* kernels);
 
@@ -231,6 +232,24 @@ MOE_B200_API int moe_b200_decode_steps(const moe_b200_layer* layer0,
                                        const moe_b200_step* steps_dev, int32_t n_steps,
                                        float eps, void* workspace, size_t workspace_bytes,
                                        void* stream);
+
+/* One rank's part of an expert-parallel decode step over the tokens of
+ * all ranks (x: [tokens x H], tokens <= 8), in one cooperative launch:
+ * route every token with the replicated router, add the outputs of the
+ * selected experts this rank holds (expert_begin / expert_count), and add
+ * the sigmoid-gated shared expert to tokens [shared_begin, shared_begin +
+ * shared_count) only -- the rank's own tokens -- so that the sum of the
+ * partial outputs y over the ranks (the combine) is each token's layer
+ * output with the shared expert counted once.  No reference function has
+ * this signature: it replaces run_moe_layer (src/flash_moe/moe_layer.py:
+ * 39-107) on the expert-sharded layer.  Flags NO_SHARED / SHARED_ONLY are
+ * not accepted (-1); returns -2 when the fused multi-token kernel does not
+ * take these shapes or formats.  Workspace as moe_b200_decode_workspace
+ * with max_tokens >= tokens. */
+MOE_B200_API int moe_b200_decode_ep(const moe_b200_layer* layer, const float* x, int32_t tokens,
+                                    int32_t shared_begin, int32_t shared_count, float* y,
+                                    int32_t* topk_ids, float* topk_weights, void* workspace,
+                                    size_t workspace_bytes, void* stream);
 
 /* The transformer block with an identity mixer around a many-token MoE
  * call, for T tokens of H values (device fp32, row-major):

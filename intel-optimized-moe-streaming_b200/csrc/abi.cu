@@ -151,6 +151,8 @@ static DecodeWs decode_ws(const moe_b200_layer* L, int T) {
     w.total = s.used;
     const size_t fused = fused_workspace_bytes(L);
     if (fused > w.total) w.total = fused;
+    const size_t multi = multi_workspace_bytes(L, T);
+    if (multi > w.total) w.total = multi;
     return w;
 }
 
@@ -329,7 +331,7 @@ int moe_b200_decode_kernels(const moe_b200_layer* L, int32_t T, int* kernels) {
     const int st = check_layer(L);
     if (st != ST_OK) return st;
     if (T < 1 || !kernels) return ST_ARG;
-    if (fused_supported(L, T, L->flags)) {
+    if (fused_supported(L, T, L->flags) || multi_supported(L, T, L->flags)) {
         *kernels = 1;
     } else {
         const bool shared_only = (L->flags & MOE_B200_SHARED_ONLY) != 0;
@@ -365,6 +367,12 @@ int moe_b200_decode(const moe_b200_layer* L, const float* x, int32_t T, float* y
         bool launched = false;
         cudaError_t fe = launch_decode_fused(L, L->flags, x, y, topk_ids, topk_weights, workspace, s,
                                              &launched);
+        if (fe != cudaSuccess) return fail(fe, ST_CUDA);
+        if (launched) return ST_OK;
+    } else if (multi_supported(L, T, L->flags)) {
+        bool launched = false;
+        cudaError_t fe = launch_decode_multi(L, L->flags, x, T, 0, T, y, topk_ids, topk_weights,
+                                             workspace, s, &launched);
         if (fe != cudaSuccess) return fail(fe, ST_CUDA);
         if (launched) return ST_OK;
     }
@@ -448,6 +456,26 @@ int moe_b200_decode_steps(const moe_b200_layer* L0, const moe_b200_layer* layers
     if (workspace_bytes < decode_ws(L0, 1).total) return ST_WORKSPACE;
     bool launched = false;
     cudaError_t e = launch_decode_steps(L0, layers, steps, n_steps, eps, workspace,
+                                        static_cast<cudaStream_t>(stream), &launched);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    return launched ? ST_OK : ST_TYPE;
+}
+
+int moe_b200_decode_ep(const moe_b200_layer* L, const float* x, int32_t T, int32_t shared_begin,
+                       int32_t shared_count, float* y, int32_t* topk_ids, float* topk_weights,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+    int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (T < 1 || !x || !y || !workspace) return ST_ARG;
+    if (L->flags & (MOE_B200_SHARED_ONLY | MOE_B200_NO_SHARED)) return ST_ARG;
+    if (shared_begin < 0 || shared_count < 0 || shared_begin + shared_count > T) return ST_ARG;
+    if (shared_count > 0 && L->shared_intermediate <= 0) return ST_ARG;
+    if (!aligned16(x) || !aligned16(y) || ((uintptr_t)workspace & 255u)) return ST_ALIGN;
+    if (!multi_supported(L, T, L->flags)) return ST_TYPE;
+    if (workspace_bytes < decode_ws(L, T).total) return ST_WORKSPACE;
+    bool launched = false;
+    cudaError_t e = launch_decode_multi(L, L->flags, x, T, shared_begin, shared_begin + shared_count,
+                                        y, topk_ids, topk_weights, workspace,
                                         static_cast<cudaStream_t>(stream), &launched);
     if (e != cudaSuccess) return fail(e, ST_CUDA);
     return launched ? ST_OK : ST_TYPE;

@@ -27,6 +27,7 @@
 #include <math.h>
 #include <stdlib.h>
 
+#include "fused.cuh"
 #include "launch.h"
 #include "qdot.cuh"
 #include "sm100.cuh"
@@ -34,13 +35,8 @@
 
 namespace moeb200 {
 
-constexpr int kFusedThreads = 512;
-constexpr uint32_t kWaitPolls = 1u << 21;
-constexpr int kTraceSlots = 32;
 constexpr int kMaxChunks = 8;  // routed gate/up copy chunks (mbarriers 3..10)
 constexpr int kXBar = 3 + kMaxChunks;  // mbarrier of the prefetched token
-
-enum { C_ROUTER = 0, C_SHARED = 1, C_GATEUP = 2, C_EXIT = 3, C_DONE = 4, C_ERROR = 8 };
 
 struct FusedParams {
     moe_b200_layer L;        // shapes and block formats of every step's layer
@@ -66,40 +62,6 @@ struct FusedParams {
     uint32_t o_x32, o_h32, o_xq, o_router, o_sgate, o_sup, o_sdown, o_rgate, o_rup, o_rdown;
     uint32_t o_act, o_aq, o_misc, total;
 };
-
-__device__ __forceinline__ int part(int n, int c, int G) { return (int)(((int64_t)n * c) / G); }
-
-__device__ __forceinline__ void set_error(uint32_t* ctr, int code) {
-    atomicExch(reinterpret_cast<int*>(ctr + C_ERROR), code);
-}
-
-// fp32 row dot with x in shared memory, one warp.
-__device__ __forceinline__ float dot_f32_warp(const float* row, const float* x, int n, int lane) {
-    float acc = 0.f;
-    const float4* r4 = reinterpret_cast<const float4*>(row);
-    const float4* x4 = reinterpret_cast<const float4*>(x);
-    for (int i = lane; i < (n >> 2); i += 32) {
-        const float4 a = r4[i], b = x4[i];
-        acc = fmaf(a.x, b.x, acc);
-        acc = fmaf(a.y, b.y, acc);
-        acc = fmaf(a.z, b.z, acc);
-        acc = fmaf(a.w, b.w, acc);
-    }
-    return warp_sum(acc);
-}
-
-// Sum of v over the CTA in a fixed order (warp trees, then warps in order);
-// every thread gets the result.  `part` holds 32 floats.
-__device__ __forceinline__ float block_sum(float v, float* part) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_sum(v);
-    __syncthreads();
-    if (lane == 0) part[warp] = v;
-    __syncthreads();
-    float t = 0.f;
-    for (int i = 0; i < kFusedThreads / 32; ++i) t += part[i];
-    return t;
-}
 
 // GU: gate and up type, DN: routed down type, SGU: shared gate and up type,
 // SDN: shared down type -- each a ggml type id fixed at compile time, or -1

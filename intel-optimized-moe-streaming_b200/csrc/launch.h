@@ -68,6 +68,14 @@ cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float*
 cudaError_t launch_decode_steps(const moe_b200_layer* L0, const moe_b200_layer* layers,
                                 const moe_b200_step* steps, int n_steps, float eps, void* ws,
                                 cudaStream_t stream, bool* launched);
+// Fused layer decode of 1..8 tokens (decode_multi.cu); the shared expert
+// goes to tokens [sh_lo, sh_hi) only (with_shared layers).  Shares the
+// counter words of the single-token kernel.
+bool multi_supported(const moe_b200_layer* L, int T, int flags);
+size_t multi_workspace_bytes(const moe_b200_layer* L, int T);
+cudaError_t launch_decode_multi(const moe_b200_layer* L, int flags, const float* x, int T,
+                                int sh_lo, int sh_hi, float* y, int32_t* ids_out, float* w_out,
+                                void* ws, cudaStream_t stream, bool* launched);
 void set_fused_trace(void* buf, int capacity_ctas);
 uint64_t* trace_buffer(int* capacity_ctas);  // the buffer set above (this thread)
 

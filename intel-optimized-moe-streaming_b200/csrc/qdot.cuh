@@ -54,14 +54,11 @@ __device__ __forceinline__ QVec qvec_at(uint8_t* base, int n) {
     return q;
 }
 
-// Quantise 256-value block b of an fp32 vector in shared memory with one
-// warp: lane l takes values 8l..8l+7 (octet l).  No block-wide barrier; the
-// caller synchronises before the codes are read.
-__device__ __forceinline__ void quantize_block_warp(const float* v, QVec q, int b) {
+// Quantise one 256-value block b with one warp, lane l holding values
+// 8l..8l+7 (octet l) in `vals`.  No block-wide barrier; the caller
+// synchronises before the codes are read.
+__device__ __forceinline__ void quantize_block_vals(const float (&vals)[8], QVec q, int b) {
     const int lane = threadIdx.x & 31;
-    const float4 a0 = *reinterpret_cast<const float4*>(v + 256 * b + 8 * lane);
-    const float4 a1 = *reinterpret_cast<const float4*>(v + 256 * b + 8 * lane + 4);
-    const float vals[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     float m = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(vals[e]));
@@ -92,6 +89,25 @@ __device__ __forceinline__ void quantize_block_warp(const float* v, QVec q, int 
     *reinterpret_cast<uint2*>(q.lo + 8 * oc) = make_uint2(pl[0], pl[1]);
     q.oh[oc] = (int16_t)sh;
     q.ol[oc] = (int16_t)sl;
+}
+
+// Block b of an fp32 vector in shared memory.
+__device__ __forceinline__ void quantize_block_warp(const float* v, QVec q, int b) {
+    const int lane = threadIdx.x & 31;
+    const float4 a0 = *reinterpret_cast<const float4*>(v + 256 * b + 8 * lane);
+    const float4 a1 = *reinterpret_cast<const float4*>(v + 256 * b + 8 * lane + 4);
+    const float vals[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    quantize_block_vals(vals, q, b);
+}
+
+// Block b of an fp32 vector in global memory written by other CTAs of this
+// launch (read through L2).
+__device__ __forceinline__ void quantize_block_gmem(const float* v, QVec q, int b) {
+    const int lane = threadIdx.x & 31;
+    const float4 a0 = __ldcg(reinterpret_cast<const float4*>(v + 256 * b + 8 * lane));
+    const float4 a1 = __ldcg(reinterpret_cast<const float4*>(v + 256 * b + 8 * lane + 4));
+    const float vals[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    quantize_block_vals(vals, q, b);
 }
 
 // One lane's 64 activation codes of pair (b, o), in registers.

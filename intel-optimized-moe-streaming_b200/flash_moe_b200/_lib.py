@@ -71,6 +71,8 @@ def _bind(lib: C.CDLL) -> None:
         "moe_b200_prefill_workspace": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_size_t)]),
         "moe_b200_decode_steps": (i, [C.POINTER(Layer), vp, vp, C.c_int32, C.c_float, vp,
                                       C.c_size_t, vp]),
+        "moe_b200_decode_ep": (i, [C.POINTER(Layer), vp, C.c_int32, C.c_int32, C.c_int32, vp, vp,
+                                   vp, vp, C.c_size_t, vp]),
         "moe_b200_block_prepare": (i, [vp, vp, vp, C.c_int32, C.c_int32, C.c_float, vp]),
         "moe_b200_block_finish": (i, [vp, vp, vp, C.c_int32, C.c_int32, vp]),
         "moe_b200_prefill_supported": (i, [C.POINTER(Layer)]),

@@ -191,6 +191,33 @@ class B200ExpertBackend:
             ws.data_ptr(), ws.numel(), stream.cuda_stream)
         _lib.check(st, "moe_b200_decode")
 
+    def ep_fused_supported(self, layer: int, tokens: int) -> bool:
+        """True when ``decode_ep_device`` takes `tokens` gathered tokens of
+        `layer` (the fused multi-token kernel: at most 8 tokens)."""
+        if tokens < 2 or tokens > 8 or self.flags & (_lib.EXACT | _lib.FP16_GRAPH):
+            return False
+        return self.kernels_per_call(layer, tokens) == 1
+
+    def decode_ep_device(self, layer: int, x: torch.Tensor, y: torch.Tensor, shared_begin: int,
+                         shared_count: int, topk_ids: torch.Tensor | None = None,
+                         topk_weights: torch.Tensor | None = None, stream=None) -> None:
+        """One rank's expert-parallel step over the gathered tokens x [T, H]
+        (``moe_b200_decode_ep``): the held routed experts of every token,
+        and the shared expert of tokens [shared_begin, shared_begin +
+        shared_count) only; y [T, H] is this rank's partial output."""
+        dl = self.store.layer(layer)
+        t = x.shape[0]
+        s = dl.with_flags(self.flags)
+        ws = self._workspace(dl, t)
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        st = self.lib.moe_b200_decode_ep(
+            C.byref(s), x.data_ptr(), t, shared_begin, shared_count, y.data_ptr(),
+            topk_ids.data_ptr() if topk_ids is not None else None,
+            topk_weights.data_ptr() if topk_weights is not None else None,
+            ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        _lib.check(st, "moe_b200_decode_ep")
+
     # ---------------------------------------------------- multi-step decode
 
     def layer_table(self, layers) -> torch.Tensor:

@@ -5,18 +5,20 @@ Expert parallelism (EP): rank r of N holds routed experts
 shared expert.  One decode step for the T tokens each rank owns:
 
   1. all-gather the N*T tokens (dispatch: every rank sees every token);
-  2. one device call per rank routes all N*T tokens with the replicated
-     router and adds the contributions of the experts it holds (experts held
-     elsewhere contribute zero) -- ``moe_b200_decode`` with NO_SHARED;
+  2. one fused launch per rank (``moe_b200_decode_ep``) routes all N*T
+     tokens with the replicated router, adds the contributions of the
+     experts it holds (experts held elsewhere contribute zero) and the
+     sigmoid-gated shared expert of its own tokens;
   3. reduce-scatter the N*T partial outputs (combine: each token's owner
-     receives the sum over ranks of the held experts' weighted outputs);
-  4. the owner adds the sigmoid-gated shared expert of its own tokens
-     (``moe_b200_decode`` with SHARED_ONLY).
+     receives the sum over ranks, the shared expert counted once).
 
-For one token per rank this moves N*8 KB each way, the same bytes as an
-all-to-all of the tokens to the ranks holding their top-8 experts, with
-fixed-size collectives.  With N = 1 a step is a single device call and no
-collective runs.
+When the fused multi-token kernel does not take the shapes (or more than 8
+tokens are gathered), step 2 is ``moe_b200_decode`` with NO_SHARED and the
+owner adds ``moe_b200_decode`` with SHARED_ONLY after step 3.  For one
+token per rank this moves N*8 KB each way, the same bytes as an all-to-all
+of the tokens to the ranks holding their top-8 experts, with fixed-size
+collectives.  With N = 1 a step is a single device call and no collective
+runs.
 """
 from __future__ import annotations
 
@@ -42,12 +44,17 @@ def ep_exchange_step(x, routed_fn, shared_fn, x_all, y_part, y_routed, y_sh, y,
 
     ``routed_fn(x_all, y_part)`` writes, for all ``world * t`` gathered
     tokens, the weighted sum of the outputs of the experts this rank holds;
-    ``shared_fn(x, y_sh)`` writes the gated shared expert of the own tokens.
-    The collectives are the same on every rank and in the same order
-    (all-gather, then reduce-scatter), whatever the device or backend."""
+    ``shared_fn(x, y_sh)`` writes the gated shared expert of the own tokens,
+    or is None when ``routed_fn`` already added it to the own tokens' rows
+    (the reduce-scatter then writes ``y`` directly).  The collectives are
+    the same on every rank and in the same order (all-gather, then
+    reduce-scatter), whatever the device or backend."""
     import torch.distributed as dist
     dist.all_gather_into_tensor(x_all, x, group=group)
     routed_fn(x_all, y_part)
+    if shared_fn is None:
+        dist.reduce_scatter_tensor(y, y_part, group=group)
+        return
     dist.reduce_scatter_tensor(y_routed, y_part, group=group)
     shared_fn(x, y_sh)
     torch.add(y_routed, y_sh, out=y)
@@ -88,13 +95,17 @@ class DecodeRunner:
             self.y_part = torch.empty((world, H), dtype=torch.float32, device=self.dev)
             self.y_routed = torch.empty((1, H), dtype=torch.float32, device=self.dev)
             self.y_sh = torch.empty((1, H), dtype=torch.float32, device=self.dev)
+        self.fused_ep = world > 1 and backend.ep_fused_supported(self.layers[0], world)
         if world == 1:
             self.launches_per_step = backend.kernels_per_call(self.layers[0], 1)
+        elif self.fused_ep:
+            self.launches_per_step = 1
         else:
             self.launches_per_step = (
                 backend.kernels_per_call(self.layers[0], world, backend.flags | _lib.NO_SHARED)
                 + backend.kernels_per_call(self.layers[0], 1, backend.flags | _lib.SHARED_ONLY))
-        self.kernel_name = ("k_decode_fused (1 launch per step)" if self.launches_per_step == 1
+        self.kernel_name = ("k_decode_multi (1 launch per step)" if self.fused_ep
+                            else "k_decode_fused (1 launch per step)" if self.launches_per_step == 1
                             else f"moe_b200_decode ({self.launches_per_step} kernels per step)")
         self.recorded = 0
         self._graph = None
@@ -112,6 +123,13 @@ class DecodeRunner:
         self.recorded = max(self.recorded, slot + 1)
         if self.world == 1:
             self.be.forward_layer_device(layer, x, y, topk_ids=self.ids[slot])
+            return
+        if self.fused_ep:
+            ep_exchange_step(
+                x,
+                lambda xa, yp: self.be.decode_ep_device(layer, xa, yp, self.rank, 1,
+                                                        topk_ids=self.ids[slot]),
+                None, self.x_all, self.y_part, None, None, y)
             return
         ep_exchange_step(
             x,

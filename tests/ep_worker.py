@@ -1,8 +1,8 @@
 """Worker of test_gpu_ep.py, one process per GPU under torchrun.
 
 Rank r holds experts [r*E/N, (r+1)*E/N) of the config-2 layer.  Decode:
-DecodeRunner steps (all-gather, held experts, reduce-scatter, own shared
-expert) for 4 tokens per rank.  Prefill: the same exchange with
+DecodeRunner steps (all-gather, one fused launch of the held experts and
+the own token's shared expert, reduce-scatter) for 4 tokens per rank.  Prefill: the same exchange with
 moe_b200_prefill for 64 tokens per rank.  Rank 0 compares every rank's
 outputs with a single-GPU run of the whole layer and prints EP_OK."""
 from __future__ import annotations
@@ -47,9 +47,11 @@ def main() -> int:
     toks = torch.from_numpy(synth.make_tokens(500 + rank, n_dec, H)).to(dev)
     runner = DecodeRunner(be, [0], toks, world, rank)
     y_dec = torch.empty((n_dec, H), dtype=torch.float32, device=dev)
+    assert runner.fused_ep and runner.launches_per_step == 1
     for i in range(n_dec):
         runner.step(i, x=toks[i:i + 1], y=y_dec[i:i + 1])
     torch.cuda.synchronize()
+    assert be.device_errors() == 0
 
     # ---- prefill: 64 tokens per rank through the tensor-core path
     n_pf = 64
@@ -89,7 +91,11 @@ def main() -> int:
         e_pf = max_rel(torch.cat(ys_pf).cpu().numpy(), want_pf.cpu().numpy())
         torch.cuda.synchronize()
         print(f"ep decode max rel {e_dec:.3e}  ep prefill max rel {e_pf:.3e}", flush=True)
-        ok = e_dec <= 1e-5 and e_pf <= 1e-5
+        # decode: the fused kernel's integer dot products (activations
+        # quantised to 16 bits per 256-value block) against the exact engine,
+        # at the layer tolerance; prefill: the same tensor-core arithmetic
+        # on both sides, summed in another order
+        ok = e_dec <= 1e-3 and e_pf <= 1e-5
         if ok:
             print("EP_OK", flush=True)
     dist.barrier()
