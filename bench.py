@@ -410,9 +410,20 @@ def run_gpu(args) -> None:
 
     peaks, peak_kind = measured_peaks()
     with ClockSampler(local) as clk:
-        # soak ~0.5 s so the clock sampler sees the GPU under this load
-        t_end = time.perf_counter() + args.soak
-        while time.perf_counter() < t_end:
+        # soak ~0.5 s so the clock sampler sees the GPU under this load; every
+        # rank runs the same number of rounds (rank 0's count), since each
+        # round holds collectives when world > 1
+        n_soak = 0
+        if args.soak > 0:
+            t0 = time.perf_counter()
+            timed_steps()
+            torch.cuda.synchronize()
+            n_soak = int(args.soak / max(time.perf_counter() - t0, 1e-6))
+        if world > 1:
+            n_t = torch.tensor([n_soak], device=dev)
+            dist.broadcast(n_t, 0)
+            n_soak = int(n_t.item())
+        for _ in range(n_soak):
             timed_steps()
             torch.cuda.synchronize()
         if world > 1:

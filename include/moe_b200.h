@@ -251,6 +251,36 @@ MOE_B200_API int moe_b200_decode_ep(const moe_b200_layer* layer, const float* x,
                                     int32_t* topk_ids, float* topk_weights, void* workspace,
                                     size_t workspace_bytes, void* stream);
 
+/* Expert-parallel decode with the dispatch and the combine inside the
+ * layer kernel, over NVLink peer memory instead of collectives.  Each rank
+ * creates an exchange context (device buffer for the gathered tokens, the
+ * partial outputs and the step flags), publishes its blob of
+ * MOE_B200_EP_BLOB_BYTES bytes (an IPC handle and the agreed shape), and
+ * connects with the blobs of all ranks in rank order.  Every rank must have
+ * the same world, tokens_per_rank, hidden and multiprocessor count.
+ * moe_b200_decode_ep_p2p then runs one step: it pushes this rank's x
+ * [tokens_per_rank x H] to every rank, routes all world * tokens_per_rank
+ * tokens, applies the experts this rank holds, pushes each token's partial
+ * output to its owner, and writes into y the sum over ranks (rank order) for
+ * this rank's tokens, with the shared expert added once by the owner.
+ * Every rank runs the same steps in the same order; a rank that waits
+ * longer than about a second for its peers records -9 in the workspace
+ * error word.  topk_ids / topk_weights ([world * tokens_per_rank x K])
+ * receive the routing of every gathered token (row r * tokens_per_rank + j:
+ * rank r's token j).  No reference function has these signatures: they
+ * replace the per-layer run_moe_layer call (src/flash_moe/moe_layer.py:
+ * 39-107) of an expert-sharded model. */
+#define MOE_B200_EP_BLOB_BYTES 128
+typedef struct moe_b200_ep moe_b200_ep;
+MOE_B200_API int moe_b200_ep_create(int32_t world, int32_t rank, int32_t tokens_per_rank,
+                                    int32_t hidden, moe_b200_ep** ctx, void* blob);
+MOE_B200_API int moe_b200_ep_connect(moe_b200_ep* ctx, const void* blobs);
+MOE_B200_API int moe_b200_ep_destroy(moe_b200_ep* ctx);
+MOE_B200_API int moe_b200_decode_ep_p2p(const moe_b200_layer* layer, moe_b200_ep* ctx,
+                                        const float* x, float* y, int32_t* topk_ids,
+                                        float* topk_weights, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
 /* The transformer block with an identity mixer around a many-token MoE
  * call, for T tokens of H values (device fp32, row-major):
  *   moe_b200_block_prepare: h = x + f16(rmsnorm(x)), n = f16(rmsnorm(h))

@@ -481,6 +481,46 @@ int moe_b200_decode_ep(const moe_b200_layer* L, const float* x, int32_t T, int32
     return launched ? ST_OK : ST_TYPE;
 }
 
+int moe_b200_ep_create(int32_t world, int32_t rank, int32_t tokens_per_rank, int32_t hidden,
+                       moe_b200_ep** ctx, void* blob) {
+    if (!ctx || !blob) return ST_ARG;
+    cudaError_t ce = cudaSuccess;
+    const int st = ep_create(world, rank, tokens_per_rank, hidden, ctx, blob, &ce);
+    return st == ST_CUDA ? fail(ce, ST_CUDA) : st;
+}
+
+int moe_b200_ep_connect(moe_b200_ep* ctx, const void* blobs) {
+    cudaError_t ce = cudaSuccess;
+    const int st = ep_connect(ctx, blobs, &ce);
+    return st == ST_CUDA ? fail(ce, ST_CUDA) : st;
+}
+
+int moe_b200_ep_destroy(moe_b200_ep* ctx) {
+    if (!ctx) return ST_ARG;
+    ep_destroy(ctx);
+    return ST_OK;
+}
+
+int moe_b200_decode_ep_p2p(const moe_b200_layer* L, moe_b200_ep* ctx, const float* x, float* y,
+                           int32_t* topk_ids, float* topk_weights, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+    int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (!ctx || !x || !y || !workspace) return ST_ARG;
+    if (!ctx->connected || L->hidden != ctx->H) return ST_ARG;
+    if (L->flags & (MOE_B200_SHARED_ONLY | MOE_B200_NO_SHARED)) return ST_ARG;
+    if (!aligned16(x) || !aligned16(y) || ((uintptr_t)workspace & 255u)) return ST_ALIGN;
+    const int T = ctx->world * ctx->tq;
+    if (!multi_supported(L, T, L->flags)) return ST_TYPE;
+    if (workspace_bytes < decode_ws(L, T).total) return ST_WORKSPACE;
+    bool launched = false;
+    cudaError_t e = launch_decode_multi(L, L->flags, x, T, 0, 0, y, topk_ids, topk_weights,
+                                        workspace, static_cast<cudaStream_t>(stream), &launched,
+                                        ctx);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    return launched ? ST_OK : ST_TYPE;
+}
+
 int moe_b200_prefill_supported(const moe_b200_layer* L) {
     if (check_layer(L) != ST_OK) return 0;
     return prefill_supported(L, L->flags) ? 1 : 0;

@@ -31,6 +31,9 @@
 // (the other ranks' partial outputs then carry routed experts only, and the
 // sum over ranks counts the shared expert once).
 #include <math.h>
+#include <string.h>
+
+#include <new>
 
 #include "fused.cuh"
 #include "launch.h"
@@ -44,6 +47,23 @@ constexpr int kMultiMaxTokens = 8;
 constexpr int kRing = 4;  // ring slots
 constexpr int kBarRouter = 0, kBarShared = 1, kBarX = 2, kBarRing = 3;
 constexpr int kMultiMisc = 2560;  // barriers + routing tables (offsets below)
+
+// Expert-parallel exchange over peer memory: every rank has one exchange
+// buffer, mapped into every other rank's address space, of exchange words
+// (payload + step number in one 64-bit store, see st_word_sys):
+//   xs    [world*tq][H]    gathered tokens (rank r's rows r*tq..)
+//   yp    [world][tq][H]   partial outputs of this rank's tokens, by sender
+//   seq                    steps run (this rank's copy only)
+struct EpView {
+    int world, rank, tq;
+    const float* x_own;          // [tq][H] this rank's tokens
+    float* y_own;                // [tq][H] their layer outputs
+    const uint64_t* xs;          // local buffer
+    const uint64_t* yp;
+    uint32_t* seq;
+    uint64_t* xs_peer[kMultiMaxTokens];    // the same regions of rank q (q = rank: local)
+    uint64_t* yp_peer[kMultiMaxTokens];
+};
 
 struct MultiParams {
     moe_b200_layer L;
@@ -66,6 +86,8 @@ struct MultiParams {
     int gu_rows;         // routed gate/up rows that fit one slot
     int dn_pairs;        // pairs whose down rows [h0, h1) fit one slot
     uint32_t o_vout, o_sgate, o_sup, o_sdown, o_q, o_ring, total;
+    uint64_t* trace;     // [G x 32] phase timestamps (ns), or null
+    EpView ep;           // peer-memory exchange (ep.world > 0), else unused
 };
 
 template <int GU, int DN, int SGU, int SDN>
@@ -112,9 +134,17 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
         mbar_fence_init();
     }
     __syncthreads();
+    uint64_t* trace = p.trace ? p.trace + (size_t)c * kTraceSlots : nullptr;
+#define TRACE(i) do { if (trace && tid == 0) trace[i] = global_ns(); } while (0)
+    TRACE(0);
+    const EpView& ep = p.ep;
+    const bool xch = ep.world > 0;
+    const uint32_t seq = xch ? *reinterpret_cast<volatile uint32_t*>(ep.seq) + 1u : 0u;
     if (tid == 0) {
-        mbar_arrive_expect_tx(&bars[kBarX], (uint32_t)(T * H * 4));
-        bulk_g2s(x32, p.x, (uint32_t)(T * H * 4), &bars[kBarX]);
+        if (!xch) {
+            mbar_arrive_expect_tx(&bars[kBarX], (uint32_t)(T * H * 4));
+            bulk_g2s(x32, p.x, (uint32_t)(T * H * 4), &bars[kBarX]);
+        }
         if (p.routed) {
             mbar_arrive_expect_tx(&bars[kBarRouter], (uint32_t)((r1 - r0) * H * 4));
             if (r1 > r0)
@@ -137,10 +167,37 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
     }
 
     // ---- the tokens; router scores of rows [r0, r1), one warp per (row, token)
-    if (tid == 0 && !mbar_wait(&bars[kBarX], 0, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+    if (xch) {
+        // dispatch: CTA q < world writes this rank's tokens into rank q's
+        // gathered-token rows; every CTA then reads all ranks' tokens from
+        // its own buffer as their words arrive
+        if (c < ep.world) {
+            uint64_t* dst = ep.xs_peer[c] + (size_t)ep.rank * ep.tq * H;
+            for (int i = tid; i < ep.tq * H; i += kFusedThreads) st_word_sys(dst + i, ep.x_own[i], seq);
+            TRACE(1);
+        }
+        bool ok = true;
+        for (int i0 = tid; i0 < T * H; i0 += 4 * kFusedThreads) {
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kFusedThreads;
+                if (i < T * H) v[u] = wait_word_sys(ep.xs + i, seq, kWaitPolls, ok);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kFusedThreads;
+                if (i < T * H) x32[i] = v[u];
+            }
+        }
+        if (!ok) set_error(p.ctr, ST_TIMEOUT);
+    } else if (tid == 0 && !mbar_wait(&bars[kBarX], 0, kWaitPolls)) {
+        set_error(p.ctr, ST_TIMEOUT);
+    }
     if (p.routed && tid == 0 && !mbar_wait(&bars[kBarRouter], 0, kWaitPolls))
         set_error(p.ctr, ST_TIMEOUT);
     __syncthreads();
+    TRACE(2);
     if (p.routed) {
         const float* bias = L.router_bias;
         const int R = r1 - r0;
@@ -154,6 +211,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
         }
         __syncthreads();
         if (tid == 0) red_release_add(p.ctr + C_ROUTER, 1);
+        TRACE(3);
     }
 
     // ---- token codes for the integer dot products; shared gates (CTA 0)
@@ -180,6 +238,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
     if (p.routed) {
         if (tid == 0 && !wait_flag(p.ctr + C_ROUTER, (uint32_t)G, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
         __syncthreads();
+        TRACE(4);
         if (warp < T) topk_softmax_warp_fast(p.scores + (size_t)warp * E, E, K, s_ids + warp * K, s_w + warp * K);
         __syncthreads();
         if (warp == 0) {
@@ -212,6 +271,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
         __syncthreads();
     }
     const int P = p.routed ? *s_np : 0;
+    TRACE(5);
 
     // ---- ring plan (identical in every thread)
     const int f0 = part(P * I, c, G), f1 = part(P * I, c + 1, G);
@@ -288,6 +348,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
         }
     }
 
+    TRACE(6);
     // ---- routed gate/up, chunk by chunk
     {
         const int rpw = 32 / lpr_h;
@@ -320,11 +381,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
         }
     }
     __syncthreads();
+    TRACE(7);
     if (tid == 0) {
         red_release_add(p.ctr + C_GATEUP, 1);
         if (!wait_flag(p.ctr + C_GATEUP, (uint32_t)G, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
     }
     __syncthreads();
+    TRACE(8);
 
     // ---- activation codes: pair v < P (routed), P + j (shared of token sh_lo + j)
     {
@@ -342,6 +405,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
         if (tid < ns) s_sg[tid] = __ldcg(p.sg + p.sh_lo + tid);
     }
     __syncthreads();
+    TRACE(9);
 
     // ---- down rows [h0, h1): item = (vector, pair of row groups)
     if (Is) {
@@ -393,6 +457,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
         }
     }
     __syncthreads();
+    TRACE(10);
 
     // ---- weighted sum in top-k order, + shared (moe_layer.py:85-86, 102-105)
     for (int i = tid; i < T * nh; i += kFusedThreads) {
@@ -406,9 +471,33 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
         }
         if (t >= p.sh_lo && t < p.sh_hi)
             comb = __fadd_rn(comb, __fmul_rn(s_sg[t - p.sh_lo], s_vout[(TK + t - p.sh_lo) * MO + rr]));
-        p.y[(size_t)t * H + h0 + rr] = comb;
+        if (xch) {
+            // combine: the partial row goes to the token's owner
+            const int q = t / ep.tq, j = t % ep.tq;
+            st_word_sys(ep.yp_peer[q] + ((size_t)ep.rank * ep.tq + j) * H + h0 + rr, comb, seq);
+        } else {
+            p.y[(size_t)t * H + h0 + rr] = comb;
+        }
+    }
+    if (xch) {
+        // CTA c of every rank sends rows [h0, h1) of its partials; the own
+        // tokens' rows are the sum over ranks in rank order
+        TRACE(11);
+        bool ok = true;
+        for (int i = tid; i < ep.tq * nh; i += kFusedThreads) {
+            const int j = i / nh, rr = i % nh;
+            float acc = 0.f;
+            for (int r = 0; r < ep.world; ++r)
+                acc = __fadd_rn(acc, wait_word_sys(ep.yp + ((size_t)r * ep.tq + j) * H + h0 + rr, seq,
+                                                   kWaitPolls, ok));
+            ep.y_own[(size_t)j * H + h0 + rr] = acc;
+        }
+        if (!ok) set_error(p.ctr, ST_TIMEOUT);
+        TRACE(12);
     }
 
+    TRACE(13);
+#undef TRACE
     // ---- exit: the last CTA resets the counters for the next launch
     if (tid == 0) {
         __threadfence();
@@ -417,6 +506,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
             p.ctr[C_ROUTER] = 0;
             p.ctr[C_GATEUP] = 0;
             p.ctr[C_EXIT] = 0;
+            if (xch) *ep.seq = seq;
             __threadfence();
         }
     }
@@ -503,8 +593,15 @@ size_t multi_workspace_bytes(const moe_b200_layer* L, int T) {
 
 cudaError_t launch_decode_multi(const moe_b200_layer* L, int flags, const float* x, int T,
                                 int sh_lo, int sh_hi, float* y, int32_t* ids_out, float* w_out,
-                                void* ws, cudaStream_t stream, bool* launched) {
+                                void* ws, cudaStream_t stream, bool* launched,
+                                const moe_b200_ep* xc) {
     *launched = false;
+    if (xc) {
+        // the exchange fixes the token set and the shared expert's tokens
+        if (!xc->connected || T != xc->world * xc->tq || sm_count() != xc->G) return cudaSuccess;
+        sh_lo = xc->rank * xc->tq;
+        sh_hi = sh_lo + xc->tq;
+    }
     const bool shared_only = (flags & MOE_B200_SHARED_ONLY) != 0;
     const bool shared = L->shared_intermediate > 0 && !(flags & MOE_B200_NO_SHARED);
     if (!shared) sh_lo = sh_hi = 0;
@@ -549,6 +646,27 @@ cudaError_t launch_decode_multi(const moe_b200_layer* L, int flags, const float*
     p.y = y;
     p.ids_out = ids_out;
     p.w_out = w_out;
+    if (xc) {
+        EpView& v = p.ep;
+        v.world = xc->world;
+        v.rank = xc->rank;
+        v.tq = xc->tq;
+        v.x_own = x;
+        v.y_own = y;
+        for (int q = 0; q < xc->world; ++q) {
+            char* b = xc->peer[q];
+            v.xs_peer[q] = reinterpret_cast<uint64_t*>(b + xc->o_xs);
+            v.yp_peer[q] = reinterpret_cast<uint64_t*>(b + xc->o_yp);
+        }
+        v.xs = v.xs_peer[xc->rank];
+        v.yp = v.yp_peer[xc->rank];
+        v.seq = reinterpret_cast<uint32_t*>(xc->local + xc->o_seq);
+        p.x = nullptr;
+        p.y = nullptr;
+    }
+    int trace_cap = 0;
+    uint64_t* tb = trace_buffer(&trace_cap);
+    p.trace = (tb && trace_cap >= G) ? tb : nullptr;
     p.T = T;
     p.routed = shared_only ? 0 : 1;
     p.sh_lo = sh_lo;
@@ -576,6 +694,108 @@ cudaError_t launch_decode_multi(const moe_b200_layer* L, int flags, const float*
     cudaError_t e = cudaLaunchKernelEx(&cfg, kInstances[pick].fn, p);
     if (e == cudaSuccess) *launched = true;
     return e;
+}
+
+// ------------------------------------------------------- exchange context
+
+// What one rank publishes to the others: its buffer's IPC handle and the
+// shape every rank must agree on.
+struct EpBlob {
+    cudaIpcMemHandle_t handle;
+    int32_t magic, world, rank, tq, H, G;
+    uint64_t bytes;
+};
+static_assert(sizeof(EpBlob) <= MOE_B200_EP_BLOB_BYTES, "exchange blob too large");
+constexpr int32_t kEpMagic = 0x4d4f4550;  // "MOEP"
+
+int ep_create(int world, int rank, int tq, int H, moe_b200_ep** out, void* blob_out,
+              cudaError_t* ce) {
+    *out = nullptr;
+    *ce = cudaSuccess;
+    if (world < 2 || world > kMultiMaxTokens || rank < 0 || rank >= world || tq < 1 ||
+        world * tq > kMultiMaxTokens || H < 256 || H % 256)
+        return ST_ARG;
+    auto* c = new (std::nothrow) moe_b200_ep();
+    if (!c) return ST_INTERNAL;
+    c->world = world;
+    c->rank = rank;
+    c->tq = tq;
+    c->H = H;
+    c->G = sm_count();
+    cudaGetDevice(&c->dev);
+    Stager st;
+    c->o_xs = st.take((size_t)world * tq * H * 8);
+    c->o_yp = st.take((size_t)world * tq * H * 8);
+    c->o_seq = st.take(4);
+    c->bytes = st.used;
+    cudaError_t e = cudaMalloc(&c->local, c->bytes);
+    if (e == cudaSuccess) e = cudaMemset(c->local, 0, c->bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    EpBlob b{};
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&b.handle, c->local);
+    if (e != cudaSuccess) {
+        if (c->local) cudaFree(c->local);
+        delete c;
+        *ce = e;
+        return ST_CUDA;
+    }
+    b.magic = kEpMagic;
+    b.world = world;
+    b.rank = rank;
+    b.tq = tq;
+    b.H = H;
+    b.G = c->G;
+    b.bytes = c->bytes;
+    memset(blob_out, 0, MOE_B200_EP_BLOB_BYTES);
+    memcpy(blob_out, &b, sizeof(b));
+    for (int q = 0; q < kMultiMaxTokens; ++q) c->peer[q] = nullptr;
+    c->peer[rank] = c->local;
+    *out = c;
+    return ST_OK;
+}
+
+int ep_connect(moe_b200_ep* c, const void* blobs, cudaError_t* ce) {
+    *ce = cudaSuccess;
+    if (!c || !blobs || c->connected) return ST_ARG;
+    const uint8_t* raw = static_cast<const uint8_t*>(blobs);
+    for (int q = 0; q < c->world; ++q) {
+        EpBlob b;
+        memcpy(&b, raw + (size_t)q * MOE_B200_EP_BLOB_BYTES, sizeof(b));
+        if (b.magic != kEpMagic || b.world != c->world || b.rank != q || b.tq != c->tq ||
+            b.H != c->H || b.G != c->G || b.bytes != c->bytes)
+            return ST_ARG;
+    }
+    for (int q = 0; q < c->world; ++q) {
+        if (q == c->rank) continue;
+        EpBlob b;
+        memcpy(&b, raw + (size_t)q * MOE_B200_EP_BLOB_BYTES, sizeof(b));
+        void* ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, b.handle, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int k = 0; k < q; ++k)
+                if (k != c->rank && c->peer[k]) {
+                    cudaIpcCloseMemHandle(c->peer[k]);
+                    c->peer[k] = nullptr;
+                }
+            *ce = e;
+            return ST_CUDA;
+        }
+        c->peer[q] = static_cast<char*>(ptr);
+    }
+    c->connected = true;
+    return ST_OK;
+}
+
+void ep_destroy(moe_b200_ep* c) {
+    if (!c) return;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(c->dev);
+    for (int q = 0; q < c->world; ++q)
+        if (q != c->rank && c->peer[q]) cudaIpcCloseMemHandle(c->peer[q]);
+    if (c->local) cudaFree(c->local);
+    cudaSetDevice(cur);
+    delete c;
 }
 
 }  // namespace moeb200

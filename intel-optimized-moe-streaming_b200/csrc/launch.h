@@ -4,6 +4,16 @@
 #include "common.cuh"
 #include "moe_b200.h"
 
+// This rank's expert-parallel exchange buffer and its peers' mappings
+// (decode_multi.cu).  Region offsets are the same on every rank.
+struct moe_b200_ep {
+    int world = 0, rank = 0, tq = 0, H = 0, G = 0, dev = 0;
+    char* local = nullptr;    // this rank's buffer
+    char* peer[8] = {};       // every rank's buffer in this process (peer[rank] = local)
+    size_t o_xs = 0, o_yp = 0, o_seq = 0, bytes = 0;
+    bool connected = false;
+};
+
 namespace moeb200 {
 
 int sm_count();  // multiprocessors of the current device (cached per device)
@@ -73,9 +83,17 @@ cudaError_t launch_decode_steps(const moe_b200_layer* L0, const moe_b200_layer* 
 // counter words of the single-token kernel.
 bool multi_supported(const moe_b200_layer* L, int T, int flags);
 size_t multi_workspace_bytes(const moe_b200_layer* L, int T);
+// With an exchange context xc (expert-parallel over peer memory): x and y
+// are this rank's xc->tq tokens, T = world * tq, the shared expert covers
+// the own tokens and the routing outputs all T gathered tokens.
 cudaError_t launch_decode_multi(const moe_b200_layer* L, int flags, const float* x, int T,
                                 int sh_lo, int sh_hi, float* y, int32_t* ids_out, float* w_out,
-                                void* ws, cudaStream_t stream, bool* launched);
+                                void* ws, cudaStream_t stream, bool* launched,
+                                const moe_b200_ep* xc = nullptr);
+int ep_create(int world, int rank, int tq, int H, moe_b200_ep** out, void* blob_out,
+              cudaError_t* ce);
+int ep_connect(moe_b200_ep* c, const void* blobs, cudaError_t* ce);
+void ep_destroy(moe_b200_ep* c);
 void set_fused_trace(void* buf, int capacity_ctas);
 uint64_t* trace_buffer(int* capacity_ctas);  // the buffer set above (this thread)
 

@@ -76,6 +76,59 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t target,
     return false;
 }
 
+// System-scope flag operations for flags in memory that another GPU writes
+// or reads over NVLink (peer mappings of device memory).
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Spin (one thread) until *flag >= target (a flag a peer GPU sets), at most
+// `limit` polls.
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t* flag, uint32_t target, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i) {
+        if ((int32_t)(ld_acquire_sys(flag) - target) >= 0) return true;
+    }
+    return false;
+}
+
+// One exchange word for memory another GPU reads: a 32-bit payload in the
+// low half and the step number in the high half, written with one 64-bit
+// store (single-copy atomic), so a reader that sees the step number also
+// sees the payload -- no fence or separate flag.
+__device__ __forceinline__ void st_word_sys(uint64_t* p, float v, uint32_t seq) {
+    const uint64_t w = ((uint64_t)seq << 32) | (uint64_t)__float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_word_sys(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+// Payload of the exchange word at p once it carries step `seq`; at most
+// `limit` polls while *ok (cleared when the limit is hit, so a thread that
+// gave up once stops waiting).
+__device__ __forceinline__ float wait_word_sys(const uint64_t* p, uint32_t seq, uint32_t limit,
+                                               bool& ok) {
+    uint64_t w = ld_word_sys(p);
+    if (ok && (uint32_t)(w >> 32) != seq) {
+        uint32_t i = 0;
+        for (; i < limit; ++i) {
+            w = ld_word_sys(p);
+            if ((uint32_t)(w >> 32) == seq) break;
+        }
+        if (i == limit) ok = false;
+    }
+    return __uint_as_float((uint32_t)w);
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -27,6 +27,7 @@ FP16_GRAPH = 1
 NO_SHARED = 2
 EXACT = 4
 SHARED_ONLY = 8
+EP_BLOB_BYTES = 128  # MOE_B200_EP_BLOB_BYTES
 STEP_CHAIN = 1
 STEP_BLOCK = 2
 
@@ -73,6 +74,11 @@ def _bind(lib: C.CDLL) -> None:
                                       C.c_size_t, vp]),
         "moe_b200_decode_ep": (i, [C.POINTER(Layer), vp, C.c_int32, C.c_int32, C.c_int32, vp, vp,
                                    vp, vp, C.c_size_t, vp]),
+        "moe_b200_ep_create": (i, [C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                   C.POINTER(C.c_void_p), vp]),
+        "moe_b200_ep_connect": (i, [vp, vp]),
+        "moe_b200_ep_destroy": (i, [vp]),
+        "moe_b200_decode_ep_p2p": (i, [C.POINTER(Layer), vp, vp, vp, vp, vp, vp, C.c_size_t, vp]),
         "moe_b200_block_prepare": (i, [vp, vp, vp, C.c_int32, C.c_int32, C.c_float, vp]),
         "moe_b200_block_finish": (i, [vp, vp, vp, C.c_int32, C.c_int32, vp]),
         "moe_b200_prefill_supported": (i, [C.POINTER(Layer)]),

@@ -218,6 +218,25 @@ class B200ExpertBackend:
             ws.data_ptr(), ws.numel(), stream.cuda_stream)
         _lib.check(st, "moe_b200_decode_ep")
 
+    def decode_ep_p2p_device(self, layer: int, exchange, x: torch.Tensor, y: torch.Tensor,
+                             topk_ids: torch.Tensor | None = None,
+                             topk_weights: torch.Tensor | None = None, stream=None) -> None:
+        """One expert-parallel step with dispatch and combine over peer
+        memory (``moe_b200_decode_ep_p2p``): x, y [tokens_per_rank, H] are
+        this rank's tokens; topk_ids / topk_weights [world * tokens_per_rank,
+        K] receive the routing of every gathered token."""
+        dl = self.store.layer(layer)
+        s = dl.with_flags(self.flags)
+        ws = self._workspace(dl, exchange.world * exchange.tokens_per_rank)
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        st = self.lib.moe_b200_decode_ep_p2p(
+            C.byref(s), exchange.handle, x.data_ptr(), y.data_ptr(),
+            topk_ids.data_ptr() if topk_ids is not None else None,
+            topk_weights.data_ptr() if topk_weights is not None else None,
+            ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        _lib.check(st, "moe_b200_decode_ep_p2p")
+
     # ---------------------------------------------------- multi-step decode
 
     def layer_table(self, layers) -> torch.Tensor:

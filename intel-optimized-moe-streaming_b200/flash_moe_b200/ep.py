@@ -2,23 +2,27 @@
 
 Expert parallelism (EP): rank r of N holds routed experts
 [r*E/N, (r+1)*E/N) of every layer plus full copies of the router and the
-shared expert.  One decode step for the T tokens each rank owns:
+shared expert.  One decode step for the T tokens each rank owns is ONE
+launch of the fused multi-token kernel per rank (``moe_b200_decode_ep_p2p``)
+that also does the exchange, over NVLink peer memory:
 
-  1. all-gather the N*T tokens (dispatch: every rank sees every token);
-  2. one fused launch per rank (``moe_b200_decode_ep``) routes all N*T
-     tokens with the replicated router, adds the contributions of the
-     experts it holds (experts held elsewhere contribute zero) and the
-     sigmoid-gated shared expert of its own tokens;
-  3. reduce-scatter the N*T partial outputs (combine: each token's owner
-     receives the sum over ranks, the shared expert counted once).
+  1. dispatch: the kernel pushes the rank's tokens into every rank's
+     exchange buffer and waits (bounded) for all ranks' tokens;
+  2. it routes all N*T tokens with the replicated router and applies the
+     experts this rank holds (experts held elsewhere contribute zero), plus
+     the sigmoid-gated shared expert of its own tokens;
+  3. combine: each CTA pushes its output rows of every token's partial sum
+     to the token's owner, waits for the same rows from every rank and adds
+     them in rank order.
 
-When the fused multi-token kernel does not take the shapes (or more than 8
-tokens are gathered), step 2 is ``moe_b200_decode`` with NO_SHARED and the
-owner adds ``moe_b200_decode`` with SHARED_ONLY after step 3.  For one
-token per rank this moves N*8 KB each way, the same bytes as an all-to-all
-of the tokens to the ranks holding their top-8 experts, with fixed-size
-collectives.  With N = 1 a step is a single device call and no collective
-runs.
+Where the buffers cannot be mapped between the ranks, the same step runs
+with collectives around the kernel: all-gather the tokens,
+``moe_b200_decode_ep`` (held experts + own shared expert), reduce-scatter
+the partial outputs.  For more than 8 gathered tokens, or shapes the fused
+kernel does not take, the kernel is ``moe_b200_decode`` with NO_SHARED and
+the owner adds ``moe_b200_decode`` with SHARED_ONLY after the
+reduce-scatter.  With N = 1 a step is a single device call and nothing is
+exchanged.
 """
 from __future__ import annotations
 
@@ -70,6 +74,52 @@ def profiled_traffic(root: Path, name: str = "decode_layer") -> float | None:
     return None
 
 
+class PeerExchange:
+    """This rank's exchange context for expert-parallel steps with the
+    dispatch and combine over NVLink peer memory (``moe_b200_ep_create`` /
+    ``_connect``).  Built collectively by every rank of `group`; when any
+    rank cannot create or map the buffers, every rank gets None from
+    ``create`` and the caller keeps the collective-based step."""
+
+    def __init__(self, lib, handle, world: int, rank: int, tokens_per_rank: int):
+        self.lib, self.handle = lib, handle
+        self.world, self.rank, self.tokens_per_rank = world, rank, tokens_per_rank
+
+    @classmethod
+    def create(cls, lib, world: int, rank: int, tokens_per_rank: int, hidden: int, group=None):
+        import ctypes as C
+        import torch.distributed as dist
+        ctx = C.c_void_p()
+        blob = (C.c_uint8 * _lib.EP_BLOB_BYTES)()
+        st = lib.moe_b200_ep_create(world, rank, tokens_per_rank, hidden, C.byref(ctx), blob)
+        got = [None] * world
+        dist.all_gather_object(got, (st, bytes(blob)), group=group)
+        if any(s != 0 for s, _ in got):
+            if st == 0:
+                lib.moe_b200_ep_destroy(ctx)
+            return None
+        blobs = (C.c_uint8 * (_lib.EP_BLOB_BYTES * world)).from_buffer_copy(
+            b"".join(b for _, b in got))
+        st = lib.moe_b200_ep_connect(ctx, blobs)
+        oks = [None] * world
+        dist.all_gather_object(oks, st, group=group)
+        if any(s != 0 for s in oks):
+            lib.moe_b200_ep_destroy(ctx)
+            return None
+        return cls(lib, ctx, world, rank, tokens_per_rank)
+
+    def close(self, group=None) -> None:
+        """Free the buffers once no rank can still write into them: after
+        every rank's last step (synchronise, then a barrier)."""
+        import torch.distributed as dist
+        if self.handle is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        self.lib.moe_b200_ep_destroy(self.handle)
+        self.handle = None
+
+
 class DecodeRunner:
     """Runs decode steps over a rotation of resident layers.
 
@@ -78,7 +128,7 @@ class DecodeRunner:
 
 
     def __init__(self, backend, layers, tokens: torch.Tensor, world: int = 1, rank: int = 0,
-                 max_steps: int = 4096):
+                 max_steps: int = 4096, peer_exchange: bool = True):
         self.be = backend
         self.layers = list(layers)
         self.tokens = tokens                      # [n, H] fp32 on device
@@ -96,6 +146,9 @@ class DecodeRunner:
             self.y_routed = torch.empty((1, H), dtype=torch.float32, device=self.dev)
             self.y_sh = torch.empty((1, H), dtype=torch.float32, device=self.dev)
         self.fused_ep = world > 1 and backend.ep_fused_supported(self.layers[0], world)
+        self.xchg = None
+        if self.fused_ep and peer_exchange:
+            self.xchg = PeerExchange.create(backend.lib, world, rank, 1, H)
         if world == 1:
             self.launches_per_step = backend.kernels_per_call(self.layers[0], 1)
         elif self.fused_ep:
@@ -104,7 +157,9 @@ class DecodeRunner:
             self.launches_per_step = (
                 backend.kernels_per_call(self.layers[0], world, backend.flags | _lib.NO_SHARED)
                 + backend.kernels_per_call(self.layers[0], 1, backend.flags | _lib.SHARED_ONLY))
-        self.kernel_name = ("k_decode_multi (1 launch per step)" if self.fused_ep
+        self.kernel_name = ("k_decode_multi (peer-memory dispatch and combine, 1 launch per step)"
+                            if self.xchg is not None
+                            else "k_decode_multi (1 launch per step)" if self.fused_ep
                             else "k_decode_fused (1 launch per step)" if self.launches_per_step == 1
                             else f"moe_b200_decode ({self.launches_per_step} kernels per step)")
         self.recorded = 0
@@ -123,6 +178,9 @@ class DecodeRunner:
         self.recorded = max(self.recorded, slot + 1)
         if self.world == 1:
             self.be.forward_layer_device(layer, x, y, topk_ids=self.ids[slot])
+            return
+        if self.xchg is not None:
+            self.be.decode_ep_p2p_device(layer, self.xchg, x, y, topk_ids=self.ids[slot])
             return
         if self.fused_ep:
             ep_exchange_step(
@@ -157,8 +215,9 @@ class DecodeRunner:
         self.be.decode_steps_device(tables[0], tables[1], steps, self.layers[0])
 
     def capture(self, steps: int):
-        """CUDA graph of `steps` consecutive steps (single GPU only)."""
-        if self.world > 1:
+        """CUDA graph of `steps` consecutive steps (single GPU, or
+        expert-parallel steps over peer memory, which hold no collective)."""
+        if self.world > 1 and self.xchg is None:
             return None
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
@@ -240,3 +299,6 @@ class DecodeRunner:
 
     def close(self):
         self._graph = None
+        if self.xchg is not None:
+            self.xchg.close()
+            self.xchg = None

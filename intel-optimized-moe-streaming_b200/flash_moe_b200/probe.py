@@ -6,6 +6,11 @@
     python -m flash_moe_b200.probe prefill [--tokens 4096]
         per-role wait and busy shares of the three prefill GEMM kernels
         (router, gate/up, down) on the config-2 layer.
+    torchrun --nproc-per-node N -m flash_moe_b200.probe ep [--steps 64]
+        phase timeline of one expert-parallel step with the exchange over
+        peer memory (k_decode_multi), per rank, us since the rank's first
+        CTA began the step (median / max over CTAs), and each rank's step
+        time in a CUDA graph of `steps` steps.
 
 Both enable the library's trace buffer (``moe_b200_set_trace``) for one
 launch; the numbers come from %globaltimer / clock64 stamps the kernels
@@ -28,6 +33,9 @@ DECODE_STAMPS = ["entry", "x_in", "router_rows", "router", "shared_gu", "routing
                  "topk", "gu_warps", "gate_up", "gu_barrier", "down_rows", "down", "exit",
                  "tk_sorted", "tk_rounds", "tk_softmax", "chunk0", "chunk1", "row0",
                  "act_loaded", "act_quantised", "down_item0", "down_item16"]
+EP_STAMPS = ["entry", "x_pushed", "x_in", "router", "routing_barrier", "topk_pairs",
+             "shared_gu", "gate_up", "gu_barrier", "act_quantised", "down", "combine_pushed",
+             "combine_in", "exit"]
 PREFILL_ROLES = ["producer_wait_stage", "raw_producer_wait_slot", "dequant_wait_raw",
                  "dequant_wait_stage", "mma_wait_full", "mma_wait_accumulator",
                  "epilogue_wait", "epilogue_busy"]
@@ -105,6 +113,74 @@ def probe_prefill(tokens: int = 4096) -> None:
     print("device error word:", be.prefill_errors())
 
 
+def probe_ep(steps: int = 64, copies: int = 16) -> None:
+    import os
+    from datetime import timedelta
+    import torch.distributed as dist
+    from .ep import expert_range
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+    lw = synth.make_layer(seed=0)
+    b, n = expert_range(lw.n_experts, world, rank)
+    arena = ExpertArena(dev)
+    first = arena.add_layer(0, lw, expert_begin=b, expert_count=n)
+    for c in range(1, copies):
+        arena.add_device_layer(c, first.clone())
+    be = B200ExpertBackend(arena)
+    toks = torch.from_numpy(synth.make_tokens(1000 + rank, 64, lw.hidden)).to(dev)
+    runner = DecodeRunner(be, list(range(copies)), toks, world, rank)
+    g = runner.capture(steps)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    G = _sms(dev)
+    buf = torch.zeros(G * 32, dtype=torch.int64, device=dev)
+    dist.barrier()
+    be.lib.moe_b200_set_trace(C.c_void_p(buf.data_ptr()), G)
+    try:
+        runner.step(steps + 7)
+        torch.cuda.synchronize()
+    finally:
+        be.lib.moe_b200_set_trace(None, 0)
+    bufs = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(bufs, buf)
+    held = runner.ids[(steps + 7) % runner.max_steps].cpu().numpy()
+    if rank == 0:
+        t_all = [bb.view(G, 32).cpu().numpy()[:, :len(EP_STAMPS)].astype(np.float64) for bb in bufs]
+        g0 = min(t[:, 0][t[:, 0] > 0].min() for t in t_all)
+        for r, t in enumerate(t_all):
+            t0 = t[:, 0][t[:, 0] > 0].min()
+            lo, hi = expert_range(lw.n_experts, world, r)
+            nh = len({int(e) for e in held.reshape(-1) if lo <= e < lo + hi})
+            print(f"rank {r}: entry {(t0 - g0) / 1e3:+.2f} us (globaltimer, unsynchronised "
+                  f"clocks possible), {nh} held experts selected")
+            tt = np.where(t > 0, (t - t0) / 1e3, np.nan)
+            print("  " + "  ".join(f"{name} {np.nanmedian(tt[:, i]):.2f}/{np.nanmax(tt[:, i]):.2f}"
+                                   for i, name in enumerate(EP_STAMPS)
+                                   if np.isfinite(tt[:, i]).any()))
+    us_t = torch.tensor([us], device=dev)
+    all_us = [torch.empty_like(us_t) for _ in range(world)]
+    dist.all_gather(all_us, us_t)
+    if rank == 0:
+        print("us/step in a graph of", steps, "steps, per rank:",
+              " ".join(f"{float(v.item()):.2f}" for v in all_us))
+    print(f"rank {rank} device error word: {be.device_errors()}", flush=True)
+    del g
+    runner.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(prog="python -m flash_moe_b200.probe")
     sub = ap.add_subparsers(dest="what", required=True)
@@ -113,10 +189,14 @@ def main() -> None:
     d.add_argument("--copies", type=int, default=16)
     p = sub.add_parser("prefill")
     p.add_argument("--tokens", type=int, default=4096)
+    q = sub.add_parser("ep")
+    q.add_argument("--steps", type=int, default=64)
     args = ap.parse_args()
     _lib.load()
     if args.what == "decode":
         probe_decode(args.steps, args.copies)
+    elif args.what == "ep":
+        probe_ep(args.steps)
     else:
         probe_prefill(args.tokens)
 

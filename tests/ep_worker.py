@@ -1,8 +1,9 @@
 """Worker of test_gpu_ep.py, one process per GPU under torchrun.
 
 Rank r holds experts [r*E/N, (r+1)*E/N) of the config-2 layer.  Decode:
-DecodeRunner steps (all-gather, one fused launch of the held experts and
-the own token's shared expert, reduce-scatter) for 4 tokens per rank.  Prefill: the same exchange with
+DecodeRunner steps for 4 tokens per rank, with the dispatch and combine
+inside the fused kernel over peer memory (also replayed from a CUDA graph),
+and with collectives around the kernel.  Prefill: the same exchange with
 moe_b200_prefill for 64 tokens per rank.  Rank 0 compares every rank's
 outputs with a single-GPU run of the whole layer and prints EP_OK."""
 from __future__ import annotations
@@ -42,14 +43,31 @@ def main() -> int:
     arena.add_layer(0, lw, expert_begin=begin, expert_count=count)
     be = B200ExpertBackend(arena)
 
-    # ---- decode: 4 tokens per rank, one DecodeRunner step each
+    # ---- decode: 4 tokens per rank, one DecodeRunner step each, with the
+    # exchange inside the kernel (peer memory) and around it (collectives)
     n_dec = 4
     toks = torch.from_numpy(synth.make_tokens(500 + rank, n_dec, H)).to(dev)
     runner = DecodeRunner(be, [0], toks, world, rank)
+    assert runner.xchg is not None and runner.launches_per_step == 1
     y_dec = torch.empty((n_dec, H), dtype=torch.float32, device=dev)
-    assert runner.fused_ep and runner.launches_per_step == 1
     for i in range(n_dec):
         runner.step(i, x=toks[i:i + 1], y=y_dec[i:i + 1])
+    torch.cuda.synchronize()
+    assert be.device_errors() == 0
+    # the same steps replayed from a CUDA graph (no collective inside): the
+    # last step's output is bit-identical
+    graph = runner.capture(n_dec)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert be.device_errors() == 0
+    assert torch.equal(runner.y[0], y_dec[n_dec - 1])
+    del graph
+    runner._graph = None
+    runner_c = DecodeRunner(be, [0], toks, world, rank, peer_exchange=False)
+    assert runner_c.xchg is None and runner_c.fused_ep
+    y_col = torch.empty_like(y_dec)
+    for i in range(n_dec):
+        runner_c.step(i, x=toks[i:i + 1], y=y_col[i:i + 1])
     torch.cuda.synchronize()
     assert be.device_errors() == 0
 
@@ -70,12 +88,14 @@ def main() -> int:
 
     # gather every rank's inputs and outputs on rank 0
     g = lambda t: [torch.empty_like(t) for _ in range(world)]  # noqa: E731
-    xs_dec, ys_dec, xs_pf, ys_pf = g(toks), g(y_dec), g(xp), g(y_pf)
+    xs_dec, ys_dec, ys_col, xs_pf, ys_pf = g(toks), g(y_dec), g(y_col), g(xp), g(y_pf)
     dist.all_gather(xs_dec, toks)
     dist.all_gather(ys_dec, y_dec)
+    dist.all_gather(ys_col, y_col)
     dist.all_gather(xs_pf, xp)
     dist.all_gather(ys_pf, y_pf)
     runner.close()
+    runner_c.close()
     ok = True
     if rank == 0:
         full = ExpertArena(dev)
@@ -85,17 +105,19 @@ def main() -> int:
         want = torch.empty_like(xd)
         ref.forward_layer_device(0, xd, want, flags=_lib.EXACT)
         e_dec = max_rel(torch.cat(ys_dec).cpu().numpy(), want.cpu().numpy())
+        e_col = max_rel(torch.cat(ys_col).cpu().numpy(), want.cpu().numpy())
         xa = torch.cat(xs_pf)
         want_pf = torch.empty_like(xa)
         ref.prefill_device(0, xa, want_pf)
         e_pf = max_rel(torch.cat(ys_pf).cpu().numpy(), want_pf.cpu().numpy())
         torch.cuda.synchronize()
-        print(f"ep decode max rel {e_dec:.3e}  ep prefill max rel {e_pf:.3e}", flush=True)
+        print(f"ep decode max rel {e_dec:.3e} (peer memory) {e_col:.3e} (collectives)  "
+              f"ep prefill max rel {e_pf:.3e}", flush=True)
         # decode: the fused kernel's integer dot products (activations
         # quantised to 16 bits per 256-value block) against the exact engine,
         # at the layer tolerance; prefill: the same tensor-core arithmetic
         # on both sides, summed in another order
-        ok = e_dec <= 1e-3 and e_pf <= 1e-5
+        ok = e_dec <= 1e-3 and e_col <= 1e-3 and e_pf <= 1e-5
         if ok:
             print("EP_OK", flush=True)
     dist.barrier()
