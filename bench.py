@@ -251,7 +251,7 @@ def bench_prefill(backend, layer: int, dev, peaks: dict, peak_kind: str) -> dict
                          "unit": "TFLOP/s", "frac": round(tf / peak, 4),
                          "flops_per_layer": flops,
                          "peak_source": f"{peak_kind} bf16_tflops (dense fp16 runs at the same rate)"},
-            "kernels_per_call": backend.prefill_kernels(layer), "device_error": err}
+            "kernels_per_call": backend.prefill_kernels(layer, T), "device_error": err}
 
 
 def bench_batched(dev, peaks: dict, peak_kind: str) -> dict:

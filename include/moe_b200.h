@@ -197,9 +197,10 @@ MOE_B200_API int moe_b200_prefill_workspace(const moe_b200_layer* layer, int32_t
  * and up of one format; at most 1024 held experts. */
 MOE_B200_API int moe_b200_prefill_supported(const moe_b200_layer* layer);
 
-/* Number of kernels one moe_b200_prefill call launches (8, or 3 with
+/* Number of kernels one moe_b200_prefill call of `tokens` tokens launches
+ * (8; 7 for at most 128 tokens, whose router runs on the CUDA cores; 3 with
  * MOE_B200_SHARED_ONLY). */
-MOE_B200_API int moe_b200_prefill_kernels(const moe_b200_layer* layer, int* kernels);
+MOE_B200_API int moe_b200_prefill_kernels(const moe_b200_layer* layer, int tokens, int* kernels);
 
 /* One step of a multi-step decode launch (moe_b200_decode_steps). */
 typedef struct moe_b200_step {

@@ -553,11 +553,11 @@ int moe_b200_prefill(const moe_b200_layer* L, const void* x, int32_t x_dtype, in
     return st;
 }
 
-int moe_b200_prefill_kernels(const moe_b200_layer* L, int* kernels) {
+int moe_b200_prefill_kernels(const moe_b200_layer* L, int tokens, int* kernels) {
     const int st = check_layer(L);
     if (st != ST_OK) return st;
-    if (!kernels) return ST_ARG;
-    *kernels = prefill_kernels(L);
+    if (!kernels || tokens <= 0) return ST_ARG;
+    *kernels = prefill_kernels(L, tokens);
     return ST_OK;
 }
 

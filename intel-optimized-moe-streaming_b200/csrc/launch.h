@@ -104,7 +104,7 @@ size_t prefill_workspace_bytes(const moe_b200_layer* L, int T);
 int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float* y,
                 int32_t* ids_out, float* w_out, void* ws, size_t ws_bytes, cudaStream_t s,
                 cudaError_t* ce);
-int prefill_kernels(const moe_b200_layer* L);
+int prefill_kernels(const moe_b200_layer* L, int T);
 
 // Identity-mixer transformer block around a many-token MoE call (block.cu).
 cudaError_t launch_block_prepare(const float* x, float* h, float* n, int T, int H, float eps,

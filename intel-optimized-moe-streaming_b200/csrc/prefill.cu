@@ -914,6 +914,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
 
 struct PfPrep {
     int T, H, E, n_routed, x_bf16;
+    int want_lo;            // write xl (the tensor-core router's lo half of x)
     const void* x;
     const float* gate_inp;  // [H] or null
     const float* router;    // [E x H]
@@ -941,41 +942,106 @@ __device__ __forceinline__ int pf_scale_exp(float amax) {
     return max(-126, min(126, 15 - e));
 }
 
-// one warp per token
+// one block (256 threads) per token; block 0 also clears the pair counts
 __global__ void __launch_bounds__(256) k_pf_prep_x(PfPrep p) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * 8 + warp;
-    if (t >= p.T) return;
+    __shared__ float s_red[2][8];
+    const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (t == 0)
+        for (int i = tid; i < p.n_routed; i += blockDim.x) p.counts[i] = 0;
     const size_t base = (size_t)t * p.H;
     float amax = 0.f, dot = 0.f;
-    for (int i = lane; i < p.H; i += 32) {
+    for (int i = tid; i < p.H; i += blockDim.x) {
         const float v = pf_x(p, base + i);
         amax = fmaxf(amax, fabsf(v));
         if (p.gate_inp) dot = fmaf(v, p.gate_inp[i], dot);
         p.y[base + i] = 0.f;
     }
     amax = warp_max(amax);
+    if (p.gate_inp) dot = warp_sum(dot);
+    if (lane == 0) {
+        s_red[0][warp] = amax;
+        s_red[1][warp] = dot;
+    }
+    __syncthreads();
+    amax = 0.f;
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, s_red[0][i]);
     const int k = pf_scale_exp(amax);
     const float sc = ldexpf(1.f, k);
-    for (int i = lane; i < p.H; i += 32) {
+    for (int i = tid; i < p.H; i += blockDim.x) {
         const float v = __fmul_rn(pf_x(p, base + i), sc);
         const __half hi = __float2half_rn(v);
         p.xh[base + i] = hi;
-        p.xl[base + i] = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+        if (p.want_lo) p.xl[base + i] = __float2half_rn(__fsub_rn(v, __half2float(hi)));
     }
-    if (p.gate_inp) dot = warp_sum(dot);
-    if (lane == 0) {
+    if (tid == 0) {
         p.xs_inv[t] = ldexpf(1.f, -k);
-        if (p.gate_inp) p.sg[t] = shared_sigmoid(dot);
+        if (p.gate_inp) {
+            // the shared-gate dot in a fixed order: warps 0..7
+            float d = 0.f;
+            for (int i = 0; i < 8; ++i) d += s_red[1][i];
+            p.sg[t] = shared_sigmoid(d);
+        }
     }
 }
 
-// one block per router row; block 0 also clears the pair counts
+// Router logits of a few tokens on the CUDA cores, in fp32: block (x, y)
+// computes the partial dots of experts [32x, 32x + 32) with every token over
+// the hidden slice [128y, 128y + 128); k_pf_topk adds the H/128 partials in
+// slice order (deterministic).  For T <= kPfSmallRouterT, where the
+// tensor-core router would run on a handful of SMs.
+constexpr int kPfSmallRouterT = 128;
+constexpr int kRsE = 32, kRsK = 128, kRsT = 32;
+
+__global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, float* part) {
+    __shared__ __align__(16) float sR[kRsE][kRsK + 4];
+    __shared__ __align__(16) float sX[kRsT][kRsK + 4];
+    const int e0 = blockIdx.x * kRsE, k0 = blockIdx.y * kRsK, tid = threadIdx.x;
+    for (int i = tid; i < kRsE * kRsK / 4; i += 256) {
+        const int r = i / (kRsK / 4), c = (i % (kRsK / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e0 + r < p.E) v = *reinterpret_cast<const float4*>(p.router + (size_t)(e0 + r) * p.H + k0 + c);
+        *reinterpret_cast<float4*>(&sR[r][c]) = v;
+    }
+    const int el = tid >> 3, tg = tid & 7;  // expert e0 + el, tokens t0 + tg + 8 j
+    for (int t0 = 0; t0 < p.T; t0 += kRsT) {
+        __syncthreads();
+        for (int i = tid; i < kRsT * kRsK / 4; i += 256) {
+            const int r = i / (kRsK / 4), c = (i % (kRsK / 4)) * 4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t0 + r < p.T) {
+                const size_t at = (size_t)(t0 + r) * p.H + k0 + c;
+                v = make_float4(pf_x(p, at), pf_x(p, at + 1), pf_x(p, at + 2), pf_x(p, at + 3));
+            }
+            *reinterpret_cast<float4*>(&sX[r][c]) = v;
+        }
+        __syncthreads();
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int k = 0; k < kRsK; k += 4) {
+            const float4 r = *reinterpret_cast<const float4*>(&sR[el][k]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float4 xv = *reinterpret_cast<const float4*>(&sX[tg + 8 * j][k]);
+                acc[j] = fmaf(r.x, xv.x, acc[j]);
+                acc[j] = fmaf(r.y, xv.y, acc[j]);
+                acc[j] = fmaf(r.z, xv.z, acc[j]);
+                acc[j] = fmaf(r.w, xv.w, acc[j]);
+            }
+        }
+        if (e0 + el < p.E) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int t = t0 + tg + 8 * j;
+                if (t < p.T) part[((size_t)blockIdx.y * p.T + t) * p.E + e0 + el] = acc[j];
+            }
+        }
+    }
+}
+
+// one block per router row
 __global__ void __launch_bounds__(256) k_pf_prep_router(PfPrep p) {
     __shared__ float s_red[8];
     const int e = blockIdx.x;
-    if (e == 0)
-        for (int i = threadIdx.x; i < p.n_routed; i += blockDim.x) p.counts[i] = 0;
     const float* r = p.router + (size_t)e * p.H;
     float amax = 0.f;
     for (int i = threadIdx.x; i < p.H; i += blockDim.x) amax = fmaxf(amax, fabsf(r[i]));
@@ -997,7 +1063,10 @@ __global__ void __launch_bounds__(256) k_pf_prep_router(PfPrep p) {
 
 struct PfRoute {
     int T, E, K, expert_begin, n_routed;
-    const float* logits;
+    int KS;                // > 0: logits = sum of KS partial slices of `part` (+ bias)
+    const float* part;     // [KS][T][E]
+    const float* bias;     // [E] or null (KS > 0 only)
+    float* logits;
     int32_t* ids;
     float* w;
     int32_t* ids_out;
@@ -1012,6 +1081,15 @@ struct PfRoute {
 __global__ void __launch_bounds__(32) k_pf_topk(PfRoute p) {
     extern __shared__ float s_sc[];
     const int t = blockIdx.x, lane = threadIdx.x;
+    if (p.KS > 0) {
+        for (int e = lane; e < p.E; e += 32) {
+            float v = 0.f;
+            for (int q = 0; q < p.KS; ++q) v += __ldcg(p.part + ((size_t)q * p.T + t) * p.E + e);
+            if (p.bias) v = __fadd_rn(v, p.bias[e]);
+            p.logits[(size_t)t * p.E + e] = v;
+        }
+        __syncwarp();
+    }
     int32_t* ids = p.ids + (size_t)t * p.K;
     float* w = p.w + (size_t)t * p.K;
     if (p.E <= 256) {
@@ -1154,8 +1232,14 @@ bool prefill_supported(const moe_b200_layer* L, int flags) {
 }
 
 struct PfWs {
-    size_t counts, xs_inv, sg, xh, xl, rh, rl, rs_inv, logits, ids, w, ptok, pw, act, xperm, total;
+    size_t counts, xs_inv, sg, xh, xl, rh, rl, rs_inv, logits, part, ids, w, ptok, pw, act, xperm,
+        total;
 };
+
+// The CUDA-core router for few tokens (needs 16-byte aligned router rows).
+static bool pf_small_router(const moe_b200_layer* L, int T) {
+    return T <= kPfSmallRouterT && ((uintptr_t)L->router & 15u) == 0;
+}
 
 static PfWs pf_ws(const moe_b200_layer* L, int T) {
     const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate
@@ -1173,6 +1257,7 @@ static PfWs pf_ws(const moe_b200_layer* L, int T) {
     w.rl = s.take(E * H * 2);
     w.rs_inv = s.take(E * 4);
     w.logits = s.take((size_t)T * E * 4);
+    w.part = s.take(pf_small_router(L, T) ? (size_t)(H / kRsK) * T * E * 4 : 0);
     w.ids = s.take((size_t)T * K * 4);
     w.w = s.take((size_t)T * K * 4);
     w.ptok = s.take((size_t)T * K * 4);
@@ -1192,20 +1277,30 @@ static size_t pf_ctrl_bytes(const PfParams& p) {
            (size_t)4 * 256 * 4 + (size_t)2 * (p.n_routed + 1) * 4;
 }
 
-// Stages (3, else 2) and raw slots (up to 4) that fit the shared memory.
+// Stages (up to 6) and raw slots (up to 4) that fit the shared memory: the
+// most stages that leave room for three raw slots, else two stages.  Few
+// tokens make small stages (the B rows of a stage are the unit's columns),
+// so small calls get a deeper pipeline.
 static bool pf_fit(PfParams& p) {
-    for (int st = 3; st >= 2; --st) {
+    for (int st = 6; st >= 2; --st) {
         p.stages = st;
         p.raw_slots = 0;
         const size_t used = 1024 + (size_t)st * p.stage_bytes + pf_ctrl_bytes(p) + 64;
         if (used >= 232448) continue;
         const int r = (int)((232448 - used) / p.raw_slot_bytes);
-        if (r >= 2 || st == 2) {
+        if (r >= 3 || st == 2) {
             p.raw_slots = r > 4 ? 4 : r;
             return p.raw_slots >= 1;
         }
     }
     return false;
+}
+
+// B rows a stage holds: a unit has at most min(T, kPfMaxN) columns (a token
+// selects an expert at most once), rounded to the MMA's 16.
+static uint32_t pf_stage_cols(int T) {
+    const int n = (T + 15) & ~15;
+    return (uint32_t)(n < kPfMaxN ? n : kPfMaxN);
 }
 
 template <int MODE>
@@ -1261,7 +1356,9 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     pp.sg = reinterpret_cast<float*>(base + W.sg);
     pp.y = y;
     pp.counts = reinterpret_cast<int32_t*>(base + W.counts);
-    k_pf_prep_x<<<(T + 7) / 8, 256, 0, s>>>(pp);
+    const bool small_router = routed && pf_small_router(L, T);
+    pp.want_lo = routed && !small_router;
+    k_pf_prep_x<<<T, 256, 0, s>>>(pp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return pf_fail(ce, e);
 
@@ -1302,7 +1399,14 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     rp.pair_tok = const_cast<int32_t*>(gp.pair_tok);
     rp.pair_w = const_cast<float*>(gp.pair_w);
 
-    if (routed) {
+    if (routed && small_router) {
+        float* part = reinterpret_cast<float*>(base + W.part);
+        k_pf_router_small<<<dim3((E + kRsE - 1) / kRsE, H / kRsK), 256, 0, s>>>(pp, part);
+        if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
+        rp.KS = H / kRsK;
+        rp.part = part;
+        rp.bias = L->router_bias;
+    } else if (routed) {
         k_pf_prep_router<<<E, 256, 0, s>>>(pp);
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
         // router logits
@@ -1322,6 +1426,8 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
         const int units = ((E + 127) / 128) * ((T + kPfRouterN - 1) / kPfRouterN);
         if ((e = pf_launch_gemm<PF_ROUTER>(rp2, units < sms ? units : sms, s)) != cudaSuccess)
             return pf_fail(ce, e);
+    }
+    if (routed) {
         const size_t tsm = E > 256 ? (size_t)E * 5 : 0;
         k_pf_topk<<<T, 32, tsm, s>>>(rp);
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
@@ -1370,7 +1476,7 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
         }
         if (!ok) return ST_INTERNAL;
         g.a_bytes = 16384;
-        g.stage_bytes = g.a_bytes + kPfMaxN * 128;
+        g.stage_bytes = g.a_bytes + pf_stage_cols(T) * 128;
         g.raw_slot_bytes = 64 * wmax_gu;
         if (!pf_fit(g)) return ST_INTERNAL;
         if ((e = pf_launch_gemm<PF_GATEUP>(g, sms, s)) != cudaSuccess) return pf_fail(ce, e);
@@ -1402,7 +1508,7 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
         }
         if (!ok) return ST_INTERNAL;
         g.a_bytes = 16384;
-        g.stage_bytes = g.a_bytes + kPfMaxN * 128;
+        g.stage_bytes = g.a_bytes + pf_stage_cols(T) * 128;
         g.raw_slot_bytes = 128 * wmax_dn;
         if (!pf_fit(g)) return ST_INTERNAL;
         if ((e = pf_launch_gemm<PF_DOWN>(g, sms, s)) != cudaSuccess) return pf_fail(ce, e);
@@ -1410,9 +1516,10 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     return ST_OK;
 }
 
-int prefill_kernels(const moe_b200_layer* L) {
+int prefill_kernels(const moe_b200_layer* L, int T) {
     const bool routed = !(L->flags & MOE_B200_SHARED_ONLY);
-    return routed ? 8 : 3;
+    if (!routed) return 3;
+    return pf_small_router(L, T) ? 7 : 8;
 }
 
 }  // namespace moeb200

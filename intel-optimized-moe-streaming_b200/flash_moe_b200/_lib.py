@@ -82,7 +82,7 @@ def _bind(lib: C.CDLL) -> None:
         "moe_b200_block_prepare": (i, [vp, vp, vp, C.c_int32, C.c_int32, C.c_float, vp]),
         "moe_b200_block_finish": (i, [vp, vp, vp, C.c_int32, C.c_int32, vp]),
         "moe_b200_prefill_supported": (i, [C.POINTER(Layer)]),
-        "moe_b200_prefill_kernels": (i, [C.POINTER(Layer), C.POINTER(C.c_int)]),
+        "moe_b200_prefill_kernels": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_int)]),
         "moe_b200_dequant": (i, [i, vp, vp, i64, i, vp]),
         "moe_b200_expert_noalloc": (i, [i, vp, i64] * 3 + [vp, i, i, vp, i, vp]),
         "moe_b200_last_cuda_error": (i, []),

@@ -141,11 +141,12 @@ class B200ExpertBackend:
             "moe_b200_workspace_error")
         return err.value
 
-    def prefill_kernels(self, layer: int, flags: int | None = None) -> int:
-        """Kernels one prefill_device call launches (from the library)."""
+    def prefill_kernels(self, layer: int, tokens: int, flags: int | None = None) -> int:
+        """Kernels one prefill_device call of `tokens` tokens launches (from
+        the library)."""
         s = self.store.layer(layer).with_flags(self.flags if flags is None else flags)
         n = C.c_int(0)
-        _lib.check(self.lib.moe_b200_prefill_kernels(C.byref(s), C.byref(n)),
+        _lib.check(self.lib.moe_b200_prefill_kernels(C.byref(s), tokens, C.byref(n)),
                    "moe_b200_prefill_kernels")
         return n.value
 

@@ -210,5 +210,7 @@ def test_prefill_kernel_count():
     be = _backend(lw)
     s = be.store.layer(0).with_flags(0)
     n = C.c_int(0)
-    assert be.lib.moe_b200_prefill_kernels(C.byref(s), C.byref(n)) == 0
+    assert be.lib.moe_b200_prefill_kernels(C.byref(s), 4096, C.byref(n)) == 0
     assert n.value == 8
+    assert be.lib.moe_b200_prefill_kernels(C.byref(s), 64, C.byref(n)) == 0
+    assert n.value == 7
