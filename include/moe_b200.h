@@ -143,6 +143,28 @@ MOE_B200_API int moe_b200_decode(const moe_b200_layer* layer, const float* x, in
                     float* y, int32_t* topk_ids, float* topk_weights,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Bytes of workspace moe_b200_decode_host needs for `max_tokens` tokens:
+ * the decode workspace plus device staging rows for x, y and the routing. */
+MOE_B200_API int moe_b200_decode_host_workspace(const moe_b200_layer* layer, int32_t max_tokens,
+                                   size_t* bytes);
+
+/* moe_b200_decode for a caller whose token rows and results live in HOST
+ * memory, synchronous like the reference's ctypes entry points: copies x
+ * ([tokens x H] fp32) to the workspace's staging rows, decodes on `stream`,
+ * copies y (and topk_ids / topk_weights when not NULL) back to the host
+ * pointers and waits for the stream.  Pinned host memory makes the copies
+ * asynchronous DMA; pageable memory works, staged by the driver.  Returns
+ * moe_b200_decode's status, or -9 when a bounded device wait gave up (the
+ * workspace error word, read and cleared here).  The workspace is device
+ * memory of moe_b200_decode_host_workspace bytes, zeroed once with
+ * moe_b200_workspace_init.  This is the host-side form of run_moe_layer
+ * (src/flash_moe/moe_layer.py:39-107), whose activations and outputs are
+ * numpy arrays: one call per layer instead of one moe_quant_expert call per
+ * selected expert (src/flash_moe/native_expert.py:23-37). */
+MOE_B200_API int moe_b200_decode_host(const moe_b200_layer* layer, const float* x, int32_t tokens,
+                         float* y, int32_t* topk_ids, float* topk_weights,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* Zero the workspace's control words (its first 256 bytes) on `stream`.
  * Call once after allocating a decode workspace; the decode kernels leave
  * them zero again when they finish. */

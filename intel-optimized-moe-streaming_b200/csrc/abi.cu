@@ -348,6 +348,106 @@ int moe_b200_decode_workspace(const moe_b200_layer* L, int32_t max_tokens, size_
     return ST_OK;
 }
 
+// Staging rows of moe_b200_decode_host after the decode workspace.
+struct HostWs {
+    size_t x, y, ids, w, total;
+};
+
+static HostWs host_ws(const moe_b200_layer* L, int T) {
+    Stager s;
+    s.used = align_up(decode_ws(L, T).total);
+    HostWs h;
+    h.x = s.take((size_t)T * L->hidden * 4);
+    h.y = s.take((size_t)T * L->hidden * 4);
+    h.ids = s.take((size_t)T * L->top_k * 4);
+    h.w = s.take((size_t)T * L->top_k * 4);
+    h.total = s.used;
+    return h;
+}
+
+int moe_b200_decode_host_workspace(const moe_b200_layer* L, int32_t max_tokens, size_t* bytes) {
+    const int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (max_tokens < 1 || !bytes) return ST_ARG;
+    *bytes = host_ws(L, max_tokens).total;
+    return ST_OK;
+}
+
+// True when the device reads and writes `p` at the same address (pinned,
+// mapped host memory under unified addressing).
+static bool device_visible(const void* p) {
+    if (!p) return true;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost && a.devicePointer == p;
+}
+
+int moe_b200_decode_host(const moe_b200_layer* L, const float* x, int32_t T, float* y,
+                         int32_t* topk_ids, float* topk_weights, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+    int st = check_layer(L);
+    if (st != ST_OK) return st;
+    if (T < 1 || !x || !y || !workspace) return ST_ARG;
+    if ((uintptr_t)workspace & 255u) return ST_ALIGN;
+    const HostWs hw = host_ws(L, T);
+    if (workspace_bytes < hw.total) return ST_WORKSPACE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    char* base = static_cast<char*>(workspace);
+    float* xd = reinterpret_cast<float*>(base + hw.x);
+    float* yd = reinterpret_cast<float*>(base + hw.y);
+    int32_t* idd = topk_ids ? reinterpret_cast<int32_t*>(base + hw.ids) : nullptr;
+    float* wd = topk_weights ? reinterpret_cast<float*>(base + hw.w) : nullptr;
+    const size_t xb = (size_t)T * L->hidden * 4, kb = (size_t)T * L->top_k * 4;
+    // the error word comes back through a pinned per-thread word, so that
+    // all copies stay asynchronous until the one synchronisation
+    static thread_local int* word_h = nullptr;
+    cudaError_t e;
+    if (!word_h && (e = cudaMallocHost(reinterpret_cast<void**>(&word_h), sizeof(int))) != cudaSuccess) {
+        word_h = nullptr;
+        return fail(e, ST_CUDA);
+    }
+    *word_h = 0;
+    // one token, pinned buffers: the fused kernel writes the result, the
+    // routing and the error word straight to host memory (one graph launch,
+    // no copy-engine transfers)
+    if (T == 1 && fused_supported(L, T, L->flags) && ((uintptr_t)x & 15u) == 0 &&
+        device_visible(x) && device_visible(y) && device_visible(topk_ids) &&
+        device_visible(topk_weights) && device_visible(word_h)) {
+        bool launched = false;
+        e = launch_decode_fused_host(L, L->flags, x, xd, y, topk_ids, topk_weights, word_h,
+                                     workspace, s, &launched);
+        if (e != cudaSuccess) return fail(e, ST_CUDA);
+        if (launched) {
+            e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess) return fail(e, ST_CUDA);
+            return *word_h;
+        }
+    }
+    e = cudaMemcpyAsync(xd, x, xb, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    st = moe_b200_decode(L, xd, T, yd, idd, wd, workspace, hw.x, stream);
+    if (st != ST_OK) {
+        cudaStreamSynchronize(s);
+        return st;
+    }
+    e = cudaMemcpyAsync(y, yd, xb, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && idd) e = cudaMemcpyAsync(topk_ids, idd, kb, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && wd) e = cudaMemcpyAsync(topk_weights, wd, kb, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(word_h, base + 32, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    const int word = *word_h;
+    if (word != 0) {
+        e = cudaMemsetAsync(base + 32, 0, sizeof(int), s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        return e == cudaSuccess ? word : fail(e, ST_CUDA);
+    }
+    return ST_OK;
+}
+
 int moe_b200_decode(const moe_b200_layer* L, const float* x, int32_t T, float* y,
                     int32_t* topk_ids, float* topk_weights, void* workspace,
                     size_t workspace_bytes, void* stream) {

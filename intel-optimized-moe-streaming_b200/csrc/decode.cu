@@ -54,6 +54,8 @@ struct FusedParams {
     float* act_s;            // [2][Imax]
     float* sg;               // [2]
     uint64_t* trace;         // [G x 32] phase timestamps of step n_steps / 2 (ns), or null
+    int* err_out;            // null, or a host-visible word that receives (and clears) the
+                             // error word at exit
     int G;
     int with_shared;
     int max_router_rows, max_sgu_rows, max_out_rows, max_rgu_rows;
@@ -505,6 +507,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             p.ctr[C_GATEUP] = 0;
             p.ctr[C_DONE] = 0;
             p.ctr[C_EXIT] = 0;
+            if (p.err_out) {
+                *p.err_out = atomicExch(reinterpret_cast<int*>(p.ctr + C_ERROR), 0);
+                __threadfence_system();
+            }
             __threadfence();
         }
     }
@@ -599,22 +605,24 @@ uint64_t* trace_buffer(int* capacity_ctas) {
     return tl_trace;
 }
 
-// One cooperative launch of the fused kernel: a single step (steps null:
-// the token x through layer *L) or n_steps steps from the device tables.
-static cudaError_t fused_launch(const moe_b200_layer* L, int flags, const float* x, float* y,
-                                int32_t* ids_out, float* w_out, const moe_b200_layer* layers,
-                                const moe_b200_step* steps, int n_steps, float eps, void* ws,
-                                cudaStream_t stream, bool* launched) {
-    *launched = false;
+using FusedFn = void (*)(FusedParams);
+
+// Parameters and kernel instance of one launch of the fused kernel: a
+// single step (steps null: the token x through layer *L) or n_steps steps
+// from the device tables.  False when the layer does not fit the plan.
+static cudaError_t fused_prepare(const moe_b200_layer* L, int flags, const float* x, float* y,
+                                 int32_t* ids_out, float* w_out, const moe_b200_layer* layers,
+                                 const moe_b200_step* steps, int n_steps, float eps, void* ws,
+                                 FusedParams& p, FusedFn& fn, bool* ok) {
+    *ok = false;
     const bool shared = L->shared_intermediate > 0 && !(flags & MOE_B200_NO_SHARED);
-    FusedParams p{};
+    p = FusedParams{};
     p.L = *L;
     const int G = sm_count();
     if (!fused_plan(L, shared, G, p)) return cudaSuccess;
-    using KernelFn = void (*)(FusedParams);
     struct Instance {
         int gu, dn, sgu, sdn;
-        KernelFn fn;
+        FusedFn fn;
     };
     static const Instance kInstances[] = {
         {Q3_K, Q4_K, Q8_0, Q8_0, k_decode_fused<Q3_K, Q4_K, Q8_0, Q8_0>},
@@ -645,6 +653,7 @@ static cudaError_t fused_launch(const moe_b200_layer* L, int flags, const float*
         if (e != cudaSuccess) return e;
         attr_set[dev][pick] = true;
     }
+    fn = kInstances[pick].fn;
     char* base = static_cast<char*>(ws);
     p.x = x;
     p.y = y;
@@ -665,9 +674,23 @@ static cudaError_t fused_launch(const moe_b200_layer* L, int flags, const float*
     off += align_up((size_t)2 * Imax * 4);
     p.sg = reinterpret_cast<float*>(base + off);
     p.trace = (tl_trace && tl_trace_cap >= G) ? tl_trace : nullptr;
+    *ok = true;
+    return cudaSuccess;
+}
 
+static cudaError_t fused_launch(const moe_b200_layer* L, int flags, const float* x, float* y,
+                                int32_t* ids_out, float* w_out, const moe_b200_layer* layers,
+                                const moe_b200_step* steps, int n_steps, float eps, void* ws,
+                                cudaStream_t stream, bool* launched) {
+    *launched = false;
+    FusedParams p;
+    FusedFn fn = nullptr;
+    bool ok = false;
+    cudaError_t e = fused_prepare(L, flags, x, y, ids_out, w_out, layers, steps, n_steps, eps, ws,
+                                  p, fn, &ok);
+    if (e != cudaSuccess || !ok) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(G);
+    cfg.gridDim = dim3(p.G);
     cfg.blockDim = dim3(kFusedThreads);
     cfg.dynamicSmemBytes = p.total;
     cfg.stream = stream;
@@ -676,7 +699,99 @@ static cudaError_t fused_launch(const moe_b200_layer* L, int flags, const float*
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kInstances[pick].fn, p);
+    e = cudaLaunchKernelEx(&cfg, fn, p);
+    if (e == cudaSuccess) *launched = true;
+    return e;
+}
+
+// x rows from host memory the device can read (pinned, mapped) into device
+// staging rows: one 16-byte word per thread.
+__global__ void __launch_bounds__(256) k_copy_in(const float4* __restrict__ src,
+                                                 float4* __restrict__ dst, int n4) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n4) dst[i] = src[i];
+}
+
+// Per-thread graph of (copy-in kernel -> fused kernel) for synchronous
+// single-token calls with host buffers: a graph launch reaches the GPU
+// sooner than a direct cooperative launch.  The nodes' parameters are
+// updated on every call; the graph is rebuilt when the device, kernel
+// instance or shared-memory size changes.  (A thread's last graph is left to
+// the driver's clean-up at process exit.)
+struct HostGraph {
+    int dev = -1;
+    FusedFn fn = nullptr;
+    uint32_t smem = 0;
+    int G = 0, n4 = 0;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaGraphNode_t copy = nullptr, fused = nullptr;
+    void reset() {
+        if (ge) cudaGraphExecDestroy(ge);
+        if (g) cudaGraphDestroy(g);
+        *this = HostGraph{};
+    }
+};
+
+cudaError_t launch_decode_fused_host(const moe_b200_layer* L, int flags, const float* x_host,
+                                     float* x_stage, float* y_host, int32_t* ids_host,
+                                     float* w_host, int* err_host, void* ws, cudaStream_t stream,
+                                     bool* launched) {
+    *launched = false;
+    FusedParams p;
+    FusedFn fn = nullptr;
+    bool ok = false;
+    cudaError_t e = fused_prepare(L, flags, x_stage, y_host, ids_host, w_host, nullptr, nullptr, 1,
+                                  0.f, ws, p, fn, &ok);
+    if (e != cudaSuccess || !ok) return e;
+    p.err_out = err_host;
+    static thread_local HostGraph hg;
+    int dev = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    const int n4 = L->hidden / 4;
+    const float4* src = reinterpret_cast<const float4*>(x_host);
+    float4* dst = reinterpret_cast<float4*>(x_stage);
+    void* cargs[] = {&src, &dst, const_cast<int*>(&n4)};
+    cudaKernelNodeParams cp = {};
+    cp.func = reinterpret_cast<void*>(k_copy_in);
+    cp.gridDim = dim3((n4 + 255) / 256);
+    cp.blockDim = dim3(256);
+    cp.kernelParams = cargs;
+    void* fargs[] = {&p};
+    cudaKernelNodeParams fp = {};
+    fp.func = reinterpret_cast<void*>(fn);
+    fp.gridDim = dim3(p.G);
+    fp.blockDim = dim3(kFusedThreads);
+    fp.sharedMemBytes = p.total;
+    fp.kernelParams = fargs;
+    const bool same = hg.ge && hg.dev == dev && hg.fn == fn && hg.smem == p.total && hg.G == p.G &&
+                      hg.n4 == n4;
+    if (same) {
+        e = cudaGraphExecKernelNodeSetParams(hg.ge, hg.copy, &cp);
+        if (e == cudaSuccess) e = cudaGraphExecKernelNodeSetParams(hg.ge, hg.fused, &fp);
+    } else {
+        hg.reset();
+        e = cudaGraphCreate(&hg.g, 0);
+        if (e == cudaSuccess) e = cudaGraphAddKernelNode(&hg.copy, hg.g, nullptr, 0, &cp);
+        if (e == cudaSuccess) e = cudaGraphAddKernelNode(&hg.fused, hg.g, &hg.copy, 1, &fp);
+        if (e == cudaSuccess) {
+            cudaLaunchAttributeValue v = {};
+            v.cooperative = 1;
+            e = cudaGraphKernelNodeSetAttribute(hg.fused, cudaLaunchAttributeCooperative, &v);
+        }
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&hg.ge, hg.g, 0);
+        if (e != cudaSuccess) {
+            hg.reset();
+            return e;
+        }
+        hg.dev = dev;
+        hg.fn = fn;
+        hg.smem = p.total;
+        hg.G = p.G;
+        hg.n4 = n4;
+    }
+    if (e != cudaSuccess) return e;
+    e = cudaGraphLaunch(hg.ge, stream);
     if (e == cudaSuccess) *launched = true;
     return e;
 }

@@ -75,6 +75,14 @@ cudaError_t launch_decode_fused(const moe_b200_layer* L, int flags, const float*
                                 bool* launched);
 // n_steps single-token steps from device tables in one launch (every layer
 // shares L0's shapes and block formats; L0's flags apply to all).
+// Single-token fused decode for host buffers the device can read and write
+// (pinned): a graph of a copy kernel (x_host -> x_stage, device staging
+// rows) and the fused kernel, which writes y, the routing and the error word
+// (err_host, cleared on the device) straight to host memory.
+cudaError_t launch_decode_fused_host(const moe_b200_layer* L, int flags, const float* x_host,
+                                     float* x_stage, float* y_host, int32_t* ids_host,
+                                     float* w_host, int* err_host, void* ws, cudaStream_t stream,
+                                     bool* launched);
 cudaError_t launch_decode_steps(const moe_b200_layer* L0, const moe_b200_layer* layers,
                                 const moe_b200_step* steps, int n_steps, float eps, void* ws,
                                 cudaStream_t stream, bool* launched);

@@ -67,6 +67,10 @@ def _bind(lib: C.CDLL) -> None:
         "moe_b200_decode_workspace": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_size_t)]),
         "moe_b200_decode_kernels": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_int)]),
         "moe_b200_decode": (i, [C.POINTER(Layer), vp, C.c_int32, vp, vp, vp, vp, C.c_size_t, vp]),
+        "moe_b200_decode_host_workspace": (i, [C.POINTER(Layer), C.c_int32,
+                                               C.POINTER(C.c_size_t)]),
+        "moe_b200_decode_host": (i, [C.POINTER(Layer), vp, C.c_int32, vp, vp, vp, vp, C.c_size_t,
+                                     vp]),
         "moe_b200_prefill": (i, [C.POINTER(Layer), vp, C.c_int32, C.c_int32, vp, vp, vp, vp,
                                  C.c_size_t, vp]),
         "moe_b200_prefill_workspace": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_size_t)]),

@@ -85,6 +85,32 @@ class B200ExpertBackend:
             cache[self.device] = ws
         return ws
 
+    def _pinned(self, tokens: int, hidden: int, k: int):
+        """This thread's pinned host rows (x, y, ids, weights) for `tokens`."""
+        cache = getattr(self._tls, "pinned", None)
+        if cache is None or cache[0].shape[0] < tokens or cache[0].shape[1] != hidden \
+                or cache[2].shape[1] != k:
+            cache = self._tls.pinned = (
+                torch.empty((tokens, hidden), dtype=torch.float32).pin_memory(),
+                torch.empty((tokens, hidden), dtype=torch.float32).pin_memory(),
+                torch.empty((tokens, k), dtype=torch.int32).pin_memory(),
+                torch.empty((tokens, k), dtype=torch.float32).pin_memory())
+        return tuple(c[:tokens] for c in cache)
+
+    def _host_workspace(self, dl, tokens: int) -> torch.Tensor:
+        cache = getattr(self._tls, "host_ws", None)
+        if cache is None:
+            cache = self._tls.host_ws = {}
+        need = C.c_size_t(0)
+        _lib.check(self.lib.moe_b200_decode_host_workspace(C.byref(dl.struct), tokens,
+                                                           C.byref(need)),
+                   "moe_b200_decode_host_workspace")
+        ws = cache.get(self.device)
+        if ws is None or ws.numel() < need.value:
+            ws = torch.zeros(max(need.value, 256), dtype=torch.uint8, device=self.device)
+            cache[self.device] = ws
+        return ws
+
     def _prefill_workspace(self, s, tokens: int) -> torch.Tensor:
         cache = getattr(self._tls, "pf_ws", None)
         if cache is None:
@@ -191,6 +217,41 @@ class B200ExpertBackend:
             topk_weights.data_ptr() if topk_weights is not None else None,
             ws.data_ptr(), ws.numel(), stream.cuda_stream)
         _lib.check(st, "moe_b200_decode")
+
+    def forward_layer_host(self, layer: int, x, y, topk_ids=None, topk_weights=None,
+                           flags: int | None = None, stream=None) -> None:
+        """Synchronous layer decode with host buffers (``moe_b200_decode_host``):
+        x and y fp32 [T, H], topk_ids int32 / topk_weights fp32 [T, K] when
+        given -- numpy arrays or CPU tensors, pinned for asynchronous copies."""
+        def host_ptr(a, dtype, shape, what):
+            if a is None:
+                return None
+            if isinstance(a, torch.Tensor):
+                ok = (a.device.type == "cpu" and a.is_contiguous() and a.dtype == dtype[1]
+                      and tuple(a.shape) == shape)
+                ptr = a.data_ptr()
+            else:
+                ok = (isinstance(a, np.ndarray) and a.flags.c_contiguous and a.dtype == dtype[0]
+                      and a.shape == shape)
+                ptr = a.ctypes.data if ok else 0
+            if not ok:
+                raise ValueError(f"{what}: contiguous host {dtype[0]} array of shape {shape} needed")
+            return ptr
+        dl = self.store.layer(layer)
+        t, h = (x.shape[0], x.shape[1]) if len(x.shape) == 2 else (0, 0)
+        k = dl.weights.top_k
+        f32, i32 = (np.float32, torch.float32), (np.int32, torch.int32)
+        xp = host_ptr(x, f32, (t, dl.weights.hidden), "x")
+        yp = host_ptr(y, f32, (t, dl.weights.hidden), "y")
+        ip = host_ptr(topk_ids, i32, (t, k), "topk_ids")
+        wp = host_ptr(topk_weights, f32, (t, k), "topk_weights")
+        s = dl.with_flags(self.flags if flags is None else flags)
+        ws = self._host_workspace(dl, t)
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        st = self.lib.moe_b200_decode_host(C.byref(s), xp, t, yp, ip, wp, ws.data_ptr(),
+                                           ws.numel(), stream.cuda_stream)
+        _lib.check(st, "moe_b200_decode_host")
 
     def ep_fused_supported(self, layer: int, tokens: int) -> bool:
         """True when ``decode_ep_device`` takes `tokens` gathered tokens of
@@ -322,10 +383,22 @@ class B200ExpertBackend:
         x = np.ascontiguousarray(activations, dtype=np.float32)
         squeeze = x.ndim == 1
         x = x.reshape(-1, self.store.layer(layer).weights.hidden)
+        k = self.store.layer(layer).weights.top_k
+        if not (x.shape[0] >= self.prefill_min_tokens and self.prefill_supported(layer)):
+            # decode: one synchronous call through this thread's pinned
+            # staging rows (the single-token call then needs no copy engine)
+            t = x.shape[0]
+            xp, yp, ip, wp = self._pinned(t, x.shape[1], k)
+            xp.numpy()[:] = x
+            with torch.cuda.device(self.device):
+                self.forward_layer_host(layer, xp, yp, ip, wp)
+            y = yp.numpy().copy()
+            routing = (ip.numpy().copy(), wp.numpy().copy())
+            y = y[0] if squeeze else y
+            return (y, routing) if return_routing else y
         with torch.cuda.device(self.device):
             xd = torch.from_numpy(x).to(self.device, non_blocking=False)
             yd = torch.empty_like(xd)
-            k = self.store.layer(layer).weights.top_k
             ids = torch.empty((x.shape[0], k), dtype=torch.int32, device=self.device)
             w = torch.empty((x.shape[0], k), dtype=torch.float32, device=self.device)
             if x.shape[0] >= self.prefill_min_tokens and self.prefill_supported(layer):

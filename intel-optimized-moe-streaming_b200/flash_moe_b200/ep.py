@@ -254,9 +254,12 @@ class DecodeRunner:
     # ------------------------------------------------------------------ e2e
 
     def e2e(self, steps: int, warmup: int) -> dict:
-        """The same steps through host memory: each step copies its token from
-        pinned host memory, decodes, and reads the result back to pinned
-        host memory, synchronising like a caller that consumes the result."""
+        """The same steps through host memory: each step's token starts in
+        pinned host memory and its result ends there, synchronised like a
+        caller that consumes the result.  One GPU: one ``moe_b200_decode_host``
+        call per step (the device reads the token and writes the result
+        through the pinned mapping); expert-parallel: host copies around the
+        rank's exchange step."""
         H = self.lw.hidden
         n = self.tokens.shape[0]
         host_x = torch.empty((n, H), dtype=torch.float32).pin_memory()
@@ -266,6 +269,11 @@ class DecodeRunner:
         stream = torch.cuda.current_stream(self.dev)
 
         def one(i):
+            if self.world == 1:
+                # one synchronous library call: pinned token in, result out
+                self.be.forward_layer_host(self.layers[i % len(self.layers)],
+                                           host_x[i % n].view(1, -1), host_y)
+                return
             xd.copy_(host_x[i % n].view(1, -1), non_blocking=True)
             self.step(i, x=xd)
             host_y.copy_(self.y, non_blocking=True)

@@ -128,3 +128,47 @@ def test_backend_per_expert_forward_matches_oracle(oracle):
         _, want = oracle.expert(lw.expert(3), lw.kinds, xs[t], lw.hidden, lw.inter, 0)
         assert O.max_relative_error(got[t], want) <= TOL
     assert be.forward_batch(ExpertKey(0, 3), xs[:0], lw.hidden, lw.inter).shape == (0, lw.hidden)
+
+
+@pytest.mark.parametrize("tokens", [1, 4, 24])
+def test_decode_host_entry_matches_device_entry(tokens):
+    """moe_b200_decode_host (host buffers, one synchronous call) gives the
+    same bits as moe_b200_decode on device buffers, for pinned tensors and
+    pageable numpy arrays alike, routing included."""
+    import ctypes as C
+    import torch
+    lw, xs = layer_case("small")
+    xs = np.ascontiguousarray(np.resize(xs, (tokens, lw.hidden)), np.float32)
+    be = _arena_backend(lw)
+    dev = be.device
+    k = lw.top_k
+    xd = torch.from_numpy(xs).to(dev)
+    yd = torch.empty_like(xd)
+    idd = torch.empty((tokens, k), dtype=torch.int32, device=dev)
+    wd = torch.empty((tokens, k), dtype=torch.float32, device=dev)
+    be.forward_layer_device(0, xd, yd, idd, wd)
+    torch.cuda.synchronize()
+    want = (yd.cpu().numpy(), idd.cpu().numpy(), wd.cpu().numpy())
+    # pinned tensors
+    xp = torch.from_numpy(xs).pin_memory()
+    yp = torch.empty((tokens, lw.hidden), dtype=torch.float32).pin_memory()
+    ip = torch.empty((tokens, k), dtype=torch.int32).pin_memory()
+    wp = torch.empty((tokens, k), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        be.forward_layer_host(0, xp, yp, ip, wp)
+        assert np.array_equal(yp.numpy().view(np.uint32), want[0].view(np.uint32))
+        assert np.array_equal(ip.numpy(), want[1])
+        assert np.array_equal(wp.numpy().view(np.uint32), want[2].view(np.uint32))
+    # pageable numpy, no routing requested
+    y = np.empty_like(xs)
+    be.forward_layer_host(0, xs, y)
+    assert np.array_equal(y.view(np.uint32), want[0].view(np.uint32))
+    # argument errors come back as status codes
+    dl = be.store.layer(0)
+    ws = be._host_workspace(dl, tokens)
+    s = dl.with_flags(0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    assert be.lib.moe_b200_decode_host(C.byref(s), None, tokens, y.ctypes.data, None, None,
+                                       ws.data_ptr(), ws.numel(), stream) == -1
+    assert be.lib.moe_b200_decode_host(C.byref(s), xs.ctypes.data, tokens, y.ctypes.data, None,
+                                       None, ws.data_ptr(), 256, stream) == -8
