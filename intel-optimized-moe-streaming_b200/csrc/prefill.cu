@@ -986,13 +986,24 @@ __global__ void __launch_bounds__(256) k_pf_prep_x(PfPrep p) {
 
 // Router logits of a few tokens on the CUDA cores, in fp32: block (x, y)
 // computes the partial dots of experts [32x, 32x + 32) with every token over
-// the hidden slice [128y, 128y + 128); k_pf_topk adds the H/128 partials in
-// slice order (deterministic).  For T <= kPfSmallRouterT, where the
-// tensor-core router would run on a handful of SMs.
+// the hidden slice [128y, 128y + 128); the last block of column x to finish
+// (an arrival counter per column) adds the H/128 partials in slice order
+// (deterministic), adds the bias and writes the logits.  For T <=
+// kPfSmallRouterT, where the tensor-core router would run on a handful of SMs.
 constexpr int kPfSmallRouterT = 128;
 constexpr int kRsE = 32, kRsK = 128, kRsT = 32;
 
-__global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, float* part) {
+__device__ __forceinline__ float4 pf_x4(const PfPrep& p, size_t i) {  // i a multiple of 4
+    if (p.x_bf16) {
+        const uint2 v = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p.x) + i);
+        return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                           __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+    }
+    return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + i);
+}
+
+__global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, float* part, uint32_t* cnt,
+                                                         const float* bias, float* logits) {
     __shared__ __align__(16) float sR[kRsE][kRsK + 4];
     __shared__ __align__(16) float sX[kRsT][kRsK + 4];
     const int e0 = blockIdx.x * kRsE, k0 = blockIdx.y * kRsK, tid = threadIdx.x;
@@ -1008,10 +1019,7 @@ __global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, float* part) 
         for (int i = tid; i < kRsT * kRsK / 4; i += 256) {
             const int r = i / (kRsK / 4), c = (i % (kRsK / 4)) * 4;
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + r < p.T) {
-                const size_t at = (size_t)(t0 + r) * p.H + k0 + c;
-                v = make_float4(pf_x(p, at), pf_x(p, at + 1), pf_x(p, at + 2), pf_x(p, at + 3));
-            }
+            if (t0 + r < p.T) v = pf_x4(p, (size_t)(t0 + r) * p.H + k0 + c);
             *reinterpret_cast<float4*>(&sX[r][c]) = v;
         }
         __syncthreads();
@@ -1036,6 +1044,26 @@ __global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, float* part) 
             }
         }
     }
+    // the last slice block of this expert column sums the partials
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t old = atomicAdd(cnt + blockIdx.x, 1u);
+        s_last = old == gridDim.y - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int ne = min(kRsE, p.E - e0);
+    for (int i = tid; i < ne * p.T; i += 256) {
+        const int t = i / ne, e = e0 + i % ne;
+        float v = 0.f;
+        for (int q = 0; q < (int)gridDim.y; ++q) v += __ldcg(part + ((size_t)q * p.T + t) * p.E + e);
+        if (bias) v = __fadd_rn(v, bias[e]);
+        logits[(size_t)t * p.E + e] = v;
+    }
+    if (tid == 0) cnt[blockIdx.x] = 0;  // ready for the next call
 }
 
 // one block per router row
@@ -1063,10 +1091,7 @@ __global__ void __launch_bounds__(256) k_pf_prep_router(PfPrep p) {
 
 struct PfRoute {
     int T, E, K, expert_begin, n_routed;
-    int KS;                // > 0: logits = sum of KS partial slices of `part` (+ bias)
-    const float* part;     // [KS][T][E]
-    const float* bias;     // [E] or null (KS > 0 only)
-    float* logits;
+    const float* logits;
     int32_t* ids;
     float* w;
     int32_t* ids_out;
@@ -1081,15 +1106,6 @@ struct PfRoute {
 __global__ void __launch_bounds__(32) k_pf_topk(PfRoute p) {
     extern __shared__ float s_sc[];
     const int t = blockIdx.x, lane = threadIdx.x;
-    if (p.KS > 0) {
-        for (int e = lane; e < p.E; e += 32) {
-            float v = 0.f;
-            for (int q = 0; q < p.KS; ++q) v += __ldcg(p.part + ((size_t)q * p.T + t) * p.E + e);
-            if (p.bias) v = __fadd_rn(v, p.bias[e]);
-            p.logits[(size_t)t * p.E + e] = v;
-        }
-        __syncwarp();
-    }
     int32_t* ids = p.ids + (size_t)t * p.K;
     float* w = p.w + (size_t)t * p.K;
     if (p.E <= 256) {
@@ -1236,9 +1252,12 @@ struct PfWs {
         total;
 };
 
-// The CUDA-core router for few tokens (needs 16-byte aligned router rows).
+// The CUDA-core router for few tokens (needs 16-byte aligned router rows;
+// its per-column arrival counters live in bytes [128, 256) of the
+// workspace, among the control words that stay zero between calls).
+constexpr int kRsCntOffset = 128;
 static bool pf_small_router(const moe_b200_layer* L, int T) {
-    return T <= kPfSmallRouterT && ((uintptr_t)L->router & 15u) == 0;
+    return T <= kPfSmallRouterT && L->n_experts <= 32 * kRsE && ((uintptr_t)L->router & 15u) == 0;
 }
 
 static PfWs pf_ws(const moe_b200_layer* L, int T) {
@@ -1356,7 +1375,7 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     pp.sg = reinterpret_cast<float*>(base + W.sg);
     pp.y = y;
     pp.counts = reinterpret_cast<int32_t*>(base + W.counts);
-    const bool small_router = routed && pf_small_router(L, T);
+    const bool small_router = routed && pf_small_router(L, T) && ((uintptr_t)x & 15u) == 0;
     pp.want_lo = routed && !small_router;
     k_pf_prep_x<<<T, 256, 0, s>>>(pp);
     cudaError_t e = cudaGetLastError();
@@ -1401,11 +1420,10 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
 
     if (routed && small_router) {
         float* part = reinterpret_cast<float*>(base + W.part);
-        k_pf_router_small<<<dim3((E + kRsE - 1) / kRsE, H / kRsK), 256, 0, s>>>(pp, part);
+        uint32_t* rcnt = reinterpret_cast<uint32_t*>(base + kRsCntOffset);
+        k_pf_router_small<<<dim3((E + kRsE - 1) / kRsE, H / kRsK), 256, 0, s>>>(
+            pp, part, rcnt, L->router_bias, gp.logits);
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
-        rp.KS = H / kRsK;
-        rp.part = part;
-        rp.bias = L->router_bias;
     } else if (routed) {
         k_pf_prep_router<<<E, 256, 0, s>>>(pp);
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);

@@ -27,6 +27,21 @@ from .key import ExpertKey
 from .store import ExpertArena
 
 
+def _host_ptr(a, np_dtype, torch_dtype, shape, what):
+    """Address of a contiguous host buffer of `shape` (numpy array or CPU
+    tensor), or None for None."""
+    if a is None:
+        return None
+    if isinstance(a, torch.Tensor):
+        if (a.dtype == torch_dtype and a.device.type == "cpu" and tuple(a.shape) == shape
+                and a.is_contiguous()):
+            return a.data_ptr()
+    elif (isinstance(a, np.ndarray) and a.dtype == np_dtype and a.shape == shape
+          and a.flags.c_contiguous):
+        return a.ctypes.data
+    raise ValueError(f"{what}: contiguous host {np.dtype(np_dtype)} array of shape {shape} needed")
+
+
 class B200ExpertBackend:
     """Expert backend over an ``ExpertArena``.
 
@@ -218,40 +233,54 @@ class B200ExpertBackend:
             ws.data_ptr(), ws.numel(), stream.cuda_stream)
         _lib.check(st, "moe_b200_decode")
 
+    def _host_call(self, layer: int, flags: int, tokens: int):
+        """(layer struct reference, workspace pointer, workspace bytes) of a
+        moe_b200_decode_host call, cached per thread, layer object and flags."""
+        cache = getattr(self._tls, "host_calls", None)
+        if cache is None:
+            cache = self._tls.host_calls = {}
+        dl = self.store.layer(layer)
+        key = (layer, flags, tokens)
+        ent = cache.get(key)
+        if ent is None or ent[0] is not dl:
+            s = dl.with_flags(flags)
+            ws = self._host_workspace(dl, tokens)
+            ent = cache[key] = (dl, s, C.byref(s), ws, ws.data_ptr(), ws.numel())
+        return ent
+
+    def decode_host_ptrs(self, layer: int, x_ptr: int, tokens: int, y_ptr: int,
+                         ids_ptr: int | None = None, w_ptr: int | None = None,
+                         stream_handle: int = 0) -> None:
+        """``moe_b200_decode_host`` on raw host addresses, like the reference's
+        ctypes binding of moe_quant_expert (src/flash_moe/native_expert.py:23-37):
+        the caller guarantees fp32 x / y rows of [tokens, H] (and int32 /
+        fp32 [tokens, K] routing rows when given); `stream_handle` is a
+        cudaStream_t (0: the legacy default stream)."""
+        ent = self._host_call(layer, self.flags, tokens)
+        st = self.lib.moe_b200_decode_host(ent[2], x_ptr, tokens, y_ptr, ids_ptr, w_ptr, ent[4],
+                                           ent[5], stream_handle)
+        if st:
+            _lib.check(st, "moe_b200_decode_host")
+
     def forward_layer_host(self, layer: int, x, y, topk_ids=None, topk_weights=None,
                            flags: int | None = None, stream=None) -> None:
         """Synchronous layer decode with host buffers (``moe_b200_decode_host``):
         x and y fp32 [T, H], topk_ids int32 / topk_weights fp32 [T, K] when
         given -- numpy arrays or CPU tensors, pinned for asynchronous copies."""
-        def host_ptr(a, dtype, shape, what):
-            if a is None:
-                return None
-            if isinstance(a, torch.Tensor):
-                ok = (a.device.type == "cpu" and a.is_contiguous() and a.dtype == dtype[1]
-                      and tuple(a.shape) == shape)
-                ptr = a.data_ptr()
-            else:
-                ok = (isinstance(a, np.ndarray) and a.flags.c_contiguous and a.dtype == dtype[0]
-                      and a.shape == shape)
-                ptr = a.ctypes.data if ok else 0
-            if not ok:
-                raise ValueError(f"{what}: contiguous host {dtype[0]} array of shape {shape} needed")
-            return ptr
-        dl = self.store.layer(layer)
-        t, h = (x.shape[0], x.shape[1]) if len(x.shape) == 2 else (0, 0)
-        k = dl.weights.top_k
-        f32, i32 = (np.float32, torch.float32), (np.int32, torch.int32)
-        xp = host_ptr(x, f32, (t, dl.weights.hidden), "x")
-        yp = host_ptr(y, f32, (t, dl.weights.hidden), "y")
-        ip = host_ptr(topk_ids, i32, (t, k), "topk_ids")
-        wp = host_ptr(topk_weights, f32, (t, k), "topk_weights")
-        s = dl.with_flags(self.flags if flags is None else flags)
-        ws = self._host_workspace(dl, t)
+        t = x.shape[0] if len(x.shape) == 2 else 0
+        ent = self._host_call(layer, self.flags if flags is None else flags, t)
+        w = ent[0].weights
+        shp_x, shp_k = (t, w.hidden), (t, w.top_k)
+        xp = _host_ptr(x, np.float32, torch.float32, shp_x, "x")
+        yp = _host_ptr(y, np.float32, torch.float32, shp_x, "y")
+        ip = _host_ptr(topk_ids, np.int32, torch.int32, shp_k, "topk_ids")
+        wp = _host_ptr(topk_weights, np.float32, torch.float32, shp_k, "topk_weights")
         if stream is None:
             stream = torch.cuda.current_stream(self.device)
-        st = self.lib.moe_b200_decode_host(C.byref(s), xp, t, yp, ip, wp, ws.data_ptr(),
-                                           ws.numel(), stream.cuda_stream)
-        _lib.check(st, "moe_b200_decode_host")
+        st = self.lib.moe_b200_decode_host(ent[2], xp, t, yp, ip, wp, ent[4], ent[5],
+                                           stream.cuda_stream)
+        if st:
+            _lib.check(st, "moe_b200_decode_host")
 
     def ep_fused_supported(self, layer: int, tokens: int) -> bool:
         """True when ``decode_ep_device`` takes `tokens` gathered tokens of

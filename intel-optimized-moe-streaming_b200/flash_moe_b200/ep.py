@@ -268,11 +268,16 @@ class DecodeRunner:
         xd = torch.empty((1, H), dtype=torch.float32, device=self.dev)
         stream = torch.cuda.current_stream(self.dev)
 
+        xrow = [host_x[j].data_ptr() for j in range(n)]
+        yptr = host_y.data_ptr()
+        sh = stream.cuda_stream
+
         def one(i):
             if self.world == 1:
-                # one synchronous library call: pinned token in, result out
-                self.be.forward_layer_host(self.layers[i % len(self.layers)],
-                                           host_x[i % n].view(1, -1), host_y)
+                # one synchronous library call on the pinned rows: token in,
+                # result out
+                self.be.decode_host_ptrs(self.layers[i % len(self.layers)], xrow[i % n], 1, yptr,
+                                         stream_handle=sh)
                 return
             xd.copy_(host_x[i % n].view(1, -1), non_blocking=True)
             self.step(i, x=xd)
