@@ -113,6 +113,49 @@ def probe_prefill(tokens: int = 4096) -> None:
     print("device error word:", be.prefill_errors())
 
 
+def probe_batched(tokens: int = 64, calls: int = 10) -> None:
+    """Batched decode on the tensor-core path (the config-3 layer: Zipf(1.1)
+    router bias): time per call, the routing's expert counts and the
+    per-role wait counters of the expert GEMMs."""
+    dev = torch.device("cuda", 0)
+    lw = synth.make_layer(seed=0, zipf_s=1.1)
+    arena = ExpertArena(dev)
+    arena.add_layer(0, lw)
+    be = B200ExpertBackend(arena)
+    x = torch.from_numpy(synth.make_tokens(3000, tokens, lw.hidden)).to(dev)
+    y = torch.empty_like(x)
+    ids = torch.empty((tokens, lw.top_k), dtype=torch.int32, device=dev)
+    for _ in range(3):
+        be.prefill_device(0, x, y, ids)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(calls):
+        be.prefill_device(0, x, y, ids)
+    e1.record()
+    torch.cuda.synchronize()
+    cnt = np.bincount(ids.cpu().numpy().ravel(), minlength=lw.n_experts)
+    print(f"{tokens} tokens: {e0.elapsed_time(e1) * 1e3 / calls:.1f} us per call, "
+          f"{int((cnt > 0).sum())} experts selected, most tokens on one expert {int(cnt.max())}")
+    G = _sms(dev)
+    buf = torch.zeros(G * 32, dtype=torch.int64, device=dev)
+    be.lib.moe_b200_set_trace(C.c_void_p(buf.data_ptr()), G)
+    try:
+        be.prefill_device(0, x, y, ids)
+        torch.cuda.synchronize()
+    finally:
+        be.lib.moe_b200_set_trace(None, 0)
+    a = buf.view(G, 32).cpu().numpy().astype(np.float64)
+    for mode, name in [(1, "gate/up"), (2, "down")]:
+        blk = a[:, mode * 10: mode * 10 + 10]
+        cyc = blk[:, 8].mean()
+        print(f"{name}: {cyc:.0f} cycles per CTA (max {blk[:, 8].max():.0f}), "
+              f"{blk[:, 9].mean():.2f} units per CTA")
+        for i, role in enumerate(PREFILL_ROLES):
+            print(f"  {role:24s} {blk[:, i].mean() / max(cyc, 1) * 100:6.1f}% of cycles")
+    print("device error word:", be.prefill_errors())
+
+
 def probe_ep(steps: int = 64, copies: int = 16) -> None:
     import os
     from datetime import timedelta
@@ -189,6 +232,9 @@ def main() -> None:
     d.add_argument("--copies", type=int, default=16)
     p = sub.add_parser("prefill")
     p.add_argument("--tokens", type=int, default=4096)
+    b = sub.add_parser("batched")
+    b.add_argument("--tokens", type=int, default=64)
+    b.add_argument("--calls", type=int, default=10)
     q = sub.add_parser("ep")
     q.add_argument("--steps", type=int, default=64)
     args = ap.parse_args()
@@ -197,6 +243,8 @@ def main() -> None:
         probe_decode(args.steps, args.copies)
     elif args.what == "ep":
         probe_ep(args.steps)
+    elif args.what == "batched":
+        probe_batched(args.tokens, args.calls)
     else:
         probe_prefill(args.tokens)
 
