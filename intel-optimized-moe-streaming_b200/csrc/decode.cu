@@ -430,12 +430,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         __syncthreads();
         TRACE(10);
 
-        // ---- down rows [h0, h1) of every vector: item = (vector, pair of row
-        // groups); the activation codes are loaded once per item
+        // ---- down rows [h0, h1) of every vector: item = (routed vector, pair
+        // of row groups), the activation codes loaded once per item; the
+        // shared vector's row groups are one per item, so that they spread
+        // over the warps of the round after the routed items
         {
             const int rpw_i = 32 / p.lpr_i, rpw_s = 32 / p.lpr_is;
             const int ng_i = (nh + rpw_i - 1) / rpw_i, ng_s = Is ? (nh + rpw_s - 1) / rpw_s : 0;
-            const int np_i = (ng_i + 1) / 2, np_s = (ng_s + 1) / 2;
+            const int np_i = (ng_i + 1) / 2, np_s = ng_s;
             for (int it = warp; it < A * np_i + np_s; it += nw) {
                 const bool sh = it >= A * np_i;
                 const int v = sh ? A : it / np_i;
@@ -451,7 +453,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                 load_xlane(xa, qvec_at(sm + p.o_aq + v * qb, n), pr >> 2, pr & 3);
 #pragma unroll
                 for (int gg = 0; gg < 2; ++gg) {
-                    const int gi = 2 * gp + gg;
+                    const int gi = sh ? (gg == 0 ? gp : ng) : 2 * gp + gg;
                     if (gi < ng) {
                         const int rr = gi * rpw + sub;
                         const bool ok = rr < nh;
