@@ -152,8 +152,11 @@ MOE_B200_API int moe_b200_decode_host_workspace(const moe_b200_layer* layer, int
  * memory, synchronous like the reference's ctypes entry points: copies x
  * ([tokens x H] fp32) to the workspace's staging rows, decodes on `stream`,
  * copies y (and topk_ids / topk_weights when not NULL) back to the host
- * pointers and waits for the stream.  Pinned host memory makes the copies
- * asynchronous DMA; pageable memory works, staged by the driver.  Returns
+ * pointers and waits for the stream.  One token goes through this calling
+ * thread's pinned staging rows (allocated on its first call, kept until the
+ * process exits) and one graph launch whose kernels read the token and write
+ * the result through the pinned mapping; several tokens are copied with
+ * cudaMemcpyAsync (pinned rows make those copies asynchronous).  Returns
  * moe_b200_decode's status, or -9 when a bounded device wait gave up (the
  * workspace error word, read and cleared here).  The workspace is device
  * memory of moe_b200_decode_host_workspace bytes, zeroed once with

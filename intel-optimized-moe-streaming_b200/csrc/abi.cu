@@ -373,16 +373,34 @@ int moe_b200_decode_host_workspace(const moe_b200_layer* L, int32_t max_tokens, 
     return ST_OK;
 }
 
-// True when the device reads and writes `p` at the same address (pinned,
-// mapped host memory under unified addressing).
-static bool device_visible(const void* p) {
-    if (!p) return true;
-    cudaPointerAttributes a;
-    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
-    }
-    return a.type == cudaMemoryTypeHost && a.devicePointer == p;
+// This thread's pinned staging rows of moe_b200_decode_host's single-token
+// path: the token, the result, the routing and the error word, which the
+// device reads and writes through the pinned mapping.
+struct HostStage {
+    float* x = nullptr;
+    float* y = nullptr;
+    int32_t* ids = nullptr;
+    float* w = nullptr;
+    int* err = nullptr;
+    int H = 0, K = 0;
+};
+
+static cudaError_t host_stage(HostStage& hs, int H, int K) {
+    if (hs.x && hs.H >= H && hs.K >= K) return cudaSuccess;
+    if (hs.x) cudaFreeHost(hs.x);
+    hs = HostStage{};
+    const size_t rows = (size_t)H * 4, kb = ((size_t)K * 4 + 15) & ~(size_t)15;
+    char* b = nullptr;
+    cudaError_t e = cudaMallocHost(reinterpret_cast<void**>(&b), 2 * rows + 2 * kb + 16);
+    if (e != cudaSuccess) return e;
+    hs.x = reinterpret_cast<float*>(b);
+    hs.y = reinterpret_cast<float*>(b + rows);
+    hs.ids = reinterpret_cast<int32_t*>(b + 2 * rows);
+    hs.w = reinterpret_cast<float*>(b + 2 * rows + kb);
+    hs.err = reinterpret_cast<int*>(b + 2 * rows + 2 * kb);
+    hs.H = H;
+    hs.K = K;
+    return cudaSuccess;
 }
 
 int moe_b200_decode_host(const moe_b200_layer* L, const float* x, int32_t T, float* y,
@@ -401,31 +419,31 @@ int moe_b200_decode_host(const moe_b200_layer* L, const float* x, int32_t T, flo
     int32_t* idd = topk_ids ? reinterpret_cast<int32_t*>(base + hw.ids) : nullptr;
     float* wd = topk_weights ? reinterpret_cast<float*>(base + hw.w) : nullptr;
     const size_t xb = (size_t)T * L->hidden * 4, kb = (size_t)T * L->top_k * 4;
-    // the error word comes back through a pinned per-thread word, so that
-    // all copies stay asynchronous until the one synchronisation
-    static thread_local int* word_h = nullptr;
-    cudaError_t e;
-    if (!word_h && (e = cudaMallocHost(reinterpret_cast<void**>(&word_h), sizeof(int))) != cudaSuccess) {
-        word_h = nullptr;
-        return fail(e, ST_CUDA);
-    }
-    *word_h = 0;
-    // one token, pinned buffers: the fused kernel writes the result, the
-    // routing and the error word straight to host memory (one graph launch,
-    // no copy-engine transfers)
-    if (T == 1 && fused_supported(L, T, L->flags) && ((uintptr_t)x & 15u) == 0 &&
-        device_visible(x) && device_visible(y) && device_visible(topk_ids) &&
-        device_visible(topk_weights) && device_visible(word_h)) {
+    static thread_local HostStage hs;
+    cudaError_t e = host_stage(hs, L->hidden, L->top_k);
+    if (e != cudaSuccess) return fail(e, ST_CUDA);
+    // one token: the token goes through the pinned staging row, one graph
+    // launch (a copy-in kernel and the fused kernel, which writes the result,
+    // the routing and the error word straight to the pinned rows), one
+    // synchronisation, and the result is copied out on the host
+    if (T == 1 && fused_supported(L, T, L->flags)) {
+        memcpy(hs.x, x, xb);
+        *hs.err = 0;
         bool launched = false;
-        e = launch_decode_fused_host(L, L->flags, x, xd, y, topk_ids, topk_weights, word_h,
-                                     workspace, s, &launched);
+        e = launch_decode_fused_host(L, L->flags, hs.x, xd, hs.y, hs.ids, hs.w, hs.err, workspace,
+                                     s, &launched);
         if (e != cudaSuccess) return fail(e, ST_CUDA);
         if (launched) {
             e = cudaStreamSynchronize(s);
             if (e != cudaSuccess) return fail(e, ST_CUDA);
-            return *word_h;
+            memcpy(y, hs.y, xb);
+            if (topk_ids) memcpy(topk_ids, hs.ids, kb);
+            if (topk_weights) memcpy(topk_weights, hs.w, kb);
+            return *hs.err;
         }
     }
+    int* word_h = hs.err;
+    *word_h = 0;
     e = cudaMemcpyAsync(xd, x, xb, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return fail(e, ST_CUDA);
     st = moe_b200_decode(L, xd, T, yd, idd, wd, workspace, hw.x, stream);

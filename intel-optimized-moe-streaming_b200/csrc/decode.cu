@@ -26,6 +26,9 @@
 // E scores, the A*I + Is fp32 activations, the shared gate value.
 #include <math.h>
 #include <stdlib.h>
+#include <string.h>
+
+#include <vector>
 
 #include "fused.cuh"
 #include "launch.h"
@@ -618,7 +621,7 @@ static cudaError_t fused_prepare(const moe_b200_layer* L, int flags, const float
                                  FusedParams& p, FusedFn& fn, bool* ok) {
     *ok = false;
     const bool shared = L->shared_intermediate > 0 && !(flags & MOE_B200_NO_SHARED);
-    p = FusedParams{};
+    memset(&p, 0, sizeof(p));
     p.L = *L;
     const int G = sm_count();
     if (!fused_plan(L, shared, G, p)) return cudaSuccess;
@@ -714,25 +717,29 @@ __global__ void __launch_bounds__(256) k_copy_in(const float4* __restrict__ src,
     if (i < n4) dst[i] = src[i];
 }
 
-// Per-thread graph of (copy-in kernel -> fused kernel) for synchronous
+// Per-thread graphs of (copy-in kernel -> fused kernel) for synchronous
 // single-token calls with host buffers: a graph launch reaches the GPU
-// sooner than a direct cooperative launch.  The nodes' parameters are
-// updated on every call; the graph is rebuilt when the device, kernel
-// instance or shared-memory size changes.  (A thread's last graph is left to
-// the driver's clean-up at process exit.)
+// sooner than a direct cooperative launch.  The caller's buffers are the
+// library's fixed pinned staging rows, so a graph's parameters depend only on
+// the layer, the workspace and the device: one graph per such combination is
+// kept (at most kHostGraphs per thread, oldest dropped first) and replayed
+// without parameter updates.  A thread's graphs are left to the driver's
+// clean-up at process exit.
+constexpr size_t kHostGraphs = 64;
+
+struct HostGraphKey {
+    int dev;
+    FusedFn fn;
+    FusedParams p;
+    const float4* src;
+    float4* dst;
+    int n4;
+};
+
 struct HostGraph {
-    int dev = -1;
-    FusedFn fn = nullptr;
-    uint32_t smem = 0;
-    int G = 0, n4 = 0;
-    cudaGraph_t g = nullptr;
-    cudaGraphExec_t ge = nullptr;
-    cudaGraphNode_t copy = nullptr, fused = nullptr;
-    void reset() {
-        if (ge) cudaGraphExecDestroy(ge);
-        if (g) cudaGraphDestroy(g);
-        *this = HostGraph{};
-    }
+    HostGraphKey key;
+    cudaGraph_t g;
+    cudaGraphExec_t ge;
 };
 
 cudaError_t launch_decode_fused_host(const moe_b200_layer* L, int flags, const float* x_host,
@@ -740,59 +747,63 @@ cudaError_t launch_decode_fused_host(const moe_b200_layer* L, int flags, const f
                                      float* w_host, int* err_host, void* ws, cudaStream_t stream,
                                      bool* launched) {
     *launched = false;
-    FusedParams p;
-    FusedFn fn = nullptr;
+    HostGraphKey k;
+    memset(&k, 0, sizeof(k));
     bool ok = false;
     cudaError_t e = fused_prepare(L, flags, x_stage, y_host, ids_host, w_host, nullptr, nullptr, 1,
-                                  0.f, ws, p, fn, &ok);
+                                  0.f, ws, k.p, k.fn, &ok);
     if (e != cudaSuccess || !ok) return e;
-    p.err_out = err_host;
-    static thread_local HostGraph hg;
-    int dev = 0;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    const int n4 = L->hidden / 4;
-    const float4* src = reinterpret_cast<const float4*>(x_host);
-    float4* dst = reinterpret_cast<float4*>(x_stage);
-    void* cargs[] = {&src, &dst, const_cast<int*>(&n4)};
-    cudaKernelNodeParams cp = {};
-    cp.func = reinterpret_cast<void*>(k_copy_in);
-    cp.gridDim = dim3((n4 + 255) / 256);
-    cp.blockDim = dim3(256);
-    cp.kernelParams = cargs;
-    void* fargs[] = {&p};
-    cudaKernelNodeParams fp = {};
-    fp.func = reinterpret_cast<void*>(fn);
-    fp.gridDim = dim3(p.G);
-    fp.blockDim = dim3(kFusedThreads);
-    fp.sharedMemBytes = p.total;
-    fp.kernelParams = fargs;
-    const bool same = hg.ge && hg.dev == dev && hg.fn == fn && hg.smem == p.total && hg.G == p.G &&
-                      hg.n4 == n4;
-    if (same) {
-        e = cudaGraphExecKernelNodeSetParams(hg.ge, hg.copy, &cp);
-        if (e == cudaSuccess) e = cudaGraphExecKernelNodeSetParams(hg.ge, hg.fused, &fp);
-    } else {
-        hg.reset();
-        e = cudaGraphCreate(&hg.g, 0);
-        if (e == cudaSuccess) e = cudaGraphAddKernelNode(&hg.copy, hg.g, nullptr, 0, &cp);
-        if (e == cudaSuccess) e = cudaGraphAddKernelNode(&hg.fused, hg.g, &hg.copy, 1, &fp);
-        if (e == cudaSuccess) {
-            cudaLaunchAttributeValue v = {};
-            v.cooperative = 1;
-            e = cudaGraphKernelNodeSetAttribute(hg.fused, cudaLaunchAttributeCooperative, &v);
-        }
-        if (e == cudaSuccess) e = cudaGraphInstantiate(&hg.ge, hg.g, 0);
-        if (e != cudaSuccess) {
-            hg.reset();
+    k.p.err_out = err_host;
+    if ((e = cudaGetDevice(&k.dev)) != cudaSuccess) return e;
+    k.n4 = L->hidden / 4;
+    k.src = reinterpret_cast<const float4*>(x_host);
+    k.dst = reinterpret_cast<float4*>(x_stage);
+    static thread_local std::vector<HostGraph> cache;
+    for (size_t i = 0; i < cache.size(); ++i) {
+        if (memcmp(&cache[i].key, &k, sizeof(k)) == 0) {
+            e = cudaGraphLaunch(cache[i].ge, stream);
+            if (e == cudaSuccess) *launched = true;
             return e;
         }
-        hg.dev = dev;
-        hg.fn = fn;
-        hg.smem = p.total;
-        hg.G = p.G;
-        hg.n4 = n4;
     }
-    if (e != cudaSuccess) return e;
+    HostGraph hg;
+    hg.key = k;
+    hg.g = nullptr;
+    hg.ge = nullptr;
+    void* cargs[] = {&hg.key.src, &hg.key.dst, &hg.key.n4};
+    cudaKernelNodeParams cp = {};
+    cp.func = reinterpret_cast<void*>(k_copy_in);
+    cp.gridDim = dim3((k.n4 + 255) / 256);
+    cp.blockDim = dim3(256);
+    cp.kernelParams = cargs;
+    void* fargs[] = {&hg.key.p};
+    cudaKernelNodeParams fp = {};
+    fp.func = reinterpret_cast<void*>(k.fn);
+    fp.gridDim = dim3(k.p.G);
+    fp.blockDim = dim3(kFusedThreads);
+    fp.sharedMemBytes = k.p.total;
+    fp.kernelParams = fargs;
+    cudaGraphNode_t copy = nullptr, fused = nullptr;
+    e = cudaGraphCreate(&hg.g, 0);
+    if (e == cudaSuccess) e = cudaGraphAddKernelNode(&copy, hg.g, nullptr, 0, &cp);
+    if (e == cudaSuccess) e = cudaGraphAddKernelNode(&fused, hg.g, &copy, 1, &fp);
+    if (e == cudaSuccess) {
+        cudaLaunchAttributeValue v = {};
+        v.cooperative = 1;
+        e = cudaGraphKernelNodeSetAttribute(fused, cudaLaunchAttributeCooperative, &v);
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&hg.ge, hg.g, 0);
+    if (e != cudaSuccess) {
+        if (hg.ge) cudaGraphExecDestroy(hg.ge);
+        if (hg.g) cudaGraphDestroy(hg.g);
+        return e;
+    }
+    if (cache.size() >= kHostGraphs) {
+        cudaGraphExecDestroy(cache.front().ge);
+        cudaGraphDestroy(cache.front().g);
+        cache.erase(cache.begin());
+    }
+    cache.push_back(hg);
     e = cudaGraphLaunch(hg.ge, stream);
     if (e == cudaSuccess) *launched = true;
     return e;

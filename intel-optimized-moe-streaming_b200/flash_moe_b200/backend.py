@@ -100,18 +100,6 @@ class B200ExpertBackend:
             cache[self.device] = ws
         return ws
 
-    def _pinned(self, tokens: int, hidden: int, k: int):
-        """This thread's pinned host rows (x, y, ids, weights) for `tokens`."""
-        cache = getattr(self._tls, "pinned", None)
-        if cache is None or cache[0].shape[0] < tokens or cache[0].shape[1] != hidden \
-                or cache[2].shape[1] != k:
-            cache = self._tls.pinned = (
-                torch.empty((tokens, hidden), dtype=torch.float32).pin_memory(),
-                torch.empty((tokens, hidden), dtype=torch.float32).pin_memory(),
-                torch.empty((tokens, k), dtype=torch.int32).pin_memory(),
-                torch.empty((tokens, k), dtype=torch.float32).pin_memory())
-        return tuple(c[:tokens] for c in cache)
-
     def _host_workspace(self, dl, tokens: int) -> torch.Tensor:
         cache = getattr(self._tls, "host_ws", None)
         if cache is None:
@@ -414,17 +402,15 @@ class B200ExpertBackend:
         x = x.reshape(-1, self.store.layer(layer).weights.hidden)
         k = self.store.layer(layer).weights.top_k
         if not (x.shape[0] >= self.prefill_min_tokens and self.prefill_supported(layer)):
-            # decode: one synchronous call through this thread's pinned
-            # staging rows (the single-token call then needs no copy engine)
+            # decode: one synchronous call with the host arrays
             t = x.shape[0]
-            xp, yp, ip, wp = self._pinned(t, x.shape[1], k)
-            xp.numpy()[:] = x
+            y = np.empty_like(x)
+            ids = np.empty((t, k), np.int32)
+            w = np.empty((t, k), np.float32)
             with torch.cuda.device(self.device):
-                self.forward_layer_host(layer, xp, yp, ip, wp)
-            y = yp.numpy().copy()
-            routing = (ip.numpy().copy(), wp.numpy().copy())
+                self.forward_layer_host(layer, x, y, ids, w)
             y = y[0] if squeeze else y
-            return (y, routing) if return_routing else y
+            return (y, (ids, w)) if return_routing else y
         with torch.cuda.device(self.device):
             xd = torch.from_numpy(x).to(self.device, non_blocking=False)
             yd = torch.empty_like(xd)
