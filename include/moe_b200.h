@@ -120,6 +120,7 @@ typedef struct moe_b200_layer {
 #define MOE_B200_NO_SHARED    2  /* skip the shared expert on this call */
 #define MOE_B200_EXACT        4  /* use the exact (fp32 dequant + FMA) engine */
 #define MOE_B200_SHARED_ONLY  8  /* only the shared expert (no routing, no routed experts) */
+#define MOE_B200_TCGEN05     16  /* prefill: the tcgen05 expert GEMMs also for <= 48 tokens */
 
 /* Bytes of workspace moe_b200_decode needs for `max_tokens` tokens.  The
  * workspace is 256-byte aligned device memory; zero it once with

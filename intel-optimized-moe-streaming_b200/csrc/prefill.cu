@@ -910,6 +910,392 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
 }
 
 // ---------------------------------------------------------------------------
+// Few tokens per expert (batched decode): warp-level MMA, dequantisation
+// straight into each warp's own A tile.
+//
+// With a handful of pairs per expert the tensor core is idle almost all the
+// time and the layer's cost is the dequantisation of every weight once.
+// k_bd_gemm keeps that work in the warps that consume it: a CTA of 8 warps
+// owns 256 weight rows (gate/up: 128 intermediate rows, each warp 16 of
+// them as 8 gate + 8 up rows per 16-row MMA tile, so that one lane holds the
+// gate and the up product of the same row; down: 256 output rows) and up to
+// kBdMaxN pairs; per 256-value group one thread brings the raw rows and the
+// B rows (x in pair order / act, 128B-swizzled 16-row boxes) into one of two
+// buffers with TMA, every lane decodes its own row of the group (the same
+// functions as the tensor-core path: the exact fp16 value of the
+// reference's f16 dequantisation) into the warp's 32 x 64 A tile per
+// 64-value stage, and the warp runs mma.sync m16n8k16 (fp16, fp32
+// accumulation) over its two row tiles and the pair tiles.  No role
+// pipeline, no shared-memory handshake beyond the two group buffers.
+// Epilogues as in k_pf_gemm: SiLU(g) * u to fp16 act rows, and
+// y[token] += w * out with fp32 reductions.
+
+constexpr int kBdMT = 2;                   // 16-row MMA tiles per warp
+constexpr int kBdWarpRows = 16 * kBdMT;
+constexpr int kBdMaxN = 64;                // pairs per unit (8 MMA column tiles)
+constexpr int kBdThreads = 256;            // 8 warps
+constexpr int kBdRows = 8 * kBdWarpRows;   // weight rows per unit
+constexpr int kBdCtasPerSm = 1;
+// Measured on the config-2 layer (Zipf-biased routing): 32 tokens 134 us per
+// call on this path against 147 us on the tcgen05 pipeline, 64 tokens 168 us
+// against 160 us; so up to kBdMaxT tokens take this path.
+constexpr int kBdMaxT = 48;
+
+struct BdLayout {
+    uint32_t raw_bytes;   // 256 rows x W per buffer
+    uint32_t buf_bytes;   // raw (rounded to 1 KB) + B tile
+    uint32_t b_bytes;     // (GV / 64) stages x kBdMaxN rows x 128 B
+};
+
+__device__ __forceinline__ void bd_ldsm4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                         uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void bd_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                       uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// One unit's K loop for weight format T: buffers `bufs` (two), their
+// mbarriers `bars` / phase bits `ph`; the producer thread (tid 0) issues a
+// group's copies with `issue(g, buffer)`.  acc[mt][nt] accumulate the
+// warp's row tile mt (16 rows) x pair tile nt (8 pairs).
+// NTC: pair tiles computed (compile time; >= the unit's tiles, the columns
+// past the unit's pairs are discarded by the epilogue).
+template <int T, int NTC, typename Issue, typename Wait>
+__device__ __forceinline__ bool bd_k_loop(int groups, uint8_t* bufs, uint32_t buf_bytes,
+                                          uint32_t b_off, uint32_t raw_row_ofs, uint8_t* atile,
+                                          float (&acc)[kBdMT][kBdMaxN / 8][4], Issue&& issue,
+                                          Wait&& wait, volatile int* abort) {
+    constexpr int GB = pf_gb(T), W = pf_w(T), NSW = W / 4, NW = PfNW<T>::n, NST = pf_gv(T) / 64;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const uint32_t a_base = smem_u32(atile);
+    for (int g = 0; g < groups; ++g) {
+        const int b = g & 1;
+        if (tid < 32 && g + 1 < groups) issue(g + 1, (g + 1) & 1);
+        if (tid == 0) wait(b);  // group g's copies (one waiter, then the CTA)
+        __syncthreads();
+        if (*abort) return false;
+        uint8_t* buf = bufs + (size_t)b * buf_bytes;
+        // this lane's row of the group, normalised to block-relative words
+        const uint8_t* rr = buf + raw_row_ofs;
+        uint32_t src[NSW];
+#pragma unroll
+        for (int k = 0; k < W / 16; ++k) {
+            const uint4 v = *reinterpret_cast<const uint4*>(rr + 16 * k);
+            src[4 * k] = v.x;
+            src[4 * k + 1] = v.y;
+            src[4 * k + 2] = v.z;
+            src[4 * k + 3] = v.w;
+        }
+        const int o = (g * GB) & 15;
+        uint32_t w[NW];
+        if (GB % 16 == 0) {
+#pragma unroll
+            for (int i = 0; i < NW; ++i) w[i] = src[i];
+        } else {
+            const int q = o >> 2;
+            const uint32_t sb = (uint32_t)(o & 3) * 8u;
+            uint32_t t1[NSW];
+#pragma unroll
+            for (int i = 0; i < NSW; ++i) t1[i] = (q & 1) ? (i + 1 < NSW ? src[i + 1] : 0u) : src[i];
+#pragma unroll
+            for (int i = 0; i < NSW; ++i) src[i] = (q & 2) ? (i + 2 < NSW ? t1[i + 2] : 0u) : t1[i];
+#pragma unroll
+            for (int i = 0; i < NW; ++i) w[i] = __funnelshift_r(src[i], src[i + 1], sb);
+        }
+        const uint32_t b_base0 = smem_u32(buf + b_off);
+        auto stage = [&](auto s_c) {
+            constexpr int S = decltype(s_c)::value;
+            if constexpr (kBdMT == 2) {
+                dq_store<T, S>(atile, lane, 0, w);
+                dq_store<T, S>(atile, lane, 1, w);
+            } else {
+                dq_store<T, S>(atile, lane & 15, lane >> 4, w);  // two lanes per row
+            }
+            __syncwarp();
+            const uint32_t b_base = b_base0 + (uint32_t)(S * kBdMaxN * 128);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                uint32_t a[kBdMT][4];
+#pragma unroll
+                for (int mt = 0; mt < kBdMT; ++mt) {
+                    const int r = 16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1), c = 2 * ks + (lane >> 4);
+                    bd_ldsm4(a_base + sw128_offset(r, c), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+                }
+#pragma unroll
+                for (int nt = 0; nt < NTC; nt += 2) {
+                    const int n = 8 * nt + (lane & 7) + 8 * (lane >> 4), c = 2 * ks + ((lane >> 3) & 1);
+                    uint32_t b0, b1, b2, b3;
+                    bd_ldsm4(b_base + sw128_offset(n, c), b0, b1, b2, b3);
+#pragma unroll
+                    for (int mt = 0; mt < kBdMT; ++mt) {
+                        bd_mma(acc[mt][nt], a[mt], b0, b1);
+                        bd_mma(acc[mt][nt + 1], a[mt], b2, b3);
+                    }
+                }
+            }
+            __syncwarp();
+        };
+        stage(std::integral_constant<int, 0>{});
+        stage(std::integral_constant<int, 1>{});
+        if constexpr (NST == 4) {
+            stage(std::integral_constant<int, 2>{});
+            stage(std::integral_constant<int, 3>{});
+        }
+        __syncthreads();  // buffer b free for group g + 2
+    }
+    return true;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kBdThreads, kBdCtasPerSm) k_bd_gemm(const __grid_constant__ PfParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // layout: two group buffers, 8 warp A tiles (32 rows x 128 B), control
+    uint8_t* bufs = smem;
+    const uint32_t buf_bytes = p.stage_bytes;  // per buffer (raw rows + B tile)
+    uint8_t* atiles = smem + 2 * (size_t)buf_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(atiles + 8 * kBdWarpRows * 128);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2);
+    int* s_tfirst = reinterpret_cast<int*>(bars + 3);
+    int* s_poff = s_tfirst + (p.n_routed + 1);
+    uint8_t* atile = atiles + warp * kBdWarpRows * 128;
+
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        *s_abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        // column tiles and pair offsets of the held experts (exclusive prefix sums)
+        int carry_t = 0, carry_p = 0;
+        for (int base = 0; base < p.n_routed; base += 32) {
+            const int e = base + lane;
+            const int c = e < p.n_routed ? p.counts[e] : 0;
+            const int t0 = (c + kBdMaxN - 1) / kBdMaxN;
+            int tl = t0, pc = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int a = __shfl_up_sync(0xffffffffu, tl, o);
+                const int b = __shfl_up_sync(0xffffffffu, pc, o);
+                if (lane >= o) {
+                    tl += a;
+                    pc += b;
+                }
+            }
+            if (e < p.n_routed) {
+                s_tfirst[e] = carry_t + tl - t0;
+                s_poff[e] = carry_p + pc - c;
+            }
+            carry_t += __shfl_sync(0xffffffffu, tl, 31);
+            carry_p += __shfl_sync(0xffffffffu, pc, 31);
+        }
+        if (lane == 0) {
+            s_tfirst[p.n_routed] = carry_t;
+            s_poff[p.n_routed] = carry_p;
+        }
+    }
+    __syncthreads();
+    constexpr int RPU = MODE == PF_GATEUP ? kBdRows / 2 : kBdRows;  // side rows per unit
+    const int ntiles_r = p.n_routed > 0 ? s_tfirst[p.n_routed] : 0;
+    const int pairs = p.n_routed > 0 ? s_poff[p.n_routed] : 0;
+    const int rt_r = p.side[0].rows / RPU, rt_s = p.side[1].rows / RPU;
+    const int units_r = ntiles_r * rt_r;
+    const int tiles_s = p.has_shared ? (p.T + kBdMaxN - 1) / kBdMaxN : 0;
+    const int n_units = units_r + tiles_s * rt_s;
+    const uint64_t stream_pol = l2_evict_first(), keep = l2_evict_last();
+    uint32_t ph = 0, pend = 0;  // (thread 0) phase bit and copies in flight, per buffer
+    auto wait = [&](int b) {     // thread 0: bounded wait for buffer b's copies
+        bool okw = false;
+        for (uint32_t i = 0; i < kPfPolls; ++i)
+            if (mbar_try_wait(&bars[b], (ph >> b) & 1u)) {
+                okw = true;
+                break;
+            }
+        ph ^= 1u << b;
+        pend &= ~(1u << b);
+        if (!okw) {
+            atomicCAS(p.err, 0u, (uint32_t)ST_TIMEOUT);
+            *s_abort = 1;
+        }
+    };
+    constexpr int kBoxRows = MODE == PF_GATEUP ? 64 : 128;  // rows of a raw weight box
+
+    // units are taken from a work counter (workspace word 16 + MODE), the
+    // shared expert's first: they have a column per token, the heaviest
+    uint32_t* work = p.err + 8 + 2 * MODE;  // [0] next unit, [1] CTAs done
+    int* s_unit = s_poff + (p.n_routed + 1);
+    const int units_s = n_units - units_r;
+    for (;;) {
+        if (tid == 0) *s_unit = (int)atomicAdd(work, 1u);
+        __syncthreads();
+        const int uw = *s_unit;
+        __syncthreads();
+        if (uw >= n_units) break;
+        const int u = uw < units_s ? units_r + uw : uw - units_s;
+        // ---- the unit: side, expert, row tile, pairs
+        int side, e = 0, rt, n, prow, tok0 = 0;
+        if (u < units_r) {
+            const int tile = u / rt_r;
+            side = 0;
+            rt = u % rt_r;
+            int lo = 0, hi = p.n_routed;
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (s_tfirst[mid] <= tile) lo = mid;
+                else hi = mid;
+            }
+            e = lo;
+            prow = s_poff[e] + (tile - s_tfirst[e]) * kBdMaxN;
+            n = min(kBdMaxN, s_poff[e + 1] - prow);
+        } else {
+            const int v = u - units_r;
+            side = 1;
+            rt = v % rt_s;
+            tok0 = (v / rt_s) * kBdMaxN;
+            n = min(kBdMaxN, p.T - tok0);
+            prow = pairs + tok0;
+        }
+        const PfSide& sd = p.side[side];
+        const int W0 = pf_w(sd.type), W1 = pf_w(sd.type2), GV = pf_gv(sd.type);
+        const int GB0 = pf_gb(sd.type), GB1 = pf_gb(sd.type2);
+        const int groups = sd.K / GV, nst = GV / 64;
+        const int N16 = (n + 15) & ~15, ntv = (n + 7) / 8;
+        const int wrow = e * sd.rows + rt * RPU;   // first weight row of the unit (per matrix)
+        const int brow = (MODE == PF_GATEUP && side == 1) ? tok0 : prow;   // first B row
+        const uint32_t raw_bytes = MODE == PF_GATEUP ? (uint32_t)(RPU * (W0 + W1)) : (uint32_t)(RPU * W0);
+        const uint32_t b_off = (raw_bytes + 1023u) & ~1023u;
+        // a group's copies, issued by the lanes of warp 0 together: lanes
+        // 0..nraw-1 one raw box each, the next lanes one 16-row B box each
+        // (lane 0 posts the byte count first)
+        const int nraw = (MODE == PF_GATEUP ? 2 : 1) * (RPU / kBoxRows);
+        const int nb16 = N16 / 16;
+        auto issue = [&](int g, int b) {
+            uint8_t* buf = bufs + (size_t)b * buf_bytes;
+            if (lane == 0) {
+                pend |= 1u << b;
+                mbar_arrive_expect_tx(&bars[b], raw_bytes + (uint32_t)(nst * N16 * 128));
+            }
+            __syncwarp();
+            if (lane < nraw) {
+                const int m = lane / (RPU / kBoxRows), q = lane % (RPU / kBoxRows);
+                if (m == 0)
+                    tma_load_2d_hint(buf + q * kBoxRows * W0, &p.wmap[side][0], (g * GB0) & ~15,
+                                     wrow + kBoxRows * q, &bars[b], stream_pol);
+                else
+                    tma_load_2d_hint(buf + RPU * W0 + q * kBoxRows * W1, &p.wmap[side][1],
+                                     (g * GB1) & ~15, wrow + kBoxRows * q, &bars[b], stream_pol);
+            }
+            for (int i = lane - nraw; i >= 0 && i < nst * nb16; i += 32 - nraw) {
+                const int st = i / nb16, r = 16 * (i % nb16);
+                tma_load_2d_hint(buf + b_off + (uint32_t)(st * kBdMaxN * 128) + r * 128, &p.bmap[side][1],
+                                 g * GV + 64 * st, brow + r, &bars[b], keep);
+            }
+        };
+        if (warp == 0) issue(0, 0);
+        // ---- this lane's weight row: 16-row MMA tiles mt = lane / 16
+        uint32_t rofs;
+        int ty;
+        // (two m-tiles: lane = staging row; one m-tile: lanes l and l + 16
+        // share staging row l % 16)
+        const int srow = kBdMT == 2 ? lane : (lane & 15);
+        if (MODE == PF_GATEUP) {
+            const int mt = srow >> 4, rr = srow & 15;
+            const int j = kBdWarpRows / 2 * warp + 8 * mt + (rr & 7);   // intermediate row in the unit
+            const bool up = rr >= 8;
+            rofs = up ? (uint32_t)(RPU * W0 + j * W1) : (uint32_t)(j * W0);
+            ty = up ? sd.type2 : sd.type;
+        } else {
+            rofs = (uint32_t)((kBdWarpRows * warp + srow) * W0);
+            ty = sd.type;
+        }
+        float acc[kBdMT][kBdMaxN / 8][4];
+#pragma unroll
+        for (int mt = 0; mt < kBdMT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < kBdMaxN / 8; ++nt)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[mt][nt][j] = 0.f;
+        // one decoder and a pair-tile count known at compile time per unit
+        auto run = [&](auto t_c) -> bool {
+            constexpr int TT = decltype(t_c)::value;
+            if (ntv <= 2) return bd_k_loop<TT, 2>(groups, bufs, buf_bytes, b_off, rofs, atile, acc, issue, wait, s_abort);
+            if (kBdMaxN <= 32 || ntv <= 4) return bd_k_loop<TT, (kBdMaxN <= 32 ? kBdMaxN / 8 : 4)>(groups, bufs, buf_bytes, b_off, rofs, atile, acc, issue, wait, s_abort);
+            return bd_k_loop<TT, kBdMaxN / 8>(groups, bufs, buf_bytes, b_off, rofs, atile, acc, issue, wait, s_abort);
+        };
+        bool ok;
+        switch (ty) {
+            case Q3_K: ok = run(std::integral_constant<int, Q3_K>{}); break;
+            case Q4_K: ok = run(std::integral_constant<int, Q4_K>{}); break;
+            case Q5_K: ok = run(std::integral_constant<int, Q5_K>{}); break;
+            case Q6_K: ok = run(std::integral_constant<int, Q6_K>{}); break;
+            default:   ok = run(std::integral_constant<int, Q8_0>{}); break;
+        }
+        if (!ok) break;
+        __syncthreads();  // the next unit's first copies reuse buffer 0
+        // ---- epilogue: C fragment rows g (c0, c1) and g + 8 (c2, c3), columns 2t, 2t + 1
+        const int gq = lane >> 2, tq = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < kBdMaxN / 8; ++nt) {
+            if (nt >= ntv) break;
+#pragma unroll
+            for (int ec = 0; ec < 2; ++ec) {
+                const int col = 8 * nt + 2 * tq + ec;
+                if (col >= n) continue;
+                int tok;
+                if (side == 0) tok = p.pair_tok[prow + col];
+                else tok = tok0 + col;
+#pragma unroll
+                for (int mt = 0; mt < kBdMT; ++mt) {
+                    if (MODE == PF_GATEUP) {
+                        // row gq of tile mt is gate row j, row gq + 8 the up row j
+                        const int j = rt * RPU + kBdWarpRows / 2 * warp + 8 * mt + gq;
+                        const float xs = p.xs_inv[tok];
+                        const float gg = __fmul_rn(acc[mt][nt][ec], xs);
+                        const float uu = __fmul_rn(acc[mt][nt][2 + ec], xs);
+                        const float a = __fdividef(gg * uu, 1.0f + __expf(-gg));
+                        if (!(fabsf(a) <= 65504.0f)) atomicCAS(p.err, 0u, (uint32_t)ST_RANGE);
+                        p.act[(size_t)(prow + col) * p.Imax + j] = __float2half_rn(a);
+                    } else {
+                        const float wgt = side == 0 ? p.pair_w[prow + col] : p.sg[tok];
+                        const int h = rt * RPU + kBdWarpRows * warp + 16 * mt + gq;
+                        float* yr = p.y + (size_t)tok * p.H;
+                        atomicAdd(yr + h, __fmul_rn(wgt, acc[mt][nt][ec]));
+                        atomicAdd(yr + h + 8, __fmul_rn(wgt, acc[mt][nt][2 + ec]));
+                    }
+                }
+            }
+        }
+    }
+    // after an abort: let the copies still in flight land before the CTA's
+    // shared memory goes away (bounded)
+    if (tid == 0)
+        for (int b = 0; b < 2; ++b)
+            if (pend & (1u << b))
+                for (uint32_t i = 0; i < kPfPolls; ++i)
+                    if (mbar_try_wait(&bars[b], (ph >> b) & 1u)) break;
+    // the last CTA out resets the work counter for the next call
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(work + 1, 1u) == gridDim.x - 1) {
+            work[0] = 0;
+            work[1] = 0;
+            __threadfence();
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // token and router preparation, top-k, pair lists
 
 struct PfPrep {
@@ -1335,6 +1721,44 @@ static cudaError_t pf_launch_gemm(PfParams& p, int grid, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// The warp-level MMA path for few tokens (k_bd_gemm): every side's gate and
+// up share one block format (a lane decodes one format for its whole row
+// tile).
+static bool bd_supported(const moe_b200_layer* L, int T, bool routed, bool shared) {
+    if (T > kBdMaxT) return false;
+    if (routed && L->gate_type != L->up_type) return false;
+    if (shared && L->shared_gate_type != L->shared_up_type) return false;
+    if (routed && (L->intermediate % 128 || L->hidden % 256)) return false;
+    if (shared && L->shared_intermediate % 128) return false;
+    return true;
+}
+
+// Buffer bytes of k_bd_gemm: raw rows of the side with the widest boxes,
+// rounded to 1 KB, plus the B tile (4 stages x kBdMaxN rows x 128 B).
+static uint32_t bd_buf_bytes(const PfParams& g, int mode) {
+    uint32_t best = 0;
+    for (int sd = 0; sd < 2; ++sd) {
+        const int w0 = pf_w(g.side[sd].type), w1 = pf_w(g.side[sd].type2);
+        const uint32_t raw = mode == PF_GATEUP ? (uint32_t)(kBdRows / 2 * (w0 + w1)) : (uint32_t)(kBdRows * w0);
+        const uint32_t b = ((raw + 1023u) & ~1023u) + 4u * kBdMaxN * 128u;
+        best = b > best ? b : best;
+    }
+    return best;
+}
+
+template <int MODE>
+static cudaError_t bd_launch(PfParams& p, int grid, cudaStream_t s) {
+    p.stage_bytes = bd_buf_bytes(p, MODE);
+    const size_t smem = 1024 + 2 * (size_t)p.stage_bytes + 8 * kBdWarpRows * 128 + 24 +
+                        (size_t)2 * (p.n_routed + 1) * 4 + 16;
+    if (smem > 232448) return cudaErrorInvalidConfiguration;
+    const cudaError_t attr = cudaFuncSetAttribute(
+        k_bd_gemm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (attr != cudaSuccess) return attr;
+    k_bd_gemm<MODE><<<grid, kBdThreads, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
 static int pf_fail(cudaError_t* ce, cudaError_t e) {
     if (ce) *ce = e;
     return ST_CUDA;
@@ -1456,7 +1880,8 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
     }
 
-    // expert GEMMs
+    // expert GEMMs: warp-level MMA for few tokens, the tcgen05 pipeline otherwise
+    const bool use_bd = bd_supported(L, T, routed, shared) && !(flags & MOE_B200_TCGEN05);
     gp.n_routed = n_routed;
     gp.has_shared = shared ? 1 : 0;
     const int act_rows = T * K + T;
@@ -1493,11 +1918,15 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
             g.side[1] = PfSide{Q8_0, Q8_0, 128, 256};
         }
         if (!ok) return ST_INTERNAL;
-        g.a_bytes = 16384;
-        g.stage_bytes = g.a_bytes + pf_stage_cols(T) * 128;
-        g.raw_slot_bytes = 64 * wmax_gu;
-        if (!pf_fit(g)) return ST_INTERNAL;
-        if ((e = pf_launch_gemm<PF_GATEUP>(g, sms, s)) != cudaSuccess) return pf_fail(ce, e);
+        if (use_bd) {
+            if ((e = bd_launch<PF_GATEUP>(g, kBdCtasPerSm * sms, s)) != cudaSuccess) return pf_fail(ce, e);
+        } else {
+            g.a_bytes = 16384;
+            g.stage_bytes = g.a_bytes + pf_stage_cols(T) * 128;
+            g.raw_slot_bytes = 64 * wmax_gu;
+            if (!pf_fit(g)) return ST_INTERNAL;
+            if ((e = pf_launch_gemm<PF_GATEUP>(g, sms, s)) != cudaSuccess) return pf_fail(ce, e);
+        }
     }
     // down
     {
@@ -1525,11 +1954,15 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
             g.side[1] = PfSide{Q8_0, Q8_0, 128, 256};
         }
         if (!ok) return ST_INTERNAL;
-        g.a_bytes = 16384;
-        g.stage_bytes = g.a_bytes + pf_stage_cols(T) * 128;
-        g.raw_slot_bytes = 128 * wmax_dn;
-        if (!pf_fit(g)) return ST_INTERNAL;
-        if ((e = pf_launch_gemm<PF_DOWN>(g, sms, s)) != cudaSuccess) return pf_fail(ce, e);
+        if (use_bd) {
+            if ((e = bd_launch<PF_DOWN>(g, kBdCtasPerSm * sms, s)) != cudaSuccess) return pf_fail(ce, e);
+        } else {
+            g.a_bytes = 16384;
+            g.stage_bytes = g.a_bytes + pf_stage_cols(T) * 128;
+            g.raw_slot_bytes = 128 * wmax_dn;
+            if (!pf_fit(g)) return ST_INTERNAL;
+            if ((e = pf_launch_gemm<PF_DOWN>(g, sms, s)) != cudaSuccess) return pf_fail(ce, e);
+        }
     }
     return ST_OK;
 }

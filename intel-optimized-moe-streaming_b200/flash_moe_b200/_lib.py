@@ -27,6 +27,7 @@ FP16_GRAPH = 1
 NO_SHARED = 2
 EXACT = 4
 SHARED_ONLY = 8
+TCGEN05 = 16
 EP_BLOB_BYTES = 128  # MOE_B200_EP_BLOB_BYTES
 STEP_CHAIN = 1
 STEP_BLOCK = 2

@@ -214,3 +214,20 @@ def test_prefill_kernel_count():
     assert n.value == 8
     assert be.lib.moe_b200_prefill_kernels(C.byref(s), 64, C.byref(n)) == 0
     assert n.value == 7
+
+
+@pytest.mark.parametrize("name,tokens", [("p_q3q4q8", 40), ("p_bias_q5", 48), ("p_h1024", 17)])
+def test_few_tokens_both_expert_gemm_paths(oracle, name, tokens):
+    """At most 48 tokens the expert GEMMs run on warp-level MMA (k_bd_gemm);
+    MOE_B200_TCGEN05 forces the tcgen05 pipeline.  Both match the oracle, and
+    each other to fp32 summation order."""
+    from flash_moe_b200 import _lib
+    lw, xs = _case(name)
+    xs = np.ascontiguousarray(xs[:tokens])
+    be = _backend(lw)
+    y0, ids0, w0 = _prefill(be, xs)
+    y1, ids1, w1 = _prefill(be, xs, flags=be.flags | _lib.TCGEN05)
+    assert np.array_equal(ids0, ids1)
+    check_prefill(oracle, lw, xs, y0, ids0, w0)
+    check_prefill(oracle, lw, xs, y1, ids1, w1)
+    assert O.max_relative_error(y0, y1) <= 2e-4
