@@ -22,8 +22,10 @@ the numpy router / combine / shared expert of its Python layer.
 
 At N = 1 the line also carries "prefill" (config 4: 4096 bf16 tokens on the
 tensor cores, TFLOP/s against the measured bf16 peak), "batched_decode"
-(config 3: 64 tokens with a Zipf(1.1) router bias) and "stack" (config 5:
-40 identity-mixer blocks, batch 1 in one launch and batch 32).
+(config 3: 64 tokens with a Zipf(1.1) router bias), "stack" (config 5:
+40 identity-mixer blocks, batch 1 in one launch and batch 32) and "delta"
+(the DeltaNet decode step, moe_delta_heads, at the model's 32 x 128 x 128
+state, with the reference's own CPU kernel timed beside it).
 
 Prints one JSON line (rank 0).
 """
@@ -289,6 +291,94 @@ def bench_batched(dev, peaks: dict, peak_kind: str) -> dict:
     return out
 
 
+def bench_delta(dev, peaks: dict, peak_kind: str, cpu: bool = True) -> dict:
+    """The DeltaNet decode step (moe_delta_heads) at the reference model's
+    linear-attention shape: 32 value heads of 128 x 128 fp32 state (2 MiB per
+    layer).  Calls rotate over 96 layer states (192 MiB > L2), one call per
+    layer as a decode step makes them; timed as stream launches, as one CUDA
+    graph of 96 calls, and through the host entry point with host arrays
+    (the reference's ctypes call, state copied in and out each call).  A
+    256-head x 512 x 512 state (256 MiB per call) shows the streaming rate.
+    Algorithmic bytes per call: the state read and written, q, k, v, output,
+    beta and gate once."""
+    import torch
+    from flash_moe_b200 import synth
+    from flash_moe_b200.native_expert import NativeDelta
+    nd = NativeDelta()
+
+    def algo(h, dk, dv):
+        return 8 * h * dv * dk + 4 * (2 * h * dk + 2 * h * dv + 2 * h)
+
+    heads, dk, dv, layers = 32, 128, 128, 96
+    states = torch.from_numpy(synth.make_delta_state(7, heads, dk, dv)).to(dev).repeat(layers, 1, 1, 1)
+    ins = [torch.from_numpy(a).to(dev) for a in synth.make_delta_step(7, 0, heads, dk, dv)]
+    ins[4].clamp_(min=-0.01)   # decay near 1 keeps the repeated steps' state bounded
+    outs = torch.empty((layers, heads, dv), device=dev)
+    counter = [0]
+
+    def one():
+        i = counter[0] % layers
+        counter[0] += 1
+        nd.forward_device(states[i], *ins, out=outs[i])
+    ms = _time_calls(one, 4 * layers, warmup=layers)
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(layers):
+                nd.forward_device(states[i], *ins, out=outs[i], stream=s)
+    ms_graph = _time_calls(graph.replay, 20) / layers
+    del graph
+    # host entry: numpy state and inputs, the reference caller's form
+    hstate = synth.make_delta_state(7, heads, dk, dv)
+    hins = synth.make_delta_step(7, 0, heads, dk, dv)
+    for _ in range(5):
+        nd.forward(hstate, *hins)
+    n_host = 200
+    t0 = time.perf_counter()
+    for _ in range(n_host):
+        nd.forward(hstate, *hins)
+    us_host = (time.perf_counter() - t0) / n_host * 1e6
+    # a large state streamed from HBM
+    H2, D2 = 256, 512
+    big = torch.empty((H2, D2, D2), device=dev).normal_(0, 0.1)
+    bins = [torch.from_numpy(a).to(dev) for a in synth.make_delta_step(8, 0, H2, D2, D2)]
+    bout = torch.empty((H2, D2), device=dev)
+    ms_big = _time_calls(lambda: nd.forward_device(big, *bins, out=bout), 10)
+    del big
+    peak = peaks["hbm_gbs"]
+    a_small, a_big = algo(heads, dk, dv), algo(H2, D2, D2)
+    gbs = a_small / (ms_graph / 1e3) / 1e9
+    gbs_big = a_big / (ms_big / 1e3) / 1e9
+    out = {"config": "DeltaNet step, 32 heads x 128 x 128 fp32 state (2 MiB), 96 layer states "
+                     "rotated (192 MiB > L2); large: 256 heads x 512 x 512 (256 MiB)",
+           "algorithmic_bytes_per_call": a_small,
+           "us_per_call_stream": round(ms * 1e3, 2),
+           "us_per_call_graph": round(ms_graph * 1e3, 2),
+           "us_per_call_host_entry": round(us_host, 1),
+           "us_per_call_large": round(ms_big * 1e3, 1),
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                        "large_achieved": round(gbs_big, 1),
+                        "large_frac": round(gbs_big / peak, 4)}}
+    if cpu:
+        import oracle as O
+        try:
+            lib, kind = O.ReferenceLibrary(), "reference"
+        except FileNotFoundError:
+            lib, kind = O.KQuantOracle(), "port"
+        cstate = synth.make_delta_state(7, heads, dk, dv)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 2.0:
+            lib.delta_heads(cstate, *hins)
+            n += 1
+        us_cpu = (time.perf_counter() - t0) / n * 1e6
+        out["cpu_baseline"] = {"us_per_call": round(us_cpu, 1), "cores": 1, "kind": kind,
+                               "sample": f"{n} calls on one 32 x 128 x 128 state (~2 s), {cpu_model()}"}
+    return out
+
+
 def bench_stack(backend, base_layer: int, dev, peaks: dict, peak_kind: str) -> dict:
     """Config 5: 40 identity-mixer blocks (RMSNorm f16 + residual around each
     MoE layer), 40 distinct resident layers (15.3 GB of packed weights), batch
@@ -478,6 +568,7 @@ def run_gpu(args) -> None:
         extra["prefill"] = bench_prefill(backend, 0, dev, peaks, peak_kind)
         extra["batched_decode"] = bench_batched(dev, peaks, peak_kind)
         extra["stack"] = bench_stack(backend, 0, dev, peaks, peak_kind)
+        extra["delta"] = bench_delta(dev, peaks, peak_kind, cpu=not args.no_cpu)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": UNIT, "n_gpus": world,
@@ -523,7 +614,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak", type=float, default=0.5)
-    ap.add_argument("--only", choices=["prefill"], default=None,
+    ap.add_argument("--only", choices=["prefill", "delta"], default=None,
                     help="run only the config-4 prefill measurement (for profiling)")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the prefill and batched-decode measurements (N = 1)")
@@ -534,6 +625,13 @@ def main() -> None:
         run_reference_arm(args)
     elif args.only == "prefill":
         run_prefill_only(args)
+    elif args.only == "delta":
+        import torch
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        peaks, peak_kind = measured_peaks()
+        print(json.dumps({"delta": bench_delta(dev, peaks, peak_kind, cpu=not args.no_cpu)}),
+              flush=True)
     else:
         run_gpu(args)
 

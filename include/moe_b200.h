@@ -18,13 +18,14 @@
  *
  * Status codes (all functions returning int): 0 success;
  *   -1 bad argument (null pointer, size <= 0 or out of range, bad flag),
- *   -2 unsupported ggml type or columns not a multiple of its block size,
+ *   -2 unsupported ggml type or columns not a multiple of its block size
+ *      (moe_delta_heads: an output is not finite, the reference's meaning),
  *   -3 tensor byte count does not match its shape,
  *   -4 an output value is not finite,
  *   -5 host-side failure (allocation),
  * and, for conditions the CPU reference cannot have,
  *   -6 a CUDA call failed (moe_b200_last_cuda_error() gives the cudaError_t),
- *   -7 a device pointer is not 16-byte aligned,
+ *   -7 a device pointer is not 16-byte aligned (4-byte for the DeltaNet step),
  *   -8 workspace too small,
  *   -9 a bounded device-side wait gave up.
  *
@@ -81,6 +82,26 @@ MOE_B200_API int moe_quant_expert(int gate_type, const uint8_t* gate, int64_t ga
                      int down_type, const uint8_t* down, int64_t down_bytes,
                      const float* input, int hidden, int intermediate, float* output,
                      int fp16_graph);
+
+/* One gated delta-rule (DeltaNet) decode step over every head, in place on
+ * the fp32 state [heads][value_dim][key_dim]:
+ *   decay = exp(double(gate[h])); row <- float(double(row) * decay);
+ *   kv = row . k[h]; delta = beta[h] * (v[h][r] - kv);
+ *   row <- row + delta * k[h]; output[h][r] = row . q[h]
+ * with q, k [heads][key_dim], v and output [heads][value_dim], beta and gate
+ * [heads].  Sums in the reference's eight-lane order: bit-identical to it.
+ * Returns 0; -1 for a null pointer, heads outside 1..256 or key_dim,
+ * value_dim outside 1..1024; -2 when an output is not finite.  On -2, as in
+ * the reference, rows up to and including the first non-finite one hold
+ * their new state and outputs are written only for the rows before it; a
+ * state in host memory keeps its later rows unchanged, a state in device
+ * memory has every row updated.  Any pointer may be host or device memory.
+ * Replaces moe_delta_heads (cpp/moe_delta.cpp:18-69); bound by ctypes in
+ * src/flash_moe/native_expert.py:76-98 (NativeDelta) and called from
+ * src/flash_moe/gated_deltanet.py:386. */
+MOE_B200_API int moe_delta_heads(float* state, const float* q, const float* k, const float* v,
+                                 const float* beta, const float* gate, float* output, int heads,
+                                 int key_dim, int value_dim);
 
 /* ------------------------------------------------------------------------
  * 2. Device-resident API
@@ -346,6 +367,19 @@ MOE_B200_API int moe_b200_expert_noalloc(int gate_type, const uint8_t* gate, int
                                          int down_type, const uint8_t* down, int64_t down_bytes,
                                          const float* input, int hidden, int intermediate,
                                          float* output, int fp16_graph, void* stream);
+
+/* moe_delta_heads on device pointers, asynchronous on `stream` (no host
+ * synchronisation, capturable in a CUDA graph).  decay = exp(double(gate))
+ * is computed on the device (CUDA's double exp: the decayed state can differ
+ * from the host entry point's in the last bit of a float, rarely).  Every
+ * row is updated and every output written.  bad_row (device int32, may be
+ * NULL) receives -1, or the smallest flat row index h * value_dim + r whose
+ * output is not finite.  Returns 0, -1 (arguments, as above), -7 for a
+ * pointer that is not 4-byte aligned, -6 on a CUDA launch failure. */
+MOE_B200_API int moe_b200_delta_heads(float* state, const float* q, const float* k,
+                                      const float* v, const float* beta, const float* gate,
+                                      float* output, int heads, int key_dim, int value_dim,
+                                      int32_t* bad_row, void* stream);
 
 /* Device-pointer dequantisation on a stream: out_dtype 0 = fp32,
  * 1 = binary16 (round to nearest even).  Same values as dequant_k. */

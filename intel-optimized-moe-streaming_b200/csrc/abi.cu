@@ -317,6 +317,136 @@ int moe_quant_expert(int gate_type, const uint8_t* gate, int64_t gate_bytes,
     }
 }
 
+// Argument checks of moe_delta_heads, in the reference's terms
+// (cpp/moe_delta.cpp:21-24).
+static bool delta_args_ok(const void* const* ptrs, int heads, int dk, int dv) {
+    for (int i = 0; i < 7; ++i)
+        if (!ptrs[i]) return false;
+    return heads >= 1 && heads <= 256 && dk >= 1 && dk <= 1024 && dv >= 1 && dv <= 1024;
+}
+
+static constexpr int DELTA_NONFINITE = -2;  // cpp/moe_delta.cpp:66
+
+int moe_delta_heads(float* state, const float* q, const float* k, const float* v,
+                    const float* beta, const float* gate, float* output, int heads,
+                    int key_dim, int value_dim) {
+    const void* all[7] = {state, q, k, v, beta, gate, output};
+    if (!delta_args_ok(all, heads, key_dim, value_dim)) return ST_ARG;
+    try {
+        Scratch* sc = thread_scratch();
+        if (!sc) return fail(cudaErrorInvalidDevice, ST_INTERNAL);
+        const size_t rows = (size_t)heads * value_dim;
+        const size_t row_bytes = (size_t)key_dim * 4;
+        // state, q, k, v, beta: used in place when on the device, else staged
+        const void* ptrs[5] = {state, q, k, v, beta};
+        const size_t bytes[5] = {rows * row_bytes, (size_t)heads * row_bytes,
+                                 (size_t)heads * row_bytes, rows * 4, (size_t)heads * 4};
+        bool dev[5];
+        size_t off[5];
+        Stager st;
+        for (int i = 0; i < 5; ++i) {
+            dev[i] = on_device(ptrs[i]) && ((uintptr_t)ptrs[i] & 3u) == 0;
+            off[i] = dev[i] ? 0 : st.take(bytes[i]);
+        }
+        const size_t o_decay = st.take((size_t)heads * 8);
+        const size_t o_out = st.take(rows * 4);
+        const size_t o_bad = st.take(4);
+        cudaError_t e = sc->ensure(st.used);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        char* base = static_cast<char*>(sc->buf);
+        void* dptr[5];
+        for (int i = 0; i < 5; ++i) {
+            if (dev[i]) {
+                dptr[i] = const_cast<void*>(ptrs[i]);
+            } else {
+                dptr[i] = base + off[i];
+                e = cudaMemcpyAsync(dptr[i], ptrs[i], bytes[i], cudaMemcpyDefault, sc->stream);
+                if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+            }
+        }
+        // decay = exp(double(gate)) on the host, with the same libm as the
+        // reference's std::exp, so the decayed state has its bits
+        std::vector<float> g(heads);
+        e = cudaMemcpyAsync(g.data(), gate, (size_t)heads * 4, cudaMemcpyDefault, sc->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        std::vector<double> decay(heads);
+        for (int h = 0; h < heads; ++h) decay[h] = std::exp(static_cast<double>(g[h]));
+        e = cudaMemcpyAsync(base + o_decay, decay.data(), (size_t)heads * 8,
+                            cudaMemcpyHostToDevice, sc->stream);
+        if (e == cudaSuccess) e = cudaMemsetAsync(base + o_bad, 0xFF, 4, sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        DeltaArgs a{};
+        a.state = static_cast<float*>(dptr[0]);
+        a.q = static_cast<const float*>(dptr[1]);
+        a.k = static_cast<const float*>(dptr[2]);
+        a.v = static_cast<const float*>(dptr[3]);
+        a.beta = static_cast<const float*>(dptr[4]);
+        a.gate = nullptr;
+        a.decay = reinterpret_cast<const double*>(base + o_decay);
+        a.out = reinterpret_cast<float*>(base + o_out);
+        a.bad = reinterpret_cast<unsigned*>(base + o_bad);
+        a.heads = heads;
+        a.dk = key_dim;
+        a.dv = value_dim;
+        e = launch_delta_heads(a, sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        unsigned bad = 0;
+        e = cudaMemcpyAsync(&bad, a.bad, 4, cudaMemcpyDeviceToHost, sc->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        // the reference stops at the first non-finite output: rows up to and
+        // including it hold their new state, later rows keep the old one, and
+        // outputs are written for the rows before it (cpp/moe_delta.cpp:64-67)
+        const bool ok = bad == 0xFFFFFFFFu;
+        const size_t n_state = ok ? rows : (size_t)bad + 1;
+        const size_t n_out = ok ? rows : (size_t)bad;
+        if (!dev[0]) {
+            e = cudaMemcpyAsync(state, a.state, n_state * row_bytes, cudaMemcpyDefault, sc->stream);
+            if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        }
+        if (n_out) {
+            e = cudaMemcpyAsync(output, a.out, n_out * 4, cudaMemcpyDefault, sc->stream);
+            if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        }
+        e = cudaStreamSynchronize(sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        return ok ? ST_OK : DELTA_NONFINITE;
+    } catch (...) {
+        return ST_INTERNAL;
+    }
+}
+
+int moe_b200_delta_heads(float* state, const float* q, const float* k, const float* v,
+                         const float* beta, const float* gate, float* output, int heads,
+                         int key_dim, int value_dim, int32_t* bad_row, void* stream) {
+    const void* all[7] = {state, q, k, v, beta, gate, output};
+    if (!delta_args_ok(all, heads, key_dim, value_dim)) return ST_ARG;
+    for (const void* p : all)
+        if ((uintptr_t)p & 3u) return ST_ALIGN;
+    if ((uintptr_t)bad_row & 3u) return ST_ALIGN;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (bad_row) {
+        cudaError_t e = cudaMemsetAsync(bad_row, 0xFF, 4, s);
+        if (e != cudaSuccess) return fail(e, ST_CUDA);
+    }
+    DeltaArgs a{};
+    a.state = state;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.beta = beta;
+    a.gate = gate;
+    a.decay = nullptr;
+    a.out = output;
+    a.bad = reinterpret_cast<unsigned*>(bad_row);
+    a.heads = heads;
+    a.dk = key_dim;
+    a.dv = value_dim;
+    cudaError_t e = launch_delta_heads(a, s);
+    return e == cudaSuccess ? ST_OK : fail(e, ST_CUDA);
+}
+
 int moe_b200_dequant(int type, const void* src, void* dst, int64_t n, int out_dtype,
                      void* stream) {
     const int bs = block_size(type);

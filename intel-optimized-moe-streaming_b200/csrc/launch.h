@@ -31,6 +31,24 @@ struct Stager {
 cudaError_t launch_dequant(int type, const void* src, void* dst, int64_t n, bool f16,
                            cudaStream_t stream);
 
+// One DeltaNet step (cpp/moe_delta.cpp:18-69), all pointers on the device.
+// decay: per-head exp(gate) computed by the caller, or null to compute it on
+// the device from gate.  bad: null, or a word the kernel lowers (atomicMin)
+// to the flat index h * dv + r of every row whose output is not finite.
+struct DeltaArgs {
+    float* state;          // [heads][dv][dk], updated in place
+    const float* q;        // [heads][dk]
+    const float* k;        // [heads][dk]
+    const float* v;        // [heads][dv]
+    const float* beta;     // [heads]
+    const float* gate;     // [heads]
+    const double* decay;   // [heads] or null
+    float* out;            // [heads][dv]
+    unsigned* bad;
+    int heads, dk, dv;
+};
+cudaError_t launch_delta_heads(const DeltaArgs& a, cudaStream_t stream);
+
 // Routing of T tokens: fp32 scores [T x E] (+ bias), top-K ids/weights, and
 // the shared-expert gate sigmoid(x . gate_inp) per token.
 struct RoutePlan {

@@ -89,6 +89,8 @@ def _bind(lib: C.CDLL) -> None:
         "moe_b200_prefill_supported": (i, [C.POINTER(Layer)]),
         "moe_b200_prefill_kernels": (i, [C.POINTER(Layer), C.c_int32, C.POINTER(C.c_int)]),
         "moe_b200_dequant": (i, [i, vp, vp, i64, i, vp]),
+        "moe_delta_heads": (i, [vp] * 7 + [i] * 3),
+        "moe_b200_delta_heads": (i, [vp] * 7 + [i] * 3 + [vp, vp]),
         "moe_b200_expert_noalloc": (i, [i, vp, i64] * 3 + [vp, i, i, vp, i, vp]),
         "moe_b200_last_cuda_error": (i, []),
         "moe_b200_workspace_init": (i, [vp, C.c_size_t, vp]),

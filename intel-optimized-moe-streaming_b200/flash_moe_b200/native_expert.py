@@ -7,6 +7,12 @@ byte buffers go to ``moe_quant_expert`` (here the sm_100a kernel), a nonzero
 status raises ``RuntimeError("native expert failed with status N")``.  Like
 the reference it passes ``fp16_graph=1`` unless told otherwise.
 
+``NativeDelta(library).forward(state, q, k, v, beta, gate)`` is the
+reference's DeltaNet binding (``native_expert.py:76-98``) over the sm_100a
+``moe_delta_heads``: same shapes, checks, in-place state update and
+``RuntimeError("native DeltaNet failed with status N")``.  ``NativeExpert``
+exposes it as ``.delta`` like the reference (``native_expert.py:21``).
+
 ``load_native_expert(mode, library, device, tensor_types)`` keeps the
 reference's ``auto|native|openvino`` policy (``native_expert.py:40-75``): the
 gate is a visible CUDA device instead of a CPU with AVX2/FMA/F16C, and
@@ -33,10 +39,7 @@ class NativeExpert:
             _lib._bind(self.library)
         self.function = self.library.moe_quant_expert
         self.fp16_graph = int(fp16_graph)
-        # moe_delta_heads (DeltaNet) is not part of this library; callers
-        # fall back to their NumPy recurrence as the reference does when the
-        # symbol is absent (native_expert.py:21).
-        self.delta = None
+        self.delta = NativeDelta(self.library) if hasattr(self.library, "moe_delta_heads") else None
 
     def forward(self, tensors, kinds, activation, hidden, intermediate):
         arrays = [np.frombuffer(tensors[name], np.uint8) if isinstance(tensors[name], (bytes, bytearray))
@@ -53,6 +56,58 @@ class NativeExpert:
                              out.ctypes.data, self.fp16_graph)
         if code:
             raise RuntimeError(f"native expert failed with status {code}")
+        return out
+
+
+class NativeDelta:
+    """All-head fp32 DeltaNet state update on the GPU (``moe_delta_heads``)."""
+
+    def __init__(self, library=None):
+        self.library = library if library is not None else _lib.load()
+        self.function = self.library.moe_delta_heads
+        self.function.argtypes = [C.c_void_p] * 7 + [C.c_int] * 3
+        self.function.restype = C.c_int
+
+    def forward(self, state, q, k, v, beta, gate):
+        """Host arrays, as the reference: ``state`` (heads, value_dim,
+        key_dim) fp32 C-contiguous, updated in place; returns the
+        (heads, value_dim) output."""
+        if state.dtype != np.float32 or not state.flags.c_contiguous:
+            raise ValueError("DeltaNet state must be contiguous FP32")
+        nv, dv, dk = state.shape
+        arrays = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v, beta, gate)]
+        shapes = [(nv, dk), (nv, dk), (nv, dv), (nv,), (nv,)]
+        if any(a.shape != shape for a, shape in zip(arrays, shapes)):
+            raise ValueError("DeltaNet native input shape mismatch")
+        out = np.empty((nv, dv), np.float32)
+        pointers = [state.ctypes.data] + [a.ctypes.data for a in arrays] + [out.ctypes.data]
+        code = self.function(*pointers, nv, dk, dv)
+        if code:
+            raise RuntimeError(f"native DeltaNet failed with status {code}")
+        return out
+
+    def forward_device(self, state, q, k, v, beta, gate, out=None, bad_row=None, stream=None):
+        """CUDA tensors, asynchronous on ``stream`` (default: torch's current
+        stream) through ``moe_b200_delta_heads``: no host synchronisation.
+        ``bad_row`` (int32 CUDA tensor of one element, optional) receives -1
+        or the first flat row whose output is not finite."""
+        import torch
+        if state.dtype != torch.float32 or not state.is_contiguous() or not state.is_cuda:
+            raise ValueError("DeltaNet state must be a contiguous FP32 CUDA tensor")
+        nv, dv, dk = state.shape
+        ins = [t.contiguous() for t in (q, k, v, beta, gate)]
+        shapes = [(nv, dk), (nv, dk), (nv, dv), (nv,), (nv,)]
+        for t, shape in zip(ins, shapes):
+            if tuple(t.shape) != shape or t.dtype != torch.float32 or t.device != state.device:
+                raise ValueError("DeltaNet device input shape, dtype or device mismatch")
+        if out is None:
+            out = torch.empty((nv, dv), dtype=torch.float32, device=state.device)
+        handle = (stream if stream is not None else torch.cuda.current_stream(state.device)).cuda_stream
+        code = self.library.moe_b200_delta_heads(
+            state.data_ptr(), *(t.data_ptr() for t in ins), out.data_ptr(), nv, dk, dv,
+            bad_row.data_ptr() if bad_row is not None else None, handle)
+        if code:
+            raise RuntimeError(f"native DeltaNet failed with status {code}")
         return out
 
 
@@ -84,6 +139,7 @@ def load_native_expert(mode, library, device, tensor_types):
             reason = f"kernel unavailable ({error})"
         else:
             print("[Experts] native quantized B200 decode")
+            print("[DeltaNet] native FP32 decode recurrence (B200)")
             return result
     if mode == "native":
         raise RuntimeError(reason)

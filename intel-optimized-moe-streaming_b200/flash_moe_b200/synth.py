@@ -221,3 +221,30 @@ def digest(*arrays: np.ndarray) -> str:
     for a in arrays:
         h.update(np.ascontiguousarray(a).view(np.uint8).tobytes())
     return h.hexdigest()
+
+
+S_DELTA_STATE, S_DELTA_STEP = 200, 201
+
+
+def make_delta_state(seed: int, heads: int, key_dim: int, value_dim: int,
+                     scale: float = 0.1) -> np.ndarray:
+    """A DeltaNet recurrent state [heads, value_dim, key_dim] ~ N(0, scale)."""
+    rng = _rng(seed, 0, S_DELTA_STATE)
+    return (rng.standard_normal((heads, value_dim, key_dim)) * scale).astype(np.float32)
+
+
+def make_delta_step(seed: int, step: int, heads: int, key_dim: int, value_dim: int):
+    """Per-token DeltaNet inputs with the value ranges of the reference's
+    caller (``src/flash_moe/gated_deltanet.py:340-386``): q and k L2-normalised
+    per head, q scaled by 1/sqrt(key_dim), v ~ N(0, 1), beta = sigmoid(.) in
+    (0, 1), gate = a log-decay <= 0 (decay = exp(gate) in (0, 1]).
+    Returns (q, k, v, beta, gate) as float32 arrays."""
+    rng = _rng(seed, step, S_DELTA_STEP)
+    q = rng.standard_normal((heads, key_dim))
+    k = rng.standard_normal((heads, key_dim))
+    q = q / np.sqrt((q * q).sum(-1, keepdims=True) + 1e-6) / np.sqrt(key_dim)
+    k = k / np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+    v = rng.standard_normal((heads, value_dim))
+    beta = 1.0 / (1.0 + np.exp(-rng.standard_normal(heads)))
+    gate = -np.log1p(np.exp(rng.standard_normal(heads))) * rng.uniform(0.05, 1.5, heads)
+    return tuple(np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v, beta, gate))

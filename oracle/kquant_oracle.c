@@ -299,3 +299,74 @@ int kq_expert(int gate_type, const uint8_t* gate, int64_t gate_bytes,
     free(act);
     return status;
 }
+
+/* ------------------------------------------------------- DeltaNet step */
+
+/* Sum of an eight-lane accumulator, lanes 0..7 into a zero start value
+   (sum8, cpp/moe_delta.cpp:10-16). */
+static float kq_sum8(const float lanes[8]) {
+    float s = 0.0f;
+    for (int l = 0; l < 8; ++l) s += lanes[l];
+    return s;
+}
+
+/* Restates moe_delta_heads (cpp/moe_delta.cpp:18-69).  Per head h:
+ *   decay = exp((double)gate[h]);
+ * per state row r (key_dim values):
+ *   row[j] <- (float)((double)row[j] * decay)                (stored)
+ *   kv     = sum_j row[j] * k[h][j]  -- eight lanes (lane = j % 8) over the
+ *            whole groups of eight, summed lanes 0..7, then the tail j in
+ *            order; each term one multiply then one add, no fusing
+ *   delta  = beta[h] * (v[h][r] - kv)
+ *   row[j] <- row[j] + delta * k[h][j]                       (stored)
+ *   out    = sum_j row[j] * q[h][j]  -- same lane order as kv
+ * A non-finite out returns -2 at once: this row and every row before it are
+ * already updated, its output and every later row are untouched. */
+int kq_delta_heads(float* state, const float* q, const float* k,
+                   const float* v, const float* beta, const float* gate,
+                   float* output, int heads, int key_dim, int value_dim) {
+    if (!state || !q || !k || !v || !beta || !gate || !output ||
+        heads < 1 || heads > 256 || key_dim < 1 || key_dim > 1024 ||
+        value_dim < 1 || value_dim > 1024)
+        return -1;
+    const int whole = key_dim - key_dim % 8;
+    for (int h = 0; h < heads; ++h) {
+        const double decay = exp((double)gate[h]);
+        const float* kh = k + (int64_t)h * key_dim;
+        const float* qh = q + (int64_t)h * key_dim;
+        for (int r = 0; r < value_dim; ++r) {
+            float* row = state + ((int64_t)h * value_dim + r) * key_dim;
+            float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            int j = 0;
+            for (; j < whole; ++j) {
+                row[j] = (float)((double)row[j] * decay);
+                const float p = row[j] * kh[j];
+                lanes[j % 8] = lanes[j % 8] + p;
+            }
+            float kv = kq_sum8(lanes);
+            for (; j < key_dim; ++j) {
+                row[j] = (float)((double)row[j] * decay);
+                const float p = row[j] * kh[j];
+                kv = kv + p;
+            }
+            const float delta = beta[h] * (v[(int64_t)h * value_dim + r] - kv);
+            for (int l = 0; l < 8; ++l) lanes[l] = 0.0f;
+            for (j = 0; j < whole; ++j) {
+                const float t = delta * kh[j];
+                row[j] = row[j] + t;
+                const float p = row[j] * qh[j];
+                lanes[j % 8] = lanes[j % 8] + p;
+            }
+            float result = kq_sum8(lanes);
+            for (; j < key_dim; ++j) {
+                const float t = delta * kh[j];
+                row[j] = row[j] + t;
+                const float p = row[j] * qh[j];
+                result = result + p;
+            }
+            if (!isfinite(result)) return -2;
+            output[(int64_t)h * value_dim + r] = result;
+        }
+    }
+    return 0;
+}

@@ -8,6 +8,7 @@
  * It restates, in plain scalar C, the algorithms of
  *   cpp/dequant_k.cpp      (block decoders, f16<->f32, the dequant_k export)
  *   cpp/moe_quant_dot.cpp  (quant_dot and the moe_quant_expert export)
+ *   cpp/moe_delta.cpp      (the moe_delta_heads DeltaNet recurrence step)
  * of vin10122/Intel-optimized-MoE-streaming, including the reference's
  * 8-lane accumulation order, so that on the same host it reproduces the
  * reference library bit for bit.  The block formats themselves are those of
@@ -55,6 +56,13 @@ int kq_expert(int gate_type, const uint8_t* gate, int64_t gate_bytes,
               int down_type, const uint8_t* down, int64_t down_bytes,
               const float* input, int hidden, int intermediate, float* output,
               int fp16_graph);
+
+/* Same contract as the reference export moe_delta_heads
+   (cpp/moe_delta.cpp:18-69): one gated delta-rule step over every head's
+   fp32 state, in place, status codes and early stop included. */
+int kq_delta_heads(float* state, const float* q, const float* k,
+                   const float* v, const float* beta, const float* gate,
+                   float* output, int heads, int key_dim, int value_dim);
 
 #ifdef __cplusplus
 }

@@ -71,10 +71,13 @@ def _bind(lib: C.CDLL, dequant: str, expert: str):
 class _KQuantLib:
     """Common numpy-facing wrapper over a library with the reference ABI."""
 
-    def __init__(self, path: Path, dequant: str, expert: str):
+    def __init__(self, path: Path, dequant: str, expert: str, delta: str):
         self.path = Path(path)
         self.lib = C.CDLL(str(self.path))
         self._dequant, self._expert = _bind(self.lib, dequant, expert)
+        self._delta = getattr(self.lib, delta)
+        self._delta.argtypes = [C.c_void_p] * 7 + [C.c_int] * 3
+        self._delta.restype = C.c_int
 
     def dequant(self, type_id: int, raw: np.ndarray, n: int | None = None,
                 want_f16: bool = False) -> tuple[int, np.ndarray]:
@@ -101,12 +104,28 @@ class _KQuantLib:
                           out.ctypes.data, fp16_graph)
         return rc, out
 
+    def delta_heads(self, state: np.ndarray, q, k, v, beta, gate,
+                    out: np.ndarray | None = None) -> tuple[int, np.ndarray]:
+        """One DeltaNet step in place on ``state`` [heads, value_dim, key_dim]
+        (``cpp/moe_delta.cpp:18-69``).  ``out`` [heads, value_dim] defaults to
+        NaN so rows the call does not write are visible."""
+        if state.dtype != np.float32 or not state.flags.c_contiguous:
+            raise ValueError("state must be contiguous float32")
+        heads, dv, dk = state.shape
+        arrays = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v, beta, gate)]
+        if out is None:
+            out = np.full((heads, dv), np.nan, np.float32)
+        rc = self._delta(state.ctypes.data, *(a.ctypes.data for a in arrays),
+                         out.ctypes.data, heads, dk, dv)
+        return rc, out
+
 
 class KQuantOracle(_KQuantLib):
     """The scalar C restatement (``kquant_oracle.c``)."""
 
     def __init__(self, path: Path | None = None):
-        super().__init__(path or build_oracle(), "kq_dequant", "kq_expert")
+        super().__init__(path or build_oracle(), "kq_dequant", "kq_expert",
+                         "kq_delta_heads")
 
 
 class ReferenceLibrary(_KQuantLib):
@@ -116,7 +135,7 @@ class ReferenceLibrary(_KQuantLib):
         path = path or REF_LIB
         if not Path(path).exists():
             raise FileNotFoundError(f"reference library not built: {path}")
-        super().__init__(path, "dequant_k", "moe_quant_expert")
+        super().__init__(path, "dequant_k", "moe_quant_expert", "moe_delta_heads")
 
 
 # ---------------------------------------------------------------- numpy layer

@@ -101,3 +101,35 @@ def oracle_layer(lib, lw, xs, fp16_graph: int = 0, selections=None):
         ids.append(e)
         ws.append(w)
     return np.stack(ys), np.array(ids), np.array(ws)
+
+
+# DeltaNet step cases: name -> (seed, heads, key_dim, value_dim, steps).
+# "model" is the reference model's linear-attention shape (32 value heads of
+# 128 x 128); the others cover the lane tail (key_dim % 8, up to 7), key_dim
+# < 8, each register-blocking width of the GPU kernel (key_dim / 8 up to 1,
+# 2, 4, 8, 16, 32 and above), the size limits of each argument, and a
+# poisoned value that stops the step.
+DELTA_SPECS = {
+    "model": (31, 32, 128, 128, 3),
+    "odd": (32, 3, 100, 37, 3),
+    "dk7": (33, 5, 7, 9, 2),
+    "one": (34, 1, 1, 1, 2),
+    "wide": (35, 1, 1024, 64, 1),
+    "dk64": (39, 4, 64, 48, 2),
+    "dk263": (40, 2, 263, 40, 2),
+    "tall": (36, 2, 16, 1024, 1),
+    "many_heads": (37, 256, 8, 8, 2),
+    "poison": (38, 3, 24, 10, 1),
+}
+# (head, row) of the poisoned case whose value is +inf
+DELTA_POISON = (1, 4)
+
+
+def delta_case(name: str):
+    """(state, [(q, k, v, beta, gate) per step]) of a DeltaNet case."""
+    seed, heads, dk, dv, steps = DELTA_SPECS[name]
+    state = synth.make_delta_state(seed, heads, dk, dv)
+    inputs = [synth.make_delta_step(seed, s, heads, dk, dv) for s in range(steps)]
+    if name == "poison":
+        inputs[0][2][DELTA_POISON] = np.inf
+    return state, inputs

@@ -12,6 +12,8 @@ What produces the expected values:
     ``dequant_k`` export (compiled from ``cpp/dequant_k.cpp``) for binary16;
   * single experts: the reference's ``moe_quant_expert`` export
     (``cpp/moe_quant_dot.cpp:171``), both ``fp16_graph`` modes;
+  * DeltaNet steps: the reference's ``moe_delta_heads`` export
+    (``cpp/moe_delta.cpp:18-69``), several steps on one state per case;
   * MoE layers and sequences: the reference's own Python
     (``flash_moe.moe_layer.run_moe_layer`` / ``run_moe_sequence``,
     ``flash_moe.router.ExpertRouter``, ``flash_moe.shared_expert.SharedExpert``,
@@ -40,7 +42,7 @@ sys.path.insert(0, str(ROOT / "intel-optimized-moe-streaming_b200"))
 sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(ROOT / "tests"))
 
-from cases import LAYER_SPECS, TRIPLES, layer_case, layer_digest, small_expert_inputs  # noqa: E402
+from cases import DELTA_SPECS, LAYER_SPECS, delta_case, TRIPLES, layer_case, layer_digest, small_expert_inputs  # noqa: E402
 from flash_moe_b200 import synth  # noqa: E402
 from flash_moe_b200.formats import BLOCK, Q3_K, Q4_K, Q5_K, Q6_K, Q8_0  # noqa: E402
 
@@ -119,6 +121,36 @@ def golden_expert_cfg1(ref) -> None:
         out[f"y{fg}"] = y
         out[f"rc{fg}"] = np.int32(rc)
     np.savez_compressed(OUT / "expert_cfg1.npz", **out)
+
+
+def golden_delta(ref) -> None:
+    out = {}
+    for name in DELTA_SPECS:
+        state, steps = delta_case(name)
+        out[f"{name}_digest"] = np.array(synth.digest(state, *[a for st in steps for a in st]))
+        ys, rcs = [], []
+        for q, k, v, beta, gate in steps:
+            rc, y = ref.delta_heads(state, q, k, v, beta, gate)
+            ys.append(y)
+            rcs.append(rc)
+        out[f"{name}_y"] = np.stack(ys)
+        out[f"{name}_rc"] = np.array(rcs, np.int32)
+        out[f"{name}_state_sha"] = np.array(synth.digest(state))
+        if state.size <= 4096:
+            out[f"{name}_state"] = state.copy()
+    # argument checks: one head of 8 x 8, then each limit crossed
+    state, steps = delta_case("many_heads")
+    q, k, v, beta, gate = steps[0]
+    bad = {"heads0": (0, 8, 8), "heads257": (257, 8, 8), "dk0": (1, 0, 8),
+           "dk1025": (1, 1025, 8), "dv0": (1, 8, 0), "dv1025": (1, 8, 1025)}
+    for key, (h, dk, dv) in bad.items():
+        out[f"rc_{key}"] = np.int32(ref._delta(state.ctypes.data, q.ctypes.data, k.ctypes.data,
+                                               v.ctypes.data, beta.ctypes.data, gate.ctypes.data,
+                                               v.ctypes.data, h, dk, dv))
+    out["rc_null"] = np.int32(ref._delta(None, q.ctypes.data, k.ctypes.data, v.ctypes.data,
+                                         beta.ctypes.data, gate.ctypes.data, v.ctypes.data, 1, 8, 8))
+    np.savez_compressed(OUT / "delta.npz", **out)
+    print("delta ok", {n: out[f"{n}_rc"].tolist() for n in DELTA_SPECS})
 
 
 class RefBackend:
@@ -203,6 +235,9 @@ def golden_layers(ref) -> None:
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="regenerate only these fixture groups "
+                         "(delta dequant expert_small expert_cfg1 layers)")
     args = ap.parse_args()
     import oracle as O
     O.build_oracle()
@@ -214,10 +249,14 @@ def main() -> int:
     with tempfile.TemporaryDirectory() as tmp:
         stub_openvino(Path(tmp))
         sys.path.insert(0, str(Path(args.reference) / "src"))
-        golden_dequant(ref, gguf)
-        golden_expert_small(ref)
-        golden_expert_cfg1(ref)
-        golden_layers(ref)
+        groups = {"delta": lambda: golden_delta(ref),
+                  "dequant": lambda: golden_dequant(ref, gguf),
+                  "expert_small": lambda: golden_expert_small(ref),
+                  "expert_cfg1": lambda: golden_expert_cfg1(ref),
+                  "layers": lambda: golden_layers(ref)}
+        for name, make in groups.items():
+            if args.only is None or name in args.only:
+                make()
     print("fixtures written to", OUT)
     return 0
 

@@ -93,3 +93,40 @@ def test_decode_rejects_bad_layer(lib):
     need = C.c_size_t(0)
     assert lib.moe_b200_decode_workspace(C.byref(L), 1, C.byref(need)) == -1
     assert lib.moe_b200_decode_workspace(None, 1, C.byref(need)) == -1
+
+
+def test_delta_heads_argument_errors(lib, golden):
+    """moe_delta_heads rejects what the reference rejects (-1), before any
+    device work; the reference's own statuses are in the golden fixture."""
+    g = golden("delta")
+    state = np.zeros((2, 8, 8), np.float32)
+    vec = np.zeros(8 * 8, np.float32)
+    p = [state.ctypes.data] + [vec.ctypes.data] * 6
+    bad = {"heads0": (0, 8, 8), "heads257": (257, 8, 8), "dk0": (1, 0, 8),
+           "dk1025": (1, 1025, 8), "dv0": (1, 8, 0), "dv1025": (1, 8, 1025)}
+    for key, (h, dk, dv) in bad.items():
+        assert lib.moe_delta_heads(*p, h, dk, dv) == int(g[f"rc_{key}"]) == -1, key
+        assert lib.moe_b200_delta_heads(*p, h, dk, dv, None, None) == -1, key
+    for i in range(7):
+        q = list(p)
+        q[i] = None
+        assert lib.moe_delta_heads(*q, 1, 8, 8) == int(g["rc_null"]) == -1
+        assert lib.moe_b200_delta_heads(*q, 1, 8, 8, None, None) == -1
+    odd = list(p)
+    odd[1] = vec.ctypes.data + 2
+    assert lib.moe_b200_delta_heads(*odd, 1, 8, 8, None, None) == -7
+
+
+def test_native_delta_checks_shapes_like_the_reference():
+    from flash_moe_b200.native_expert import NativeDelta
+    nd = NativeDelta()
+    state = np.zeros((2, 4, 8), np.float32)
+    q = k = np.zeros((2, 8), np.float32)
+    v = np.zeros((2, 4), np.float32)
+    b = g = np.zeros(2, np.float32)
+    with pytest.raises(ValueError, match="contiguous FP32"):
+        nd.forward(state.astype(np.float64), q, k, v, b, g)
+    with pytest.raises(ValueError, match="contiguous FP32"):
+        nd.forward(np.zeros((2, 8, 4), np.float32).transpose(0, 2, 1), q, k, v, b, g)
+    with pytest.raises(ValueError, match="shape mismatch"):
+        nd.forward(state, q, k, np.zeros((2, 5), np.float32), b, g)

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from cases import LAYER_SPECS, TRIPLES, layer_case, layer_digest, oracle_layer, small_expert_inputs
+from cases import DELTA_POISON, DELTA_SPECS, LAYER_SPECS, delta_case, TRIPLES, layer_case, layer_digest, oracle_layer, small_expert_inputs
 from flash_moe_b200 import synth
 
 TYPES = [8, 11, 12, 13, 14]
@@ -141,3 +141,56 @@ def test_oracle_matches_reference_library_when_built(oracle):
         a, b = oracle.expert(tensors, kinds, x, 512, 256, fg), ref.expert(tensors, kinds, x, 512, 256, fg)
         assert a[0] == b[0]
         np.testing.assert_array_equal(a[1].view(np.uint32), b[1].view(np.uint32))
+
+
+@pytest.mark.parametrize("name", list(DELTA_SPECS))
+def test_delta_step_bits_match_reference(oracle, golden, name):
+    """``kq_delta_heads`` reproduces ``moe_delta_heads`` step after step:
+    outputs (NaN where the call wrote nothing), statuses and the final state,
+    bit for bit."""
+    g = golden("delta")
+    state, steps = delta_case(name)
+    assert synth.digest(state, *[a for st in steps for a in st]) == str(g[f"{name}_digest"])
+    ys, rcs = [], []
+    for q, k, v, beta, gate in steps:
+        rc, y = oracle.delta_heads(state, q, k, v, beta, gate)
+        ys.append(y)
+        rcs.append(rc)
+    assert rcs == g[f"{name}_rc"].tolist()
+    np.testing.assert_array_equal(np.stack(ys).view(np.uint32), g[f"{name}_y"].view(np.uint32))
+    assert synth.digest(state) == str(g[f"{name}_state_sha"])
+    if f"{name}_state" in g:
+        np.testing.assert_array_equal(state.view(np.uint32), g[f"{name}_state"].view(np.uint32))
+
+
+def test_delta_poison_stops_at_the_failing_row(golden):
+    """The reference's early stop: rows after the poisoned one keep their
+    input state and get no output."""
+    g = golden("delta")
+    before, _ = delta_case("poison")
+    after = g["poison_state"]
+    h, r = DELTA_POISON
+    y = g["poison_y"][0]
+    assert int(g["poison_rc"][0]) == -2
+    assert np.isfinite(y.reshape(-1)[:h * y.shape[1] + r]).all()
+    assert np.isnan(y.reshape(-1)[h * y.shape[1] + r:]).all()
+    flat_b = before.reshape(-1, before.shape[-1])
+    flat_a = after.reshape(-1, after.shape[-1])
+    stop = h * before.shape[1] + r
+    np.testing.assert_array_equal(flat_a[stop + 1:], flat_b[stop + 1:])
+    assert not np.array_equal(flat_a[:stop + 1], flat_b[:stop + 1])
+
+
+def test_delta_status_codes_match_reference(oracle, golden):
+    g = golden("delta")
+    state, steps = delta_case("many_heads")
+    q, k, v, beta, gate = steps[0]
+    bad = {"heads0": (0, 8, 8), "heads257": (257, 8, 8), "dk0": (1, 0, 8),
+           "dk1025": (1, 1025, 8), "dv0": (1, 8, 0), "dv1025": (1, 8, 1025)}
+    for key, (h, dk, dv) in bad.items():
+        rc = oracle._delta(state.ctypes.data, q.ctypes.data, k.ctypes.data, v.ctypes.data,
+                           beta.ctypes.data, gate.ctypes.data, v.ctypes.data, h, dk, dv)
+        assert rc == int(g[f"rc_{key}"]) == -1, key
+    rc = oracle._delta(None, q.ctypes.data, k.ctypes.data, v.ctypes.data, beta.ctypes.data,
+                       gate.ctypes.data, v.ctypes.data, 1, 8, 8)
+    assert rc == int(g["rc_null"]) == -1
