@@ -333,6 +333,14 @@ int moe_delta_heads(float* state, const float* q, const float* k, const float* v
     const void* all[7] = {state, q, k, v, beta, gate, output};
     if (!delta_args_ok(all, heads, key_dim, value_dim)) return ST_ARG;
     try {
+        bool any_device = false;
+        for (const void* p : all) any_device = any_device || on_device(p);
+        if (!any_device) {   // the reference caller's form: every array on the host
+            cudaError_t ce = cudaSuccess;
+            const int rc = delta_heads_host(state, q, k, v, beta, gate, output, heads, key_dim,
+                                            value_dim, &ce);
+            return rc == ST_INTERNAL ? fail(ce, ST_INTERNAL) : rc;
+        }
         Scratch* sc = thread_scratch();
         if (!sc) return fail(cudaErrorInvalidDevice, ST_INTERNAL);
         const size_t rows = (size_t)heads * value_dim;

@@ -18,10 +18,9 @@
 // reference's order, the lane sums are gathered by shuffles and added 0..7 in
 // every thread, and the tail is added in every thread.  Every operation is
 // an explicitly rounded intrinsic (no contraction).  The decayed row stays
-// in registers between the two passes (key_dim <= 263), so each state byte
-// is read once and written once: the step is HBM bound at
-// 8 * heads * value_dim * key_dim bytes.  Wider rows (up to 1024) run a
-// variant that re-reads the row (from L1/L2) in the second pass.
+// in registers between the two passes (up to the 1024-value limit), so each
+// state byte is read once and written once: the step is HBM bound at
+// 8 * heads * value_dim * key_dim bytes.
 //
 // A non-finite output records the smallest flat row index h * value_dim + r
 // in a device word (atomicMin); the host entry point uses it to reproduce
@@ -48,11 +47,15 @@ __device__ __forceinline__ float lane_sum8(float acc) {
     return s;
 }
 
-// NC > 0: up to NC whole chunks of eight per row, held in registers.
-// NC == 0: any row width, the second pass re-reads the row.
+// Each thread holds its lane of up to NC whole chunks of eight in registers
+// (NC * 8 >= key_dim - key_dim % 8), so every state byte is read once and
+// written once.  All loads of a row (state, k, q, tail, v, beta, gate) are
+// issued before the first use; with NC <= 32 k and q stay in registers too,
+// wider rows re-read them from L1 (one head's k and q serve all its rows).
 template <int NC>
 __global__ void __launch_bounds__(kDeltaThreads)
 k_delta_heads(DeltaArgs a) {
+    constexpr bool kRegKQ = NC <= 32;
     const int lane = threadIdx.x & 7;
     const int sub = (threadIdx.x >> 3) & (kDeltaRowsPerWarp - 1);
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -72,79 +75,79 @@ k_delta_heads(DeltaArgs a) {
         float* srow = a.state + static_cast<int64_t>(valid ? row : 0) * dk;
         const float* kh = a.k + static_cast<int64_t>(h) * dk;
         const float* qh = a.q + static_cast<int64_t>(h) * dk;
+
+        float x[NC];
+        float kr[kRegKQ ? NC : 1];
+        float qr[kRegKQ ? NC : 1];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            x[c] = 0.0f;
+            if (c < nc && valid) x[c] = __ldcs(srow + 8 * c + lane);
+        }
+        if constexpr (kRegKQ) {
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                kr[c] = 0.0f;
+                qr[c] = 0.0f;
+                if (c < nc && valid) {
+                    kr[c] = __ldg(kh + 8 * c + lane);
+                    qr[c] = __ldg(qh + 8 * c + lane);
+                }
+            }
+        }
+        float xt[7], kt[7], qt[7];
+#pragma unroll
+        for (int t = 0; t < 7; ++t) {
+            xt[t] = kt[t] = qt[t] = 0.0f;
+            if (t < tail && valid) {
+                xt[t] = srow[whole + t];
+                kt[t] = __ldg(kh + whole + t);
+                qt[t] = __ldg(qh + whole + t);
+            }
+        }
+        const float vr = valid ? __ldg(a.v + row) : 0.0f;
+        const float br = valid ? __ldg(a.beta + h) : 0.0f;
         const double decay = a.decay ? a.decay[h] : exp(static_cast<double>(__ldg(a.gate + h)));
 
         // pass 1: decay, kv lane sum
         float acc = 0.0f;
-        float x[NC > 0 ? NC : 1];
-        float kr[NC > 0 ? NC : 1];
-        if constexpr (NC > 0) {
 #pragma unroll
-            for (int c = 0; c < NC; ++c) {
-                x[c] = 0.0f;
-                kr[c] = 0.0f;
-                if (c < nc && valid) {
-                    x[c] = srow[8 * c + lane];
-                    kr[c] = __ldg(kh + 8 * c + lane);
-                }
-            }
-#pragma unroll
-            for (int c = 0; c < NC; ++c) {
-                if (c < nc) {
-                    x[c] = decay_value(x[c], decay);
-                    acc = __fadd_rn(acc, __fmul_rn(x[c], kr[c]));
-                }
-            }
-        } else {
-            if (valid) {
-                for (int c = 0; c < nc; ++c) {
-                    const float d = decay_value(srow[8 * c + lane], decay);
-                    acc = __fadd_rn(acc, __fmul_rn(d, __ldg(kh + 8 * c + lane)));
-                }
+        for (int c = 0; c < NC; ++c) {
+            if (c < nc) {
+                const float kc = kRegKQ ? kr[c] : (valid ? __ldg(kh + 8 * c + lane) : 0.0f);
+                x[c] = decay_value(x[c], decay);
+                acc = __fadd_rn(acc, __fmul_rn(x[c], kc));
             }
         }
         float kv = lane_sum8(acc);
-        float xt[7];
 #pragma unroll
         for (int t = 0; t < 7; ++t) {
-            xt[t] = 0.0f;
-            if (t < tail && valid) {
-                xt[t] = decay_value(srow[whole + t], decay);
-                kv = __fadd_rn(kv, __fmul_rn(xt[t], __ldg(kh + whole + t)));
+            if (t < tail) {
+                xt[t] = decay_value(xt[t], decay);
+                kv = __fadd_rn(kv, __fmul_rn(xt[t], kt[t]));
             }
         }
-        const float vr = valid ? __ldg(a.v + row) : 0.0f;
-        const float delta = __fmul_rn(valid ? __ldg(a.beta + h) : 0.0f, __fsub_rn(vr, kv));
+        const float delta = __fmul_rn(br, __fsub_rn(vr, kv));
 
         // pass 2: update, store, output lane sum
         float acc2 = 0.0f;
-        if constexpr (NC > 0) {
 #pragma unroll
-            for (int c = 0; c < NC; ++c) {
-                if (c < nc && valid) {
-                    const float u = __fadd_rn(x[c], __fmul_rn(delta, kr[c]));
-                    srow[8 * c + lane] = u;
-                    acc2 = __fadd_rn(acc2, __fmul_rn(u, __ldg(qh + 8 * c + lane)));
-                }
-            }
-        } else {
-            if (valid) {
-                for (int c = 0; c < nc; ++c) {
-                    const int j = 8 * c + lane;
-                    const float kj = __ldg(kh + j);
-                    const float u = __fadd_rn(decay_value(srow[j], decay), __fmul_rn(delta, kj));
-                    srow[j] = u;
-                    acc2 = __fadd_rn(acc2, __fmul_rn(u, __ldg(qh + j)));
-                }
+        for (int c = 0; c < NC; ++c) {
+            if (c < nc && valid) {
+                const float kc = kRegKQ ? kr[c] : __ldg(kh + 8 * c + lane);
+                const float qc = kRegKQ ? qr[c] : __ldg(qh + 8 * c + lane);
+                const float u = __fadd_rn(x[c], __fmul_rn(delta, kc));
+                __stcs(srow + 8 * c + lane, u);
+                acc2 = __fadd_rn(acc2, __fmul_rn(u, qc));
             }
         }
         float result = lane_sum8(acc2);
 #pragma unroll
         for (int t = 0; t < 7; ++t) {
             if (t < tail && valid) {
-                const float u = __fadd_rn(xt[t], __fmul_rn(delta, __ldg(kh + whole + t)));
+                const float u = __fadd_rn(xt[t], __fmul_rn(delta, kt[t]));
                 if (lane == t) srow[whole + t] = u;
-                result = __fadd_rn(result, __fmul_rn(u, __ldg(qh + whole + t)));
+                result = __fadd_rn(result, __fmul_rn(u, qt[t]));
             }
         }
         if (valid && lane == 0) {
@@ -156,10 +159,21 @@ k_delta_heads(DeltaArgs a) {
 
 template <int NC>
 cudaError_t launch_nc(const DeltaArgs& a, cudaStream_t s) {
+    static int per_sm[64] = {0};   // resident CTAs per SM, per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!per_sm[dev]) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_delta_heads<NC>, kDeltaThreads, 0) !=
+                cudaSuccess || n < 1)
+            n = 1;
+        per_sm[dev] = n;
+    }
     const int rows = a.heads * a.dv;
     const int rows_per_cta = kDeltaThreads / 8;
     int grid = (rows + rows_per_cta - 1) / rows_per_cta;
-    const int cap = sm_count() * 16;   // 16 CTAs of 4 warps fill an SM's 64 warp slots
+    const int cap = sm_count() * per_sm[dev];   // one wave; the loop strides over the rest
     if (grid > cap) grid = cap;
     k_delta_heads<NC><<<grid, kDeltaThreads, 0, s>>>(a);
     return cudaGetLastError();
@@ -175,7 +189,8 @@ cudaError_t launch_delta_heads(const DeltaArgs& a, cudaStream_t s) {
     if (nc <= 8) return launch_nc<8>(a, s);
     if (nc <= 16) return launch_nc<16>(a, s);
     if (nc <= 32) return launch_nc<32>(a, s);
-    return launch_nc<0>(a, s);
+    if (nc <= 64) return launch_nc<64>(a, s);
+    return launch_nc<128>(a, s);
 }
 
 }  // namespace moeb200

@@ -48,6 +48,16 @@ struct DeltaArgs {
     int heads, dk, dv;
 };
 cudaError_t launch_delta_heads(const DeltaArgs& a, cudaStream_t stream);
+// moe_delta_heads with every array in (pageable) host memory: pinned staging
+// and a chunked copy/compute pipeline (delta_host.cu).  Returns 0, -2 (the
+// reference's early stop) or ST_INTERNAL with *ce set.
+int delta_heads_host(float* state, const float* q, const float* k, const float* v,
+                     const float* beta, const float* gate, float* output, int heads, int dk,
+                     int dv, cudaError_t* ce);
+
+// memcpy split over a few persistent host threads (hostcopy.cu); small copies
+// run on the calling thread.
+void host_parallel_copy(void* dst, const void* src, size_t bytes);
 
 // Routing of T tokens: fp32 scores [T x E] (+ bias), top-K ids/weights, and
 // the shared-expert gate sigmoid(x . gate_inp) per token.

@@ -107,7 +107,7 @@ def oracle_layer(lib, lw, xs, fp16_graph: int = 0, selections=None):
 # "model" is the reference model's linear-attention shape (32 value heads of
 # 128 x 128); the others cover the lane tail (key_dim % 8, up to 7), key_dim
 # < 8, each register-blocking width of the GPU kernel (key_dim / 8 up to 1,
-# 2, 4, 8, 16, 32 and above), the size limits of each argument, and a
+# 2, 4, 8, 16, 32, 64, 128), the size limits of each argument, and a
 # poisoned value that stops the step.
 DELTA_SPECS = {
     "model": (31, 32, 128, 128, 3),
@@ -116,6 +116,7 @@ DELTA_SPECS = {
     "one": (34, 1, 1, 1, 2),
     "wide": (35, 1, 1024, 64, 1),
     "dk64": (39, 4, 64, 48, 2),
+    "dk512": (41, 2, 512, 24, 2),
     "dk263": (40, 2, 263, 40, 2),
     "tall": (36, 2, 16, 1024, 1),
     "many_heads": (37, 256, 8, 8, 2),
