@@ -95,7 +95,8 @@ MOE_B200_API int moe_quant_expert(int gate_type, const uint8_t* gate, int64_t ga
  * the reference, rows up to and including the first non-finite one hold
  * their new state and outputs are written only for the rows before it; a
  * state in host memory keeps its later rows unchanged, a state in device
- * memory has every row updated.  Any pointer may be host or device memory.
+ * memory has every row updated.  -9 when a bounded device-side wait gave up.
+ * Any pointer may be host or device memory.
  * Replaces moe_delta_heads (cpp/moe_delta.cpp:18-69); bound by ctypes in
  * src/flash_moe/native_expert.py:76-98 (NativeDelta) and called from
  * src/flash_moe/gated_deltanet.py:386. */
@@ -372,14 +373,16 @@ MOE_B200_API int moe_b200_expert_noalloc(int gate_type, const uint8_t* gate, int
  * synchronisation, capturable in a CUDA graph).  decay = exp(double(gate))
  * is computed on the device (CUDA's double exp: the decayed state can differ
  * from the host entry point's in the last bit of a float, rarely).  Every
- * row is updated and every output written.  bad_row (device int32, may be
- * NULL) receives -1, or the smallest flat row index h * value_dim + r whose
- * output is not finite.  Returns 0, -1 (arguments, as above), -7 for a
- * pointer that is not 4-byte aligned, -6 on a CUDA launch failure. */
+ * row is updated and every output written.  status (device int32[2], may be
+ * NULL) receives in [0] -1, or the smallest flat row index h * value_dim + r
+ * whose output is not finite, and in [1] 0, or nonzero when a bounded
+ * device-side wait gave up (the state is then partly updated).  Returns 0,
+ * -1 (arguments, as above), -7 for a pointer that is not 4-byte aligned, -6
+ * on a CUDA launch failure. */
 MOE_B200_API int moe_b200_delta_heads(float* state, const float* q, const float* k,
                                       const float* v, const float* beta, const float* gate,
                                       float* output, int heads, int key_dim, int value_dim,
-                                      int32_t* bad_row, void* stream);
+                                      int32_t* status, void* stream);
 
 /* Device-pointer dequantisation on a stream: out_dtype 0 = fp32,
  * 1 = binary16 (round to nearest even).  Same values as dequant_k. */

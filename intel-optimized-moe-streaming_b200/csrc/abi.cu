@@ -358,7 +358,7 @@ int moe_delta_heads(float* state, const float* q, const float* k, const float* v
         }
         const size_t o_decay = st.take((size_t)heads * 8);
         const size_t o_out = st.take(rows * 4);
-        const size_t o_bad = st.take(4);
+        const size_t o_bad = st.take(8);   // first non-finite row, timeout word
         cudaError_t e = sc->ensure(st.used);
         if (e != cudaSuccess) return fail(e, ST_INTERNAL);
         char* base = static_cast<char*>(sc->buf);
@@ -383,6 +383,7 @@ int moe_delta_heads(float* state, const float* q, const float* k, const float* v
         e = cudaMemcpyAsync(base + o_decay, decay.data(), (size_t)heads * 8,
                             cudaMemcpyHostToDevice, sc->stream);
         if (e == cudaSuccess) e = cudaMemsetAsync(base + o_bad, 0xFF, 4, sc->stream);
+        if (e == cudaSuccess) e = cudaMemsetAsync(base + o_bad + 4, 0, 4, sc->stream);
         if (e != cudaSuccess) return fail(e, ST_INTERNAL);
         DeltaArgs a{};
         a.state = static_cast<float*>(dptr[0]);
@@ -394,15 +395,18 @@ int moe_delta_heads(float* state, const float* q, const float* k, const float* v
         a.decay = reinterpret_cast<const double*>(base + o_decay);
         a.out = reinterpret_cast<float*>(base + o_out);
         a.bad = reinterpret_cast<unsigned*>(base + o_bad);
+        a.err = a.bad + 1;
         a.heads = heads;
         a.dk = key_dim;
         a.dv = value_dim;
         e = launch_delta_heads(a, sc->stream);
         if (e != cudaSuccess) return fail(e, ST_INTERNAL);
-        unsigned bad = 0;
-        e = cudaMemcpyAsync(&bad, a.bad, 4, cudaMemcpyDeviceToHost, sc->stream);
+        unsigned words[2] = {0, 0};
+        e = cudaMemcpyAsync(words, a.bad, 8, cudaMemcpyDeviceToHost, sc->stream);
         if (e == cudaSuccess) e = cudaStreamSynchronize(sc->stream);
         if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+        if (words[1]) return ST_TIMEOUT;
+        const unsigned bad = words[0];
         // the reference stops at the first non-finite output: rows up to and
         // including it hold their new state, later rows keep the old one, and
         // outputs are written for the rows before it (cpp/moe_delta.cpp:64-67)
@@ -427,15 +431,16 @@ int moe_delta_heads(float* state, const float* q, const float* k, const float* v
 
 int moe_b200_delta_heads(float* state, const float* q, const float* k, const float* v,
                          const float* beta, const float* gate, float* output, int heads,
-                         int key_dim, int value_dim, int32_t* bad_row, void* stream) {
+                         int key_dim, int value_dim, int32_t* status, void* stream) {
     const void* all[7] = {state, q, k, v, beta, gate, output};
     if (!delta_args_ok(all, heads, key_dim, value_dim)) return ST_ARG;
     for (const void* p : all)
         if ((uintptr_t)p & 3u) return ST_ALIGN;
-    if ((uintptr_t)bad_row & 3u) return ST_ALIGN;
+    if ((uintptr_t)status & 3u) return ST_ALIGN;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (bad_row) {
-        cudaError_t e = cudaMemsetAsync(bad_row, 0xFF, 4, s);
+    if (status) {
+        cudaError_t e = cudaMemsetAsync(status, 0xFF, 4, s);
+        if (e == cudaSuccess) e = cudaMemsetAsync(status + 1, 0, 4, s);
         if (e != cudaSuccess) return fail(e, ST_CUDA);
     }
     DeltaArgs a{};
@@ -447,7 +452,8 @@ int moe_b200_delta_heads(float* state, const float* q, const float* k, const flo
     a.gate = gate;
     a.decay = nullptr;
     a.out = output;
-    a.bad = reinterpret_cast<unsigned*>(bad_row);
+    a.bad = reinterpret_cast<unsigned*>(status);
+    a.err = status ? reinterpret_cast<unsigned*>(status + 1) : nullptr;
     a.heads = heads;
     a.dk = key_dim;
     a.dv = value_dim;

@@ -27,6 +27,7 @@
 // the reference's early stop exactly.
 #include "common.cuh"
 #include "launch.h"
+#include "sm100.cuh"
 
 namespace moeb200 {
 
@@ -179,9 +180,209 @@ cudaError_t launch_nc(const DeltaArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Streaming variant for states larger than the GPU can hold in flight in
+// registers: one persistent CTA per SM walks tiles of 16 consecutive rows.
+// A tile's rows, and the k and q rows of the heads it touches, arrive in a
+// shared-memory stage by TMA bulk copies (one per row, completion counted on
+// the stage's mbarrier); the four warps compute from shared memory (row
+// stride P = key_dim padded to 8 mod 32 floats, so the four rows a warp
+// reads fall in distinct banks), write the updated rows back in place, and
+// one thread bulk-stores them to HBM.  S stages keep S - 1 tiles of loads in
+// flight behind the tile being computed; a stage is refilled once the bulk
+// store of its previous tile has finished reading it.  Needs key_dim % 4 == 0
+// and 16-byte aligned state, k and q (TMA bulk copy alignment).
+
+constexpr int kStreamRows = 16;
+constexpr int kStreamThreads = 128;
+constexpr uint32_t kDeltaWaitPolls = 1u << 21;
+constexpr int kStreamSmemHead = 256;        // mbarriers and the abort flag
+constexpr size_t kStreamSmemMax = 232448;   // 227 KiB dynamic shared memory
+
+struct StreamShape {
+    int P = 0, NH = 0, S = 0;
+    size_t stage_floats = 0, smem = 0;
+};
+
+StreamShape stream_shape(int dk, int dv) {
+    StreamShape sh;
+    sh.P = dk + ((8 - dk % 32) + 32) % 32;
+    const int nh = 15 / dv + 2;   // heads 16 consecutive rows can touch
+    sh.NH = nh < kStreamRows ? nh : kStreamRows;
+    sh.stage_floats = (size_t)(kStreamRows + 2 * sh.NH) * sh.P;
+    const size_t stage_bytes = sh.stage_floats * 4;
+    size_t S = (kStreamSmemMax - kStreamSmemHead) / stage_bytes;
+    if (S > 8) S = 8;
+    sh.S = (int)S;
+    sh.smem = kStreamSmemHead + S * stage_bytes;
+    return sh;
+}
+
+__global__ void __launch_bounds__(kStreamThreads, 1)
+k_delta_stream(DeltaArgs a, int P, int NH, int S, int tiles) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);   // S <= 8 barriers
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_raw + 128);
+    float* stages = reinterpret_cast<float*>(smem_raw + kStreamSmemHead);
+    const size_t stage_floats = (size_t)(kStreamRows + 2 * NH) * P;
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 7;
+    const int rsub = tid >> 3;   // row of the tile, 0..15; a warp holds rows 4w..4w+3
+    const int rows = a.heads * a.dv;
+    const int dk = a.dk, dv = a.dv;
+    const int whole = dk & ~7;
+    const int nc = whole >> 3;
+    const int tail = dk - whole;
+    const uint32_t rb = (uint32_t)dk * 4u;
+
+    if (tid == 0) {
+        for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
+        mbar_fence_init();
+        *abort_flag = 0;
+    }
+    __syncthreads();
+
+    // tile of this CTA's i-th iteration; issued by thread 0 only
+    auto issue = [&](int i) {
+        const int t = blockIdx.x + i * gridDim.x;
+        if (t >= tiles) return false;
+        float* st = stages + (size_t)(i % S) * stage_floats;
+        const int r0 = t * kStreamRows;
+        const int n = rows - r0 < kStreamRows ? rows - r0 : kStreamRows;
+        const int h0 = r0 / dv;
+        const int nh = (r0 + n - 1) / dv - h0 + 1;
+        uint64_t* bar = &full[i % S];
+        mbar_arrive_expect_tx(bar, (uint32_t)(n + 2 * nh) * rb);
+        for (int rr = 0; rr < n; ++rr)
+            bulk_g2s(st + (size_t)rr * P, a.state + (size_t)(r0 + rr) * dk, rb, bar);
+        for (int hh = 0; hh < nh; ++hh) {
+            bulk_g2s(st + (size_t)(kStreamRows + 2 * hh) * P, a.k + (size_t)(h0 + hh) * dk, rb, bar);
+            bulk_g2s(st + (size_t)(kStreamRows + 2 * hh + 1) * P, a.q + (size_t)(h0 + hh) * dk, rb,
+                     bar);
+        }
+        return true;
+    };
+
+    int issued = 0;   // thread 0: iterations whose loads are in flight or consumed
+    if (tid == 0)
+        while (issued < S && issue(issued)) ++issued;
+
+    int i = 0;
+    for (;; ++i) {
+        const int t = blockIdx.x + i * gridDim.x;
+        if (t >= tiles) break;
+        const int s = i % S;
+        if (tid == 0 && !mbar_wait(&full[s], (uint32_t)(i / S) & 1u, kDeltaWaitPolls)) *abort_flag = 1;
+        __syncthreads();
+        if (*abort_flag) break;
+
+        float* st = stages + (size_t)s * stage_floats;
+        const int r0 = t * kStreamRows;
+        const int n = rows - r0 < kStreamRows ? rows - r0 : kStreamRows;
+        const bool valid = rsub < n;
+        const int row = r0 + (valid ? rsub : 0);
+        const int h = row / dv;
+        float* xs = st + (size_t)rsub * P;
+        const float* ks = st + (size_t)(kStreamRows + 2 * (h - r0 / dv)) * P;
+        const float* qs = ks + P;
+        const double decay = a.decay ? a.decay[h] : exp(static_cast<double>(__ldg(a.gate + h)));
+        const float vr = __ldg(a.v + row);
+        const float br = __ldg(a.beta + h);
+
+        // pass 1 (rows past the tile's end compute on stale shared memory and
+        // store nothing; they keep the warp's shuffles complete)
+        float acc = 0.0f;
+        for (int c = 0; c < nc; ++c) {
+            const int j = 8 * c + lane;
+            acc = __fadd_rn(acc, __fmul_rn(decay_value(xs[j], decay), ks[j]));
+        }
+        float kv = lane_sum8(acc);
+        float xt[7];
+#pragma unroll
+        for (int u = 0; u < 7; ++u) {
+            xt[u] = 0.0f;
+            if (u < tail) {
+                xt[u] = decay_value(xs[whole + u], decay);
+                kv = __fadd_rn(kv, __fmul_rn(xt[u], ks[whole + u]));
+            }
+        }
+        const float delta = __fmul_rn(br, __fsub_rn(vr, kv));
+
+        // pass 2: the decayed value is recomputed from the unchanged input
+        float acc2 = 0.0f;
+        for (int c = 0; c < nc; ++c) {
+            const int j = 8 * c + lane;
+            const float u = __fadd_rn(decay_value(xs[j], decay), __fmul_rn(delta, ks[j]));
+            xs[j] = u;
+            acc2 = __fadd_rn(acc2, __fmul_rn(u, qs[j]));
+        }
+        float result = lane_sum8(acc2);
+#pragma unroll
+        for (int u = 0; u < 7; ++u) {
+            if (u < tail) {
+                const float nu = __fadd_rn(xt[u], __fmul_rn(delta, ks[whole + u]));
+                if (lane == u) xs[whole + u] = nu;
+                result = __fadd_rn(result, __fmul_rn(nu, qs[whole + u]));
+            }
+        }
+        if (valid && lane == 0) {
+            a.out[row] = result;
+            if (!isfinite(result) && a.bad) atomicMin(a.bad, static_cast<unsigned>(row));
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            for (int rr = 0; rr < n; ++rr)
+                bulk_s2g(a.state + (size_t)(r0 + rr) * dk, st + (size_t)rr * P, rb);
+            bulk_commit();
+            if (i >= 1 && issued == i - 1 + S) {
+                bulk_wait_read<1>();   // the previous tile's stores have read their stage
+                if (issue(issued)) ++issued;
+            }
+        }
+    }
+    if (tid == 0) {
+        if (*abort_flag) {
+            if (a.err) atomicOr(a.err, 1u);
+            // loads still in flight land before the CTA's shared memory goes
+            for (int j = i; j < issued; ++j) mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u, kDeltaWaitPolls);
+        }
+        bulk_wait_all();
+    }
+}
+
+cudaError_t launch_stream(const DeltaArgs& a, const StreamShape& sh, cudaStream_t s) {
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!attr[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(k_delta_stream, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kStreamSmemMax);
+        if (e != cudaSuccess) return e;
+        attr[dev] = true;
+    }
+    const int rows = a.heads * a.dv;
+    const int tiles = (rows + kStreamRows - 1) / kStreamRows;
+    int grid = sm_count();
+    if (grid > tiles) grid = tiles;
+    k_delta_stream<<<grid, kStreamThreads, sh.smem, s>>>(a, sh.P, sh.NH, sh.S, tiles);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
+// Rows from which the streaming variant is used: four tiles per SM.
+constexpr int kStreamMinRowsPerSm = 4 * kStreamRows;
+
 cudaError_t launch_delta_heads(const DeltaArgs& a, cudaStream_t s) {
+    const int rows = a.heads * a.dv;
+    const bool aligned = ((uintptr_t)a.state | (uintptr_t)a.k | (uintptr_t)a.q) % 16 == 0;
+    if (a.dk % 4 == 0 && aligned && rows >= kStreamMinRowsPerSm * sm_count()) {
+        const StreamShape sh = stream_shape(a.dk, a.dv);
+        if (sh.S >= 2) return launch_stream(a, sh, s);
+    }
     const int nc = a.dk >> 3;
     if (nc <= 1) return launch_nc<1>(a, s);
     if (nc <= 2) return launch_nc<2>(a, s);

@@ -75,7 +75,8 @@ int delta_heads_host(float* state, const float* q, const float* k, const float* 
     const size_t row_bytes = (size_t)dk * 4;
     // pinned and device buffers share one layout
     Stager st;
-    const size_t o_bad = st.take(kMaxChunks * 4);
+    const size_t o_bad = st.take(kMaxChunks * 4);   // per chunk: first non-finite row
+    const size_t o_err = st.take(4);                 // a bounded device wait gave up
     const size_t o_out = st.take(rows * 4);
     const size_t o_decay = st.take((size_t)heads * 8);   // start of the inputs region
     const size_t o_beta = st.take((size_t)heads * 4);
@@ -100,6 +101,7 @@ int delta_heads_host(float* state, const float* q, const float* k, const float* 
     host_parallel_copy(P + o_k, k, (size_t)heads * row_bytes);
     e = cudaMemcpyAsync(D + o_decay, P + o_decay, o_state - o_decay, cudaMemcpyHostToDevice, sg->s0);
     if (e == cudaSuccess) e = cudaMemsetAsync(D + o_bad, 0xFF, kMaxChunks * 4, sg->s0);
+    if (e == cudaSuccess) e = cudaMemsetAsync(D + o_err, 0, 4, sg->s0);
 
     const int chunks = heads < kMaxChunks ? heads : kMaxChunks;
     const int per = (heads + chunks - 1) / chunks;
@@ -123,6 +125,7 @@ int delta_heads_host(float* state, const float* q, const float* k, const float* 
         a.decay = reinterpret_cast<const double*>(D + o_decay) + h0;
         a.out = reinterpret_cast<float*>(D + o_out) + r0;
         a.bad = reinterpret_cast<unsigned*>(D + o_bad) + c;
+        a.err = reinterpret_cast<unsigned*>(D + o_err);
         a.heads = hc;
         a.dk = dk;
         a.dv = dv;
@@ -138,6 +141,8 @@ int delta_heads_host(float* state, const float* q, const float* k, const float* 
         if (e == cudaSuccess)
             e = cudaMemcpyAsync(P + o_bad + c * 4, D + o_bad + c * 4, 4, cudaMemcpyDeviceToHost,
                                 sg->s1);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(P + o_err, D + o_err, 4, cudaMemcpyDeviceToHost, sg->s1);
         if (e == cudaSuccess) e = cudaEventRecord(sg->back[c], sg->s1);
         if (e == cudaSuccess) ++launched;
     }
@@ -147,6 +152,10 @@ int delta_heads_host(float* state, const float* q, const float* k, const float* 
         if (e != cudaSuccess) break;
         const size_t r0 = (size_t)c * per * dv;
         const size_t rc = (size_t)((c + 1) * per <= heads ? per : heads - c * per) * dv;
+        if (*reinterpret_cast<const unsigned*>(P + o_err)) {
+            status = ST_TIMEOUT;
+            break;
+        }
         const unsigned bad = reinterpret_cast<const unsigned*>(P + o_bad)[c];
         size_t n_state = rc, n_out = rc;
         if (bad != 0xFFFFFFFFu) {

@@ -45,6 +45,7 @@ struct DeltaArgs {
     const double* decay;   // [heads] or null
     float* out;            // [heads][dv]
     unsigned* bad;
+    unsigned* err;         // null, or a word set to 1 when a bounded wait gave up
     int heads, dk, dv;
 };
 cudaError_t launch_delta_heads(const DeltaArgs& a, cudaStream_t stream);

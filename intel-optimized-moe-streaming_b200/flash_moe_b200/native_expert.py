@@ -86,11 +86,12 @@ class NativeDelta:
             raise RuntimeError(f"native DeltaNet failed with status {code}")
         return out
 
-    def forward_device(self, state, q, k, v, beta, gate, out=None, bad_row=None, stream=None):
+    def forward_device(self, state, q, k, v, beta, gate, out=None, status=None, stream=None):
         """CUDA tensors, asynchronous on ``stream`` (default: torch's current
         stream) through ``moe_b200_delta_heads``: no host synchronisation.
-        ``bad_row`` (int32 CUDA tensor of one element, optional) receives -1
-        or the first flat row whose output is not finite."""
+        ``status`` (int32 CUDA tensor of two elements, optional) receives in
+        [0] -1 or the first flat row whose output is not finite, in [1] 0 or
+        nonzero when a bounded device-side wait gave up."""
         import torch
         if state.dtype != torch.float32 or not state.is_contiguous() or not state.is_cuda:
             raise ValueError("DeltaNet state must be a contiguous FP32 CUDA tensor")
@@ -100,12 +101,15 @@ class NativeDelta:
         for t, shape in zip(ins, shapes):
             if tuple(t.shape) != shape or t.dtype != torch.float32 or t.device != state.device:
                 raise ValueError("DeltaNet device input shape, dtype or device mismatch")
+        if status is not None and (status.dtype != torch.int32 or status.numel() < 2
+                                   or not status.is_cuda):
+            raise ValueError("DeltaNet status must be an int32 CUDA tensor of two elements")
         if out is None:
             out = torch.empty((nv, dv), dtype=torch.float32, device=state.device)
         handle = (stream if stream is not None else torch.cuda.current_stream(state.device)).cuda_stream
         code = self.library.moe_b200_delta_heads(
             state.data_ptr(), *(t.data_ptr() for t in ins), out.data_ptr(), nv, dk, dv,
-            bad_row.data_ptr() if bad_row is not None else None, handle)
+            status.data_ptr() if status is not None else None, handle)
         if code:
             raise RuntimeError(f"native DeltaNet failed with status {code}")
         return out

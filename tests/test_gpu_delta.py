@@ -92,12 +92,12 @@ def test_device_entry_matches_oracle(oracle, name):
     state, steps = delta_case(name)
     dstate = torch.from_numpy(state.copy()).cuda()
     nd = NativeDelta()
-    bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
     got, want = [], []
     for st in steps:
         dins = [torch.from_numpy(a).cuda() for a in st]
-        got.append(nd.forward_device(dstate, *dins, bad_row=bad).cpu().numpy())
-        assert int(bad.item()) == -1
+        got.append(nd.forward_device(dstate, *dins, status=status).cpu().numpy())
+        assert status.tolist() == [-1, 0]
         rc, y = oracle.delta_heads(state, *st)
         assert rc == 0
         want.append(y)
@@ -115,11 +115,11 @@ def test_device_entry_reports_first_bad_row():
     state, steps = delta_case("poison")
     heads, dv, dk = state.shape
     dstate = torch.from_numpy(state).cuda()
-    bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
     out = NativeDelta().forward_device(dstate, *[torch.from_numpy(a).cuda() for a in steps[0]],
-                                       bad_row=bad)
+                                       status=status)
     h, r = DELTA_POISON
-    assert int(bad.item()) == h * dv + r
+    assert status.tolist() == [h * dv + r, 0]
     assert not np.isfinite(out.cpu().numpy()[h, r])
 
 
@@ -174,3 +174,53 @@ def test_device_entry_large_state_properties():
     decay = torch.tensor(-0.5, dtype=torch.float64, device="cuda").exp()
     want = (before.double() * decay).float()
     assert torch.equal(state, want)
+
+
+# Shapes with enough rows (>= 64 per SM) for the TMA-staged streaming kernel:
+# key_dim with and without a tail of four, value_dim that puts one and two
+# heads in a 16-row tile.
+STREAM_SHAPES = [(80, 100, 128), (160, 64, 64), (256, 132, 40)]
+
+
+@pytest.mark.parametrize("heads,dk,dv", STREAM_SHAPES)
+def test_streaming_kernel_bits_match_oracle(oracle, lib, heads, dk, dv):
+    """Device-resident state through the host entry point (host decay):
+    bit-exact against the oracle on two steps, and the non-finite early stop
+    reported at the right row."""
+    state = synth.make_delta_state(50 + heads, heads, dk, dv)
+    dstate = torch.from_numpy(state.copy()).cuda()
+    for step in range(2):
+        ins = synth.make_delta_step(50 + heads, step, heads, dk, dv)
+        out = np.empty((heads, dv), np.float32)
+        rc = lib.moe_delta_heads(dstate.data_ptr(), *(a.ctypes.data for a in ins),
+                                 out.ctypes.data, heads, dk, dv)
+        rc_o, want = oracle.delta_heads(state, *ins)
+        assert rc == rc_o == 0
+        np.testing.assert_array_equal(out.view(np.uint32), want.view(np.uint32))
+    np.testing.assert_array_equal(dstate.cpu().numpy().view(np.uint32), state.view(np.uint32))
+    ins = list(synth.make_delta_step(50 + heads, 9, heads, dk, dv))
+    ins[2][heads // 2, dv - 1] = np.nan
+    out = np.full((heads, dv), np.nan, np.float32)
+    rc = lib.moe_delta_heads(dstate.data_ptr(), *(a.ctypes.data for a in ins), out.ctypes.data,
+                             heads, dk, dv)
+    assert rc == -2
+    stop = (heads // 2) * dv + dv - 1
+    assert np.isfinite(out.reshape(-1)[:stop]).all() and np.isnan(out.reshape(-1)[stop:]).all()
+
+
+@pytest.mark.parametrize("heads,dk,dv", STREAM_SHAPES[:1])
+def test_streaming_kernel_device_entry(oracle, heads, dk, dv):
+    state = synth.make_delta_state(60, heads, dk, dv)
+    ins = synth.make_delta_step(60, 0, heads, dk, dv)
+    dstate = torch.from_numpy(state.copy()).cuda()
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    got = NativeDelta().forward_device(dstate, *[torch.from_numpy(a).cuda() for a in ins],
+                                       status=status).cpu().numpy()
+    assert status.tolist() == [-1, 0]
+    rc, want = oracle.delta_heads(state, *ins)
+    assert rc == 0
+    if _device_decay_agrees([ins]):
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+        np.testing.assert_array_equal(dstate.cpu().numpy().view(np.uint32), state.view(np.uint32))
+    else:
+        assert O.max_relative_error(got, want) <= 1e-6
