@@ -4,6 +4,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace moeb200 {
 
@@ -47,13 +48,6 @@ __device__ __forceinline__ float block_sum(float v, float* part) {
     float t = 0.f;
     for (int i = 0; i < kFusedThreads / 32; ++i) t += part[i];
     return t;
-}
-
-// Orders this thread's earlier generic-proxy accesses of shared memory
-// before its later async-proxy (TMA) accesses: issued before a bulk copy
-// into shared memory that other threads have read since the last barrier.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 }  // namespace moeb200

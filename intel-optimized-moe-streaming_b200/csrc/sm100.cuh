@@ -81,8 +81,10 @@ __device__ __forceinline__ void bulk_wait_all() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
-// Order this thread's generic-proxy shared-memory writes before later
-// async-proxy (TMA) reads of them.
+// Orders this thread's earlier generic-proxy accesses of shared memory
+// before later async-proxy (TMA) accesses: before a bulk copy out of shared
+// memory this thread wrote, or (after a barrier) into shared memory that
+// other threads have read.
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
