@@ -182,34 +182,36 @@ cudaError_t launch_nc(const DeltaArgs& a, cudaStream_t s) {
 
 // ---------------------------------------------------------------------------
 // Streaming variant for states larger than the GPU can hold in flight in
-// registers: one persistent CTA per SM walks tiles of 16 consecutive rows.
+// registers: one persistent CTA per SM walks tiles of ROWS (32, or 16 when
+// a wide row leaves room for fewer than three 32-row stages) consecutive
+// rows, eight threads per row.
 // A tile's rows, and the k and q rows of the heads it touches, arrive in a
 // shared-memory stage by TMA bulk copies (one per row, completion counted on
-// the stage's mbarrier); the four warps compute from shared memory (row
-// stride P = key_dim padded to 8 mod 32 floats, so the four rows a warp
-// reads fall in distinct banks), write the updated rows back in place, and
-// one thread bulk-stores them to HBM.  S stages keep S - 1 tiles of loads in
+// the stage's mbarrier); the warps compute from shared memory (row stride
+// P = key_dim padded to 8 mod 32 floats, so the four rows a warp reads fall
+// in distinct banks), keep the decayed row there between the two passes
+// (one double multiply per value), write the updated rows back in place,
+// and one thread bulk-stores them to HBM.  S stages keep S - 1 tiles of loads in
 // flight behind the tile being computed; a stage is refilled once the bulk
 // store of its previous tile has finished reading it.  Needs key_dim % 4 == 0
 // and 16-byte aligned state, k and q (TMA bulk copy alignment).
 
-constexpr int kStreamRows = 16;
-constexpr int kStreamThreads = 128;
 constexpr uint32_t kDeltaWaitPolls = 1u << 21;
 constexpr int kStreamSmemHead = 256;        // mbarriers and the abort flag
 constexpr size_t kStreamSmemMax = 232448;   // 227 KiB dynamic shared memory
 
 struct StreamShape {
-    int P = 0, NH = 0, S = 0;
+    int rows = 0, P = 0, NH = 0, S = 0;
     size_t stage_floats = 0, smem = 0;
 };
 
-StreamShape stream_shape(int dk, int dv) {
+StreamShape stream_shape(int dk, int dv, int tile_rows) {
     StreamShape sh;
+    sh.rows = tile_rows;
     sh.P = dk + ((8 - dk % 32) + 32) % 32;
-    const int nh = 15 / dv + 2;   // heads 16 consecutive rows can touch
-    sh.NH = nh < kStreamRows ? nh : kStreamRows;
-    sh.stage_floats = (size_t)(kStreamRows + 2 * sh.NH) * sh.P;
+    const int nh = (tile_rows - 1) / dv + 2;   // heads tile_rows consecutive rows can touch
+    sh.NH = nh < tile_rows ? nh : tile_rows;
+    sh.stage_floats = (size_t)(tile_rows + 2 * sh.NH) * sh.P;
     const size_t stage_bytes = sh.stage_floats * 4;
     size_t S = (kStreamSmemMax - kStreamSmemHead) / stage_bytes;
     if (S > 8) S = 8;
@@ -218,17 +220,18 @@ StreamShape stream_shape(int dk, int dv) {
     return sh;
 }
 
-__global__ void __launch_bounds__(kStreamThreads, 1)
+template <int ROWS>
+__global__ void __launch_bounds__(ROWS * 8, 1)
 k_delta_stream(DeltaArgs a, int P, int NH, int S, int tiles) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);   // S <= 8 barriers
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_raw + 128);
     float* stages = reinterpret_cast<float*>(smem_raw + kStreamSmemHead);
-    const size_t stage_floats = (size_t)(kStreamRows + 2 * NH) * P;
+    const size_t stage_floats = (size_t)(ROWS + 2 * NH) * P;
 
     const int tid = threadIdx.x;
     const int lane = tid & 7;
-    const int rsub = tid >> 3;   // row of the tile, 0..15; a warp holds rows 4w..4w+3
+    const int rsub = tid >> 3;   // row of the tile; warp w holds rows 4w..4w+3
     const int rows = a.heads * a.dv;
     const int dk = a.dk, dv = a.dv;
     const int whole = dk & ~7;
@@ -248,8 +251,8 @@ k_delta_stream(DeltaArgs a, int P, int NH, int S, int tiles) {
         const int t = blockIdx.x + i * gridDim.x;
         if (t >= tiles) return false;
         float* st = stages + (size_t)(i % S) * stage_floats;
-        const int r0 = t * kStreamRows;
-        const int n = rows - r0 < kStreamRows ? rows - r0 : kStreamRows;
+        const int r0 = t * ROWS;
+        const int n = rows - r0 < ROWS ? rows - r0 : ROWS;
         const int h0 = r0 / dv;
         const int nh = (r0 + n - 1) / dv - h0 + 1;
         uint64_t* bar = &full[i % S];
@@ -257,8 +260,8 @@ k_delta_stream(DeltaArgs a, int P, int NH, int S, int tiles) {
         for (int rr = 0; rr < n; ++rr)
             bulk_g2s(st + (size_t)rr * P, a.state + (size_t)(r0 + rr) * dk, rb, bar);
         for (int hh = 0; hh < nh; ++hh) {
-            bulk_g2s(st + (size_t)(kStreamRows + 2 * hh) * P, a.k + (size_t)(h0 + hh) * dk, rb, bar);
-            bulk_g2s(st + (size_t)(kStreamRows + 2 * hh + 1) * P, a.q + (size_t)(h0 + hh) * dk, rb,
+            bulk_g2s(st + (size_t)(ROWS + 2 * hh) * P, a.k + (size_t)(h0 + hh) * dk, rb, bar);
+            bulk_g2s(st + (size_t)(ROWS + 2 * hh + 1) * P, a.q + (size_t)(h0 + hh) * dk, rb,
                      bar);
         }
         return true;
@@ -278,13 +281,13 @@ k_delta_stream(DeltaArgs a, int P, int NH, int S, int tiles) {
         if (*abort_flag) break;
 
         float* st = stages + (size_t)s * stage_floats;
-        const int r0 = t * kStreamRows;
-        const int n = rows - r0 < kStreamRows ? rows - r0 : kStreamRows;
+        const int r0 = t * ROWS;
+        const int n = rows - r0 < ROWS ? rows - r0 : ROWS;
         const bool valid = rsub < n;
         const int row = r0 + (valid ? rsub : 0);
         const int h = row / dv;
         float* xs = st + (size_t)rsub * P;
-        const float* ks = st + (size_t)(kStreamRows + 2 * (h - r0 / dv)) * P;
+        const float* ks = st + (size_t)(ROWS + 2 * (h - r0 / dv)) * P;
         const float* qs = ks + P;
         const double decay = a.decay ? a.decay[h] : exp(static_cast<double>(__ldg(a.gate + h)));
         const float vr = __ldg(a.v + row);
@@ -295,7 +298,9 @@ k_delta_stream(DeltaArgs a, int P, int NH, int S, int tiles) {
         float acc = 0.0f;
         for (int c = 0; c < nc; ++c) {
             const int j = 8 * c + lane;
-            acc = __fadd_rn(acc, __fmul_rn(decay_value(xs[j], decay), ks[j]));
+            const float d = decay_value(xs[j], decay);
+            xs[j] = d;   // this thread's own value: no other thread reads it
+            acc = __fadd_rn(acc, __fmul_rn(d, ks[j]));
         }
         float kv = lane_sum8(acc);
         float xt[7];
@@ -309,11 +314,12 @@ k_delta_stream(DeltaArgs a, int P, int NH, int S, int tiles) {
         }
         const float delta = __fmul_rn(br, __fsub_rn(vr, kv));
 
-        // pass 2: the decayed value is recomputed from the unchanged input
+        // pass 2 (the tail's decayed values stay in registers: every lane of
+        // the row reads the tail, so it is not overwritten before the shuffles)
         float acc2 = 0.0f;
         for (int c = 0; c < nc; ++c) {
             const int j = 8 * c + lane;
-            const float u = __fadd_rn(decay_value(xs[j], decay), __fmul_rn(delta, ks[j]));
+            const float u = __fadd_rn(xs[j], __fmul_rn(delta, ks[j]));
             xs[j] = u;
             acc2 = __fadd_rn(acc2, __fmul_rn(u, qs[j]));
         }
@@ -352,36 +358,40 @@ k_delta_stream(DeltaArgs a, int P, int NH, int S, int tiles) {
     }
 }
 
+template <int ROWS>
 cudaError_t launch_stream(const DeltaArgs& a, const StreamShape& sh, cudaStream_t s) {
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     if (!attr[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(k_delta_stream, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(k_delta_stream<ROWS>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kStreamSmemMax);
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
     const int rows = a.heads * a.dv;
-    const int tiles = (rows + kStreamRows - 1) / kStreamRows;
+    const int tiles = (rows + ROWS - 1) / ROWS;
     int grid = sm_count();
     if (grid > tiles) grid = tiles;
-    k_delta_stream<<<grid, kStreamThreads, sh.smem, s>>>(a, sh.P, sh.NH, sh.S, tiles);
+    k_delta_stream<ROWS><<<grid, ROWS * 8, sh.smem, s>>>(a, sh.P, sh.NH, sh.S, tiles);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 // Rows from which the streaming variant is used: four tiles per SM.
-constexpr int kStreamMinRowsPerSm = 4 * kStreamRows;
+constexpr int kStreamMinRowsPerSm = 64;
 
 cudaError_t launch_delta_heads(const DeltaArgs& a, cudaStream_t s) {
     const int rows = a.heads * a.dv;
     const bool aligned = ((uintptr_t)a.state | (uintptr_t)a.k | (uintptr_t)a.q) % 16 == 0;
     if (a.dk % 4 == 0 && aligned && rows >= kStreamMinRowsPerSm * sm_count()) {
-        const StreamShape sh = stream_shape(a.dk, a.dv);
-        if (sh.S >= 2) return launch_stream(a, sh, s);
+        const StreamShape wide = stream_shape(a.dk, a.dv, 32);
+        if (wide.S >= 3) return launch_stream<32>(a, wide, s);
+        const StreamShape sh = stream_shape(a.dk, a.dv, 16);
+        if (sh.S >= 2) return launch_stream<16>(a, sh, s);
     }
     const int nc = a.dk >> 3;
     if (nc <= 1) return launch_nc<1>(a, s);

@@ -178,8 +178,8 @@ def test_device_entry_large_state_properties():
 
 # Shapes with enough rows (>= 64 per SM) for the TMA-staged streaming kernel:
 # key_dim with and without a tail of four, value_dim that puts one and two
-# heads in a 16-row tile.
-STREAM_SHAPES = [(80, 100, 128), (160, 64, 64), (256, 132, 40)]
+# heads in a tile, and a 1024-wide row (16-row tiles; the others use 32).
+STREAM_SHAPES = [(80, 100, 128), (160, 64, 64), (256, 132, 40), (148, 1024, 64)]
 
 
 @pytest.mark.parametrize("heads,dk,dv", STREAM_SHAPES)
