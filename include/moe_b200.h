@@ -191,9 +191,12 @@ MOE_B200_API int moe_b200_decode_host(const moe_b200_layer* layer, const float* 
                          float* y, int32_t* topk_ids, float* topk_weights,
                          void* workspace, size_t workspace_bytes, void* stream);
 
-/* Zero the workspace's control words (its first 256 bytes) on `stream`.
- * Call once after allocating a decode workspace; the decode kernels leave
- * them zero again when they finish. */
+/* Zero the whole workspace (`workspace_bytes`) on `stream`.  Call once
+ * after allocating a decode workspace, before its first use.  The decode
+ * kernels leave the counters zero again when they finish; the fused
+ * single-token kernel also keeps a step sequence number there that tags the
+ * values its CTAs exchange, so zeroing only part of a workspace that has
+ * been used could let a stale value pass as a current one. */
 MOE_B200_API int moe_b200_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
 
 /* Synchronously read (and clear) the device-side error word of a

@@ -166,7 +166,7 @@ int moe_b200_version(void) { return 100; }
 
 int moe_b200_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
     if (!workspace || workspace_bytes < 256) return ST_ARG;
-    cudaError_t e = cudaMemsetAsync(workspace, 0, 256, static_cast<cudaStream_t>(stream));
+    cudaError_t e = cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? ST_OK : fail(e, ST_CUDA);
 }
 

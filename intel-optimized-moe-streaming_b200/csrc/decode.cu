@@ -23,7 +23,14 @@
 //
 // The routing is recomputed identically by every CTA from the E scores, so
 // no CTA waits for another to publish it.  Exchanges through global memory:
-// E scores, the A*I + Is fp32 activations, the shared gate value.
+// E scores, the A*I + Is fp32 activations, the shared gate value, each as a
+// 64-bit word of the fp32 value and the step's tag written with one store.
+// A CTA polls exactly the words it needs until they carry the current tag:
+// no release fence, no counter, no separate data read.  This orders the
+// phases on its own when every CTA owns a router row (E >= G): a CTA cannot
+// reach step s+2, which reuses step s's buffers, before every CTA has
+// written its step s+1 scores, i.e. finished step s.  With E < G the
+// counters C_ROUTER / C_GATEUP also separate the phases.
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -52,10 +59,10 @@ struct FusedParams {
     int n_steps;
     float eps;               // RMSNorm epsilon of MOE_B200_STEP_BLOCK steps
     uint32_t* ctr;           // counters, error word at ctr[C_ERROR]
-    float* scores;           // [2][E]       (buffer = step parity)
-    float* act_r;            // [2][K x I]
-    float* act_s;            // [2][Imax]
-    float* sg;               // [2]
+    uint64_t* scores;        // [2][E]       exchange words (buffer = step parity)
+    uint64_t* act_r;         // [2][K x I]
+    uint64_t* act_s;         // [2][Imax]
+    uint64_t* sg;            // [2]
     uint64_t* trace;         // [G x 32] phase timestamps of step n_steps / 2 (ns), or null
     int* err_out;            // null, or a host-visible word that receives (and clears) the
                              // error word at exit
@@ -87,6 +94,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     const int64_t rb_su = Is ? row_bytes(L0.shared_up_type, H) : 0;
     const int64_t rb_sd = Is ? row_bytes(L0.shared_down_type, Is) : 0;
     const int Imax = max(I, Is);
+    const bool tagged = E >= G;
+    const uint32_t seq0 = ld_acquire(p.ctr + C_SEQ);
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + p.o_misc);       // [kXBar + 1]
     int* s_ids = reinterpret_cast<int*>(sm + p.o_misc + 128);          // [16]
@@ -160,6 +169,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         TRACE(0);
         const moe_b200_layer* Ls = step_layer(s);
         const uint32_t gen = (uint32_t)G * (uint32_t)(s + 1);  // counter value once step s is done
+        const uint32_t tag = seq0 + (uint32_t)s + 1u;             // exchange-word tag of step s
         int sflags = 0;
         const float* xin = p.x;
         float* yout = p.y;
@@ -174,10 +184,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             w_out = st.topk_weights;
         }
         const int buf = s & 1;
-        float* scores = p.scores + (size_t)buf * E;
-        float* act_r = p.act_r + (size_t)buf * K * I;
-        float* act_s = p.act_s + (size_t)buf * Imax;
-        float* sgp = p.sg + buf;
+        uint64_t* scores = p.scores + (size_t)buf * E;
+        uint64_t* act_r = p.act_r + (size_t)buf * K * I;
+        uint64_t* act_s = p.act_s + (size_t)buf * Imax;
+        uint64_t* sgp = p.sg + buf;
         const bool chain = (sflags & MOE_B200_STEP_CHAIN) && s > 0;
         const bool block = (sflags & MOE_B200_STEP_BLOCK) != 0;
 
@@ -240,20 +250,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                     float acc = 0.f;
                     for (int q = 0; q < spr; ++q) acc += s_part[tid * spr + q];
                     if (bias) acc = __fadd_rn(acc, bias[r0 + tid]);
-                    scores[r0 + tid] = acc;
+                    st_word_gpu(scores + r0 + tid, acc, tag);
                 }
             } else {
                 for (int rr = warp; rr < R; rr += nw) {
                     float acc = dot_f32_warp(router_s + (size_t)rr * H, x32, H, lane);
                     if (lane == 0) {
                         if (bias) acc = __fadd_rn(acc, bias[r0 + rr]);
-                        scores[r0 + rr] = acc;
+                        st_word_gpu(scores + r0 + rr, acc, tag);
                     }
                 }
             }
         }
         __syncthreads();
-        if (tid == 0) red_release_add(p.ctr + C_ROUTER, 1);
+        if (tid == 0 && !tagged) red_release_add(p.ctr + C_ROUTER, 1);
         TRACE(3);
 
         // ---- the token quantised for the integer dot products; shared gate
@@ -263,39 +273,45 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             float acc = 0.f;
             for (int i = lane; i < H; i += 32) acc = fmaf(x32[i], ginp[i], acc);
             acc = warp_sum(acc);
-            if (lane == 0) *sgp = shared_sigmoid(acc);
+            if (lane == 0) st_word_gpu(sgp, shared_sigmoid(acc), tag);
         }
         __syncthreads();
         XLane xl;
         load_xlane(xl, xq, pr_h >> 2, pr_h & 3);
 
-        // ---- routing (every CTA, identically)
-        if (tid == 0 && !wait_flag(p.ctr + C_ROUTER, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
-        __syncthreads();
-        TRACE(5);
-        if (E > 256) {
-            for (int e = tid; e < E; e += kFusedThreads) s_scores[e] = __ldcg(scores + e);
+        // ---- routing (every CTA, identically): the selection first, so the
+        // routed copies start at once; the weights later, off that path
+        if (!tagged) {
+            if (tid == 0 && !wait_flag(p.ctr + C_ROUTER, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
             __syncthreads();
         }
+        TRACE(5);
+        if (E > 256) {
+            bool ok = true;
+            for (int e = tid; e < E; e += kFusedThreads) s_scores[e] = wait_word_gpu(scores + e, tag, kWaitPolls, ok);
+            if (!ok) set_error(p.ctr, ST_TIMEOUT);
+            __syncthreads();
+        }
+        uint32_t sel_k = 0;
+        int sel_id = 0;
         if (warp == 0) {
-            if (E <= 256)
-                topk_softmax_warp_fast(scores, E, K, s_ids, s_w, trace);
-            else
+            if (E <= 256) {
+                uint32_t kk[8];
+                int kid[8];
+                if (!load_score_words(scores, E, tag, kWaitPolls, kk, kid) && lane == 0)
+                    set_error(p.ctr, ST_TIMEOUT);
+                topk_select_warp(kk, kid, K, sel_k, sel_id, trace);
+                if (lane < K) s_ids[lane] = sel_id;
+            } else {
                 topk_softmax_warp(s_scores, s_taken, E, K, s_ids, s_w);
-            if (lane == 0) {
-                int na = 0;
-                for (int k = 0; k < K; ++k) {
-                    const int e = s_ids[k];
-                    if (e >= ebeg && e < ebeg + ecnt) s_act[na++] = k;
-                }
-                *s_nact = na;
-                if (c == 0) {
-                    for (int k = 0; k < K; ++k) {
-                        if (ids_out) ids_out[k] = s_ids[k];
-                        if (w_out) w_out[k] = s_w[k];
-                    }
-                }
             }
+            __syncwarp();
+            // the selections this GPU holds, in top-k order
+            const int e = lane < K ? s_ids[lane] : -1;
+            const bool held = lane < K && e >= ebeg && e < ebeg + ecnt;
+            const uint32_t hb = __ballot_sync(0xffffffffu, held);
+            if (held) s_act[__popc(hb & ((1u << lane) - 1u))] = lane;
+            if (lane == 0) *s_nact = __popc(hb);
         }
         __syncthreads();
         TRACE(6);
@@ -335,6 +351,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                 bulk_g2s(sm + p.o_rdown + (int64_t)a * p.max_out_rows * rb_down,
                          down + e * st_down + h0 * rb_down, (uint32_t)(nh * rb_down), &bars[2]);
             }
+            // routing weights (float64 softmax over the selections), needed
+            // only by the combine
+            if (E <= 256) topk_weights_warp(sel_k, sel_id, K, s_ids, s_w);
+            if (c == 0 && lane < K) {
+                if (ids_out) ids_out[lane] = s_ids[lane];
+                if (w_out) w_out[lane] = s_w[lane];
+            }
+            TRACE(15);
         }
 
         // ---- shared expert gate/up (x is the token), while the routed rows
@@ -352,7 +376,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                 float u = qdot_t<SGU>(L0.shared_up_type, sm + p.o_sup + rs * rb_su, pr_h >> 2, pr_h & 3, xl);
                 g = group_sum(g, lpr_h);
                 u = group_sum(u, lpr_h);
-                if (ok && pr_h == 0) act_s[s0 + rr] = (g * shared_sigmoid(g)) * u;
+                if (ok && pr_h == 0) st_word_gpu(act_s + s0 + rr, (g * shared_sigmoid(g)) * u, tag);
             }
         }
         TRACE(4);
@@ -378,7 +402,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                 u = group_sum(u, lpr_h);
                 if (ok && pr_h == 0) {
                     const float sgm = 1.0f / (1.0f + expf(-g));
-                    act_r[f0 + rr] = (g * sgm) * u;
+                    st_word_gpu(act_r + f0 + rr, (g * sgm) * u, tag);
                 }
                 if (rb == 0) TRACE(18);
             }
@@ -392,7 +416,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         TRACE(7);
         __syncthreads();
         TRACE(8);
-        if (tid == 0) {
+        if (tid == 0 && !tagged) {
             if (Is) red_release_add(p.ctr + C_SHARED, 1);
             red_release_add(p.ctr + C_GATEUP, 1);
             if (Is && !wait_flag(p.ctr + C_SHARED, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
@@ -401,18 +425,49 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         __syncthreads();
         TRACE(9);
 
-        // ---- activations of the A routed experts (+ shared), quantised
+        // ---- activations of the A routed experts (+ shared), quantised.
+        // Word j < A*I is routed (slot j / I, row j % I), then the Is shared
+        // ones, then the shared gate; a thread polls its words kActBatch at a
+        // time, every load of a round in flight together.
         float* act32 = reinterpret_cast<float*>(sm + p.o_act);
-        for (int i = tid; i < (A * I) / 4; i += kFusedThreads) {
-            const int e = 4 * i;
-            *reinterpret_cast<float4*>(act32 + (e / I) * Imax + (e % I)) =
-                __ldcg(reinterpret_cast<const float4*>(act_r) + i);
-        }
-        if (Is) {
-            for (int i = tid; i < Is / 4; i += kFusedThreads)
-                *reinterpret_cast<float4*>(act32 + A * Imax + 4 * i) =
-                    __ldcg(reinterpret_cast<const float4*>(act_s) + i);
-            if (tid == 0) *s_sg = __ldcg(sgp);
+        {
+            constexpr int kActBatch = 10;
+            const int nr = A * I, nt = nr + (Is ? Is + 1 : 0);
+            bool ok = true;
+            for (int jb = tid; jb < nt && ok; jb += kActBatch * kFusedThreads) {
+                uint32_t pend = 0;
+#pragma unroll
+                for (int q = 0; q < kActBatch; ++q)
+                    if (jb + q * kFusedThreads < nt) pend |= 1u << q;
+                for (uint32_t round = 0; pend != 0u; ++round) {
+                    if (round == kWaitPolls) {
+                        ok = false;
+                        break;
+                    }
+                    uint64_t wv[kActBatch];
+#pragma unroll
+                    for (int q = 0; q < kActBatch; ++q) {
+                        const int j = jb + q * kFusedThreads;
+                        const uint64_t* src = j < nr ? act_r + j : (j < nr + Is ? act_s + (j - nr) : sgp);
+                        wv[q] = ((pend >> q) & 1u) ? ld_word_gpu(src) : 0ull;
+                    }
+#pragma unroll
+                    for (int q = 0; q < kActBatch; ++q) {
+                        if (((pend >> q) & 1u) && (uint32_t)(wv[q] >> 32) == tag) {
+                            pend &= ~(1u << q);
+                            const int j = jb + q * kFusedThreads;
+                            const float v = __uint_as_float((uint32_t)wv[q]);
+                            if (j < nr)
+                                act32[(j / I) * Imax + j % I] = v;
+                            else if (j < nr + Is)
+                                act32[A * Imax + (j - nr)] = v;
+                            else
+                                *s_sg = v;
+                        }
+                    }
+                }
+            }
+            if (!ok) set_error(p.ctr, ST_TIMEOUT);
         }
         __syncthreads();
         TRACE(19);
@@ -512,6 +567,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             p.ctr[C_GATEUP] = 0;
             p.ctr[C_DONE] = 0;
             p.ctr[C_EXIT] = 0;
+            p.ctr[C_SEQ] = seq0 + (uint32_t)p.n_steps;
             if (p.err_out) {
                 *p.err_out = atomicExch(reinterpret_cast<int*>(p.ctr + C_ERROR), 0);
                 __threadfence_system();
@@ -555,8 +611,8 @@ size_t fused_workspace_bytes(const moe_b200_layer* L) {
     const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate : L->intermediate;
     // counters, then two buffers (step parity) of scores, routed and shared
     // activations and the shared gate
-    return 256 + align_up((size_t)2 * L->n_experts * 4) +
-           align_up((size_t)2 * L->top_k * L->intermediate * 4) + align_up((size_t)2 * Imax * 4) + 256;
+    return 256 + align_up((size_t)2 * L->n_experts * 8) +
+           align_up((size_t)2 * L->top_k * L->intermediate * 8) + align_up((size_t)2 * Imax * 8) + 256;
 }
 
 static bool fused_plan(const moe_b200_layer* L, bool shared, int G, FusedParams& p) {
@@ -671,13 +727,13 @@ static cudaError_t fused_prepare(const moe_b200_layer* L, int flags, const float
     p.ctr = reinterpret_cast<uint32_t*>(base);
     const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate : L->intermediate;
     size_t off = 256;
-    p.scores = reinterpret_cast<float*>(base + off);
-    off += align_up((size_t)2 * L->n_experts * 4);
-    p.act_r = reinterpret_cast<float*>(base + off);
-    off += align_up((size_t)2 * L->top_k * L->intermediate * 4);
-    p.act_s = reinterpret_cast<float*>(base + off);
-    off += align_up((size_t)2 * Imax * 4);
-    p.sg = reinterpret_cast<float*>(base + off);
+    p.scores = reinterpret_cast<uint64_t*>(base + off);
+    off += align_up((size_t)2 * L->n_experts * 8);
+    p.act_r = reinterpret_cast<uint64_t*>(base + off);
+    off += align_up((size_t)2 * L->top_k * L->intermediate * 8);
+    p.act_s = reinterpret_cast<uint64_t*>(base + off);
+    off += align_up((size_t)2 * Imax * 8);
+    p.sg = reinterpret_cast<uint64_t*>(base + off);
     p.trace = (tl_trace && tl_trace_cap >= G) ? tl_trace : nullptr;
     *ok = true;
     return cudaSuccess;

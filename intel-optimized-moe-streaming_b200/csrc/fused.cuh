@@ -13,8 +13,11 @@ constexpr uint32_t kWaitPolls = 1u << 21;
 constexpr int kTraceSlots = 32;
 
 // Counters in the first 256 bytes of the workspace (uint32 words); the error
-// word sits at byte 32, where moe_b200_workspace_error reads it.
-enum { C_ROUTER = 0, C_SHARED = 1, C_GATEUP = 2, C_EXIT = 3, C_DONE = 4, C_ERROR = 8 };
+// word sits at byte 32, where moe_b200_workspace_error reads it.  C_SEQ is
+// the fused single-token kernel's step sequence number: it only grows (each
+// launch adds its step count), so the tag seq + s + 1 of step s never
+// repeats on a workspace and a stale exchange word never matches.
+enum { C_ROUTER = 0, C_SHARED = 1, C_GATEUP = 2, C_EXIT = 3, C_DONE = 4, C_SEQ = 5, C_ERROR = 8 };
 
 __device__ __forceinline__ int part(int n, int c, int G) { return (int)(((int64_t)n * c) / G); }
 

@@ -160,6 +160,37 @@ __device__ __forceinline__ float wait_word_sys(const uint64_t* p, uint32_t seq, 
     return __uint_as_float((uint32_t)w);
 }
 
+// The same exchange word between the CTAs of one GPU (gpu scope): the
+// payload and the step tag arrive together, so a CTA that polls the words it
+// needs waits for exactly those values, with no release fence on the writer
+// side and no counter round trip before the data read.
+__device__ __forceinline__ void st_word_gpu(uint64_t* p, float v, uint32_t tag) {
+    const uint64_t w = ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_word_gpu(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+// Payload of the gpu-scope exchange word at p once it carries `tag` (at most
+// `limit` polls while ok; ok is cleared when the limit is hit).
+__device__ __forceinline__ float wait_word_gpu(const uint64_t* p, uint32_t tag, uint32_t limit,
+                                               bool& ok) {
+    uint64_t w = ld_word_gpu(p);
+    if (ok && (uint32_t)(w >> 32) != tag) {
+        uint32_t i = 0;
+        for (; i < limit; ++i) {
+            w = ld_word_gpu(p);
+            if ((uint32_t)(w >> 32) == tag) break;
+        }
+        if (i == limit) ok = false;
+    }
+    return __uint_as_float((uint32_t)w);
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -11,6 +11,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace moeb200 {
 
@@ -107,24 +108,15 @@ __device__ __forceinline__ bool kbefore(uint32_t ka, int ia, uint32_t kb, int ib
         }                                                                \
     } while (0)
 
-// Fast form of topk_softmax_warp for E <= 256 with the scores in global
-// memory written by other CTAs (read through L2).  Each lane sorts its (up
-// to) 8 scores in registers; each of the K rounds takes the warp maximum of
-// the lane heads with one redux.sync, and the winning lane pops its head.
-// Lane k (k < K) ends with selection k; the float64 softmax then runs across
-// lanes.  Identical results to topk_softmax_warp.
-__device__ __forceinline__ void topk_softmax_warp_fast(const float* gscores, int E, int K,
-                                                       int* ids, float* w,
-                                                       uint64_t* trace = nullptr) {
+// Top-k of E <= 256 keys held 8 per lane (lane l: experts 8l..8l+7, absent
+// ones key 0 / id 0x7fffffff).  Each lane sorts its keys in registers; each
+// of the K rounds takes the warp maximum of the lane heads with one
+// redux.sync, and the winning lane pops its head.  Lane r (r < K) ends with
+// selection r: its key in my_k, its expert in my_id.
+__device__ __forceinline__ void topk_select_warp(uint32_t (&k)[8], int (&id)[8], int K,
+                                                 uint32_t& my_k, int& my_id,
+                                                 uint64_t* trace = nullptr) {
     const int lane = threadIdx.x & 31;
-    uint32_t k[8];
-    int id[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int e = 8 * lane + i;
-        k[i] = e < E ? fkey(__ldcg(gscores + e)) : 0u;
-        id[i] = e < E ? e : 0x7fffffff;
-    }
     // Batcher odd-even merge sort of 8, descending (19 compare-exchanges)
     MOE_CSWAP(0, 1); MOE_CSWAP(2, 3); MOE_CSWAP(4, 5); MOE_CSWAP(6, 7);
     MOE_CSWAP(0, 2); MOE_CSWAP(1, 3); MOE_CSWAP(4, 6); MOE_CSWAP(5, 7);
@@ -137,8 +129,8 @@ __device__ __forceinline__ void topk_softmax_warp_fast(const float* gscores, int
         asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
         trace[13] = t;
     }
-    uint32_t my_k = 0;
-    int my_id = 0;
+    my_k = 0;
+    my_id = 0;
     for (int r = 0; r < K; ++r) {
         const uint32_t m = __reduce_max_sync(0xffffffffu, k[0]);
         // equal keys: lower lane holds lower ids; within a lane the sort
@@ -165,7 +157,14 @@ __device__ __forceinline__ void topk_softmax_warp_fast(const float* gscores, int
         asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
         trace[14] = t;
     }
-    // softmax over the K selected scores in float64 (router.py:258-269)
+}
+
+// Routing weights of the K selections lanes 0..K-1 hold (topk_select_warp):
+// the float64 softmax over those k only (router.py:258-269), written to
+// ids[lane] / w[lane].  All 32 lanes must call.
+__device__ __forceinline__ void topk_weights_warp(uint32_t my_k, int my_id, int K, int* ids,
+                                                  float* w) {
+    const int lane = threadIdx.x & 31;
     const double v = (lane < K) ? (double)fkey_inv(my_k) : 0.0;
     const double mx = __shfl_sync(0xffffffffu, v, 0);  // selection 0 is the maximum
     const double ex = (lane < K) ? exp(v - mx) : 0.0;
@@ -187,11 +186,64 @@ __device__ __forceinline__ void topk_softmax_warp_fast(const float* gscores, int
         w[lane] = uniform ? (float)(1.0 / K) : (float)(ex / tot);
     }
     __syncwarp();
+}
+
+// Fast form of topk_softmax_warp for E <= 256 with the scores in global
+// memory written by other CTAs (read through L2).  Identical results to
+// topk_softmax_warp.
+__device__ __forceinline__ void topk_softmax_warp_fast(const float* gscores, int E, int K,
+                                                       int* ids, float* w,
+                                                       uint64_t* trace = nullptr) {
+    const int lane = threadIdx.x & 31;
+    uint32_t k[8];
+    int id[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = 8 * lane + i;
+        k[i] = e < E ? fkey(__ldcg(gscores + e)) : 0u;
+        id[i] = e < E ? e : 0x7fffffff;
+    }
+    uint32_t my_k;
+    int my_id;
+    topk_select_warp(k, id, K, my_k, my_id, trace);
+    topk_weights_warp(my_k, my_id, K, ids, w);
     if (trace && lane == 0) {
         uint64_t t;
         asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
         trace[15] = t;
     }
+}
+
+// Lane l's keys for topk_select_warp (experts 8l..8l+7 of E <= 256) from
+// exchange words (st_word_gpu: the fp32 score and the step tag in one 64-bit
+// word), polled until every word carries `tag`: all eight loads of a round
+// are in flight together, and only the words still missing are read again.
+// At most `limit` rounds; false (the same in every lane) when it gave up.
+__device__ __forceinline__ bool load_score_words(const uint64_t* words, int E, uint32_t tag,
+                                                 uint32_t limit, uint32_t (&k)[8], int (&id)[8]) {
+    const int lane = threadIdx.x & 31;
+    uint32_t pend = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = 8 * lane + i;
+        id[i] = e < E ? e : 0x7fffffff;
+        k[i] = 0u;
+        if (e < E) pend |= 1u << i;
+    }
+    for (uint32_t round = 0; __any_sync(0xffffffffu, pend != 0u); ++round) {
+        if (round == limit) return false;
+        uint64_t wv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) wv[i] = (pend >> i) & 1u ? ld_word_gpu(words + 8 * lane + i) : 0ull;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (((pend >> i) & 1u) && (uint32_t)(wv[i] >> 32) == tag) {
+                k[i] = fkey(__uint_as_float((uint32_t)wv[i]));
+                pend &= ~(1u << i);
+            }
+        }
+    }
+    return true;
 }
 #undef MOE_CSWAP
 
