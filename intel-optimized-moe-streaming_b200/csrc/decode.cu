@@ -47,6 +47,7 @@ namespace moeb200 {
 
 constexpr int kMaxChunks = 8;  // routed gate/up copy chunks (mbarriers 3..10)
 constexpr int kXBar = 3 + kMaxChunks;  // mbarrier of the prefetched token
+constexpr int kGatherPairs = 8;  // exchange-word pairs a lane has in flight per poll round
 
 struct FusedParams {
     moe_b200_layer L;        // shapes and block formats of every step's layer
@@ -107,6 +108,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     float* s_scores = reinterpret_cast<float*>(sm + p.o_misc + 512);   // [E]
     unsigned char* s_taken = reinterpret_cast<unsigned char*>(s_scores + E);
     float* s_vout = reinterpret_cast<float*>(sm + p.o_misc + 512 + ((5 * E + 15) & ~15));
+    // per activation vector: the tag of the step whose codes it holds
+    volatile uint32_t* s_ready = reinterpret_cast<volatile uint32_t*>(
+        sm + p.o_misc + 512 + ((5 * E + 15) & ~15) + (K + 1) * p.max_out_rows * 4);
     float* x32 = reinterpret_cast<float*>(sm + p.o_x32);
     float* h32 = reinterpret_cast<float*>(sm + p.o_h32);
 
@@ -156,6 +160,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         for (int i = 0; i <= kXBar; ++i) mbar_init(&bars[i], 1);
         mbar_fence_init();
     }
+    if (tid <= kMaxTopK) s_ready[tid] = 0u;
     __syncthreads();
     if (tid == 0) {
         issue_phase0(step_layer(0));
@@ -298,7 +303,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             if (E <= 256) {
                 uint32_t kk[8];
                 int kid[8];
-                if (!load_score_words(scores, E, tag, kWaitPolls, kk, kid) && lane == 0)
+                if (!load_score_words(scores, E, tag, kWaitPolls,
+                                      reinterpret_cast<uint32_t*>(s_scores), kk, kid) &&
+                    lane == 0)
                     set_error(p.ctr, ST_TIMEOUT);
                 topk_select_warp(kk, kid, K, sel_k, sel_id, trace);
                 if (lane < K) s_ids[lane] = sel_id;
@@ -425,81 +432,73 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         __syncthreads();
         TRACE(9);
 
-        // ---- activations of the A routed experts (+ shared), quantised.
-        // Word j < A*I is routed (slot j / I, row j % I), then the Is shared
-        // ones, then the shared gate; a thread polls its words kActBatch at a
-        // time, every load of a round in flight together.
+        // ---- activations, vector by vector: warp w gathers vector v = w
+        // (+16, ...) -- routed slot v < A (I values) or the shared vector
+        // v == A (Is values and the shared gate) -- from the exchange words,
+        // quantises it and marks it ready (s_ready[v] = tag).  A down item
+        // starts as soon as its vector is ready, so the exchange of the late
+        // vectors overlaps the down rows of the early ones; the shared
+        // vector, whose rows were done first, leads.
         float* act32 = reinterpret_cast<float*>(sm + p.o_act);
-        {
-            constexpr int kActBatch = 10;
-            const int nr = A * I, nt = nr + (Is ? Is + 1 : 0);
+        const uint32_t qb = qvec_bytes(Imax);
+        const int nvec = A + (Is ? 1 : 0);
+        for (int v = warp; v < nvec; v += nw) {
+            const int n = v < A ? I : Is;
+            const uint64_t* src = v < A ? act_r + (size_t)v * I : act_s;
+            float* dst = act32 + v * Imax;
             bool ok = true;
-            for (int jb = tid; jb < nt && ok; jb += kActBatch * kFusedThreads) {
+            for (int j0 = 2 * lane; j0 < n; j0 += 2 * 32 * kGatherPairs) {
                 uint32_t pend = 0;
 #pragma unroll
-                for (int q = 0; q < kActBatch; ++q)
-                    if (jb + q * kFusedThreads < nt) pend |= 1u << q;
+                for (int q = 0; q < kGatherPairs; ++q)
+                    if (j0 + 64 * q < n) pend |= 1u << q;
                 for (uint32_t round = 0; pend != 0u; ++round) {
                     if (round == kWaitPolls) {
                         ok = false;
                         break;
                     }
-                    uint64_t wv[kActBatch];
+                    ulonglong2 wv[kGatherPairs];
 #pragma unroll
-                    for (int q = 0; q < kActBatch; ++q) {
-                        const int j = jb + q * kFusedThreads;
-                        const uint64_t* src = j < nr ? act_r + j : (j < nr + Is ? act_s + (j - nr) : sgp);
-                        wv[q] = ((pend >> q) & 1u) ? ld_word_gpu(src) : 0ull;
-                    }
+                    for (int q = 0; q < kGatherPairs; ++q)
+                        wv[q] = ((pend >> q) & 1u) ? ld_word2_gpu(src + j0 + 64 * q) : make_ulonglong2(0ull, 0ull);
 #pragma unroll
-                    for (int q = 0; q < kActBatch; ++q) {
-                        if (((pend >> q) & 1u) && (uint32_t)(wv[q] >> 32) == tag) {
+                    for (int q = 0; q < kGatherPairs; ++q) {
+                        if (((pend >> q) & 1u) && (uint32_t)(wv[q].x >> 32) == tag &&
+                            (uint32_t)(wv[q].y >> 32) == tag) {
                             pend &= ~(1u << q);
-                            const int j = jb + q * kFusedThreads;
-                            const float v = __uint_as_float((uint32_t)wv[q]);
-                            if (j < nr)
-                                act32[(j / I) * Imax + j % I] = v;
-                            else if (j < nr + Is)
-                                act32[A * Imax + (j - nr)] = v;
-                            else
-                                *s_sg = v;
+                            *reinterpret_cast<float2*>(dst + j0 + 64 * q) =
+                                make_float2(__uint_as_float((uint32_t)wv[q].x), __uint_as_float((uint32_t)wv[q].y));
                         }
                     }
                 }
+                if (!ok) break;
             }
-            if (!ok) set_error(p.ctr, ST_TIMEOUT);
+            if (v == A && lane == 0) *s_sg = wait_word_gpu(sgp, tag, kWaitPolls, ok);
+            if (!__all_sync(0xffffffffu, ok) && lane == 0) set_error(p.ctr, ST_TIMEOUT);
+            __syncwarp();
+            if (v == 0) TRACE(19);
+            for (int b = 0; b < n / 256; ++b) quantize_block_warp(dst, qvec_at(sm + p.o_aq + v * qb, n), b);
+            __syncwarp();
+            __threadfence_block();
+            if (lane == 0) s_ready[v] = tag;
+            if (v == 0) TRACE(20);
         }
-        __syncthreads();
-        TRACE(19);
-        const uint32_t qb = qvec_bytes(Imax);
-        {
-            const int bi = I / 256, bs = Is / 256;
-            for (int it = warp; it < A * bi + bs; it += nw) {
-                const int v = it < A * bi ? it / bi : A;
-                const int b = it < A * bi ? it % bi : it - A * bi;
-                const int n = v < A ? I : Is;
-                quantize_block_warp(act32 + v * Imax, qvec_at(sm + p.o_aq + v * qb, n), b);
-            }
-        }
-        __syncthreads();
-        TRACE(20);
-        if (tid == 0 && !mbar_wait(&bars[2], (ph >> 2) & 1u, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+        // the down rows of this CTA (every warp checks the copy)
+        if (!mbar_wait(&bars[2], (ph >> 2) & 1u, kWaitPolls) && lane == 0) set_error(p.ctr, ST_TIMEOUT);
         ph ^= 4u;
-        __syncthreads();
         TRACE(10);
 
         // ---- down rows [h0, h1) of every vector: item = (routed vector, pair
         // of row groups), the activation codes loaded once per item; the
-        // shared vector's row groups are one per item, so that they spread
-        // over the warps of the round after the routed items
+        // shared vector's row groups come first, one per item
         {
             const int rpw_i = 32 / p.lpr_i, rpw_s = 32 / p.lpr_is;
             const int ng_i = (nh + rpw_i - 1) / rpw_i, ng_s = Is ? (nh + rpw_s - 1) / rpw_s : 0;
             const int np_i = (ng_i + 1) / 2, np_s = ng_s;
             for (int it = warp; it < A * np_i + np_s; it += nw) {
-                const bool sh = it >= A * np_i;
-                const int v = sh ? A : it / np_i;
-                const int gp = sh ? it - A * np_i : it % np_i;
+                const bool sh = it < np_s;
+                const int v = sh ? A : (it - np_s) / np_i;
+                const int gp = sh ? it : (it - np_s) % np_i;
                 const int lpr = sh ? p.lpr_is : p.lpr_i;
                 const int ng = sh ? ng_s : ng_i;
                 const int rpw = 32 / lpr, sub = lane / lpr, pr = lane % lpr;
@@ -507,6 +506,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                 const int64_t rb = sh ? rb_sd : rb_down;
                 const uint8_t* rows = sh ? sm + p.o_sdown : sm + p.o_rdown + (int64_t)v * p.max_out_rows * rb_down;
                 const int n = sh ? Is : I;
+                {
+                    uint32_t i = 0;
+                    while (s_ready[v] != tag && ++i < kWaitPolls) {
+                    }
+                    if (i == kWaitPolls && lane == 0) set_error(p.ctr, ST_TIMEOUT);
+                    __syncwarp();
+                    __threadfence_block();
+                }
                 XLane xa;
                 load_xlane(xa, qvec_at(sm + p.o_aq + v * qb, n), pr >> 2, pr & 3);
 #pragma unroll
@@ -648,7 +655,8 @@ static bool fused_plan(const moe_b200_layer* L, bool shared, int G, FusedParams&
     p.o_rdown = take((uint64_t)K * p.max_out_rows * row_bytes(L->down_type, I));
     p.o_act = take((uint64_t)(K + 1) * Imax * 4);
     p.o_aq = take((uint64_t)(K + 1) * qvec_bytes(Imax));
-    p.o_misc = take(512 + ((5 * E + 15) & ~15) + (uint64_t)(K + 1) * p.max_out_rows * 4);
+    p.o_misc = take(512 + ((5 * E + 15) & ~15) + (uint64_t)(K + 1) * p.max_out_rows * 4 +
+                    4 * (kMaxTopK + 1));
     p.total = o;
     return p.total <= 227 * 1024;
 }

@@ -175,6 +175,14 @@ __device__ __forceinline__ uint64_t ld_word_gpu(const uint64_t* p) {
     return w;
 }
 
+// Two consecutive exchange words (p 16-byte aligned) in one load; each
+// 64-bit element is read whole.
+__device__ __forceinline__ ulonglong2 ld_word2_gpu(const uint64_t* p) {
+    ulonglong2 w;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    return w;
+}
+
 // Payload of the gpu-scope exchange word at p once it carries `tag` (at most
 // `limit` polls while ok; ok is cleared when the limit is hit).
 __device__ __forceinline__ float wait_word_gpu(const uint64_t* p, uint32_t tag, uint32_t limit,

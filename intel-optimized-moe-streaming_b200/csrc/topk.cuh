@@ -216,35 +216,50 @@ __device__ __forceinline__ void topk_softmax_warp_fast(const float* gscores, int
 
 // Lane l's keys for topk_select_warp (experts 8l..8l+7 of E <= 256) from
 // exchange words (st_word_gpu: the fp32 score and the step tag in one 64-bit
-// word), polled until every word carries `tag`: all eight loads of a round
-// are in flight together, and only the words still missing are read again.
-// At most `limit` rounds; false (the same in every lane) when it gave up.
+// word), polled until every word carries `tag`.  The polling loads are
+// coalesced: lane l reads words l + 32 i, so a warp's load is 256 contiguous
+// bytes (8 sectors, not 32 at a 64-byte lane stride) -- every CTA of the
+// grid polls the same E words, and the sectors per round are what the L2
+// slices serve.  Only the words still missing are read again.  The keys are
+// staged in shared memory (`stage`, E uint32) and each lane then takes its
+// own experts from there.  At most `limit` rounds; false (the same in every
+// lane) when it gave up.
 __device__ __forceinline__ bool load_score_words(const uint64_t* words, int E, uint32_t tag,
-                                                 uint32_t limit, uint32_t (&k)[8], int (&id)[8]) {
+                                                           uint32_t limit, uint32_t* stage,
+                                                           uint32_t (&k)[8], int (&id)[8]) {
     const int lane = threadIdx.x & 31;
     uint32_t pend = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int e = 8 * lane + i;
-        id[i] = e < E ? e : 0x7fffffff;
-        k[i] = 0u;
-        if (e < E) pend |= 1u << i;
-    }
+    for (int i = 0; i < 8; ++i)
+        if (lane + 32 * i < E) pend |= 1u << i;
+    bool ok = true;
     for (uint32_t round = 0; __any_sync(0xffffffffu, pend != 0u); ++round) {
-        if (round == limit) return false;
+        if (round == limit) {
+            ok = false;
+            break;
+        }
         uint64_t wv[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) wv[i] = (pend >> i) & 1u ? ld_word_gpu(words + 8 * lane + i) : 0ull;
+        for (int i = 0; i < 8; ++i) wv[i] = (pend >> i) & 1u ? ld_word_gpu(words + lane + 32 * i) : 0ull;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if (((pend >> i) & 1u) && (uint32_t)(wv[i] >> 32) == tag) {
-                k[i] = fkey(__uint_as_float((uint32_t)wv[i]));
+                stage[lane + 32 * i] = fkey(__uint_as_float((uint32_t)wv[i]));
                 pend &= ~(1u << i);
             }
         }
     }
-    return true;
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = 8 * lane + i;
+        id[i] = e < E ? e : 0x7fffffff;
+        k[i] = e < E ? stage[e] : 0u;
+    }
+    __syncwarp();
+    return ok;
 }
+
 #undef MOE_CSWAP
 
 // sigmoid of the reference shared-expert gate (shared_expert.py:250-257).
