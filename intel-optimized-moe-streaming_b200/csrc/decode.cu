@@ -331,12 +331,22 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         const int nrows = f1 - f0;
         const int CR = p.chunk_rows;
         const int nchunks = (nrows + CR - 1) / CR;
-        // issued by the lanes of warp 0 in parallel: lane q < nchunks chunk q,
-        // lanes 16.. the down rows of expert 16 - lane
+        // issued by the lanes of warp 0 in parallel: lane q < nchunks chunk q;
+        // the down rows (lane 16 + a: slot a) once the last gate/up chunk has
+        // landed, so they do not compete with the gate/up bytes, which are
+        // needed first
+        auto issue_down = [&]() {
+            if (lane == 16) mbar_arrive_expect_tx(&bars[2], (uint32_t)(A * nh * rb_down));
+            if (lane >= 16 && lane - 16 < A && nh > 0) {
+                const int a = lane - 16;
+                const int64_t e = s_ids[s_act[a]] - ebeg;
+                bulk_g2s(sm + p.o_rdown + (int64_t)a * p.max_out_rows * rb_down,
+                         Ls->down + e * st_down + h0 * rb_down, (uint32_t)(nh * rb_down), &bars[2]);
+            }
+        };
         if (warp == 0) {
             const uint8_t* gate = Ls->gate;
             const uint8_t* up = Ls->up;
-            const uint8_t* down = Ls->down;
             if (lane < nchunks) {
                 const int q = lane, q0 = q * CR, q1 = min(nrows, q0 + CR);
                 mbar_arrive_expect_tx(&bars[3 + q], (uint32_t)((q1 - q0) * (rb_gate + rb_up)));
@@ -350,13 +360,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                              (uint32_t)(n * rb_up), &bars[3 + q]);
                     f += n;
                 }
-            }
-            if (lane == 16) mbar_arrive_expect_tx(&bars[2], (uint32_t)(A * nh * rb_down));
-            if (lane >= 16 && lane - 16 < A && nh > 0) {
-                const int a = lane - 16;
-                const int64_t e = s_ids[s_act[a]] - ebeg;
-                bulk_g2s(sm + p.o_rdown + (int64_t)a * p.max_out_rows * rb_down,
-                         down + e * st_down + h0 * rb_down, (uint32_t)(nh * rb_down), &bars[2]);
             }
             // routing weights (float64 softmax over the selections), needed
             // only by the combine
@@ -399,6 +402,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                     if (!mbar_wait(&bars[3 + waited], (ph >> (3 + waited)) & 1u, kWaitPolls) && lane == 0)
                         set_error(p.ctr, ST_TIMEOUT);
                     if (waited < 2) TRACE(16 + waited);
+                    if (warp == 0 && waited == nchunks - 1) issue_down();
                 }
                 const int rr = rb + sub_h;
                 const bool ok = rr < nrows;
@@ -415,9 +419,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             }
             // every chunk barrier must have completed before the CTA moves on
             // (its copies write shared memory)
-            for (int q = waited + 1; q < nchunks; ++q)
+            for (int q = waited + 1; q < nchunks; ++q) {
                 if (!mbar_wait(&bars[3 + q], (ph >> (3 + q)) & 1u, kWaitPolls) && lane == 0)
                     set_error(p.ctr, ST_TIMEOUT);
+                if (warp == 0 && q == nchunks - 1) issue_down();
+            }
+            if (warp == 0 && nchunks == 0) issue_down();
             ph ^= ((1u << nchunks) - 1u) << 3;
         }
         TRACE(7);
