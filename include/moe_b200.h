@@ -237,8 +237,8 @@ MOE_B200_API int moe_b200_prefill(const moe_b200_layer* layer, const void* x, in
                                   void* stream);
 
 /* Workspace bytes of moe_b200_prefill for up to max_tokens tokens (device
- * memory, 256-byte aligned; its first 256 bytes are the control words
- * that moe_b200_workspace_init clears). */
+ * memory, 256-byte aligned; its first 256 bytes are the control words;
+ * moe_b200_workspace_init zeroes it before first use). */
 MOE_B200_API int moe_b200_prefill_workspace(const moe_b200_layer* layer, int32_t max_tokens,
                                             size_t* bytes);
 
