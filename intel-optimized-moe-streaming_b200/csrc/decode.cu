@@ -273,6 +273,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
 
         // ---- the token quantised for the integer dot products; shared gate
         for (int b = warp; b < H / 256; b += nw) quantize_block_warp(x32, xq, b);
+        TRACE(23);
         if (Is && c == 0 && warp == nw - 1) {
             const float* ginp = Ls->shared_gate_inp;
             float acc = 0.f;
@@ -281,8 +282,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             if (lane == 0) st_word_gpu(sgp, shared_sigmoid(acc), tag);
         }
         __syncthreads();
+        TRACE(24);
         XLane xl;
         load_xlane(xl, xq, pr_h >> 2, pr_h & 3);
+        TRACE(25);
 
         // ---- routing (every CTA, identically): the selection first, so the
         // routed copies start at once; the weights later, off that path

@@ -31,12 +31,21 @@
 
 namespace moeb200 {
 
+// Codes are stored G-major: value 256 b + 32 G + 8 o + j (block b, group
+// G of 32, octet o, byte j) sits at byte G * (n/8) + 8 * (4 b + o) + j of
+// hi / lo, and the octet sums of (b, G, o) at G * (n/64) + 4 b + o.  A
+// reader lane owns (b, o) (lane = 4 b + o within its row group) and loads
+// all eight G, so for each G the lanes of a warp read one contiguous run:
+// no shared-memory bank conflicts (block-major order put the 8 blocks 256
+// bytes apart, 8 lanes on one bank, while every warp of the CTA loads its
+// codes at the same time).
 struct QVec {
     int8_t* hi;
     int8_t* lo;
     float* s;     // [n/256] block scales
     int16_t* oh;  // [n/8] octet sums of hi
     int16_t* ol;  // [n/8] octet sums of lo
+    int n8;       // n / 8: bytes of one G plane of hi / lo
 };
 
 // Bytes of shared memory a QVec of n values uses (16-byte multiple).
@@ -51,6 +60,7 @@ __device__ __forceinline__ QVec qvec_at(uint8_t* base, int n) {
     q.s = reinterpret_cast<float*>(base + 2 * n);
     q.oh = reinterpret_cast<int16_t*>(base + 2 * n + 4 * (n / 256));
     q.ol = q.oh + n / 8;
+    q.n8 = n / 8;
     return q;
 }
 
@@ -84,9 +94,10 @@ __device__ __forceinline__ void quantize_block_vals(const float (&vals)[8], QVec
         ph[e >> 2] |= (uint32_t)(hi & 255) << (8 * (e & 3));
         pl[e >> 2] |= (uint32_t)(lo & 255) << (8 * (e & 3));
     }
-    const int oc = 32 * b + lane;
-    *reinterpret_cast<uint2*>(q.hi + 8 * oc) = make_uint2(ph[0], ph[1]);
-    *reinterpret_cast<uint2*>(q.lo + 8 * oc) = make_uint2(pl[0], pl[1]);
+    const int G = lane >> 2, o = lane & 3;
+    const int off = G * q.n8 + 8 * (4 * b + o), oc = G * (q.n8 >> 3) + 4 * b + o;
+    *reinterpret_cast<uint2*>(q.hi + off) = make_uint2(ph[0], ph[1]);
+    *reinterpret_cast<uint2*>(q.lo + off) = make_uint2(pl[0], pl[1]);
     q.oh[oc] = (int16_t)sh;
     q.ol[oc] = (int16_t)sl;
 }
@@ -126,15 +137,15 @@ struct XLane {
 __device__ __forceinline__ void load_xlane(XLane& x, const QVec& v, int b, int o) {
 #pragma unroll
     for (int G = 0; G < 8; ++G) {
-        const int base = 256 * b + 32 * G + 8 * o;
-        const uint2 hh = *reinterpret_cast<const uint2*>(v.hi + base);
-        const uint2 ll = *reinterpret_cast<const uint2*>(v.lo + base);
+        const int off = G * v.n8 + 8 * (4 * b + o), oc = G * (v.n8 >> 3) + 4 * b + o;
+        const uint2 hh = *reinterpret_cast<const uint2*>(v.hi + off);
+        const uint2 ll = *reinterpret_cast<const uint2*>(v.lo + off);
         x.h[G][0] = hh.x;
         x.h[G][1] = hh.y;
         x.l[G][0] = ll.x;
         x.l[G][1] = ll.y;
-        x.sh8[G] = v.oh[base >> 3];
-        x.sl8[G] = v.ol[base >> 3];
+        x.sh8[G] = v.oh[oc];
+        x.sl8[G] = v.ol[oc];
     }
     x.s = v.s[b];
 }

@@ -32,7 +32,8 @@ from .store import ExpertArena
 DECODE_STAMPS = ["entry", "x_in", "router_rows", "router", "shared_gu", "routing_barrier",
                  "topk", "gu_warps", "gate_up", "gu_barrier", "down_rows", "down", "exit",
                  "tk_sorted", "tk_rounds", "tk_softmax", "chunk0", "chunk1", "row0",
-                 "act_loaded", "act_quantised", "down_item0", "down_item16"]
+                 "act_loaded", "act_quantised", "down_item0", "down_item16",
+                 "x_quantised", "x_synced", "x_codes"]
 EP_STAMPS = ["entry", "x_pushed", "x_in", "router", "routing_barrier", "topk_pairs",
              "shared_gu", "gate_up", "gu_barrier", "act_quantised", "down", "combine_pushed",
              "combine_in", "exit"]
