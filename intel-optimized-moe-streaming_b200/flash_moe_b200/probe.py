@@ -85,6 +85,41 @@ def probe_decode(steps: int = 40, copies: int = 16) -> None:
     print("device error word:", be.device_errors())
 
 
+def probe_multi(copies: int = 16, rounds: int = 4) -> None:
+    """Time per moe_b200_decode call of 1, 2, 4 and 8 tokens on the config-2
+    layer: `copies` resident copies at distinct addresses, a CUDA graph of
+    rounds x copies calls (one launch each), CUDA events around its replay."""
+    dev = torch.device("cuda", 0)
+    lw = synth.make_layer(seed=0)
+    arena = ExpertArena(dev)
+    arena.add_layer(0, lw)
+    for c in range(1, copies):
+        arena.add_device_layer(c, arena.layer(0).clone())
+    be = B200ExpertBackend(arena)
+    toks = torch.from_numpy(synth.make_tokens(3, 64, lw.hidden)).to(dev)
+    for T in (1, 2, 4, 8):
+        xs = [toks[(i * T) % 64:(i * T) % 64 + T].contiguous() for i in range(copies)]
+        ys = [torch.empty_like(x) for x in xs]
+        for i in range(copies):
+            be.forward_layer_device(i, xs[i], ys[i])
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(rounds):
+                for i in range(copies):
+                    be.forward_layer_device(i, xs[i], ys[i])
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        print(f"{T} token(s): {e0.elapsed_time(e1) * 1e3 / (rounds * copies):.1f} us per call")
+        del g
+    print("device error word:", be.device_errors())
+
+
 def probe_prefill(tokens: int = 4096) -> None:
     dev = torch.device("cuda", 0)
     arena = ExpertArena(dev)
@@ -236,12 +271,16 @@ def main() -> None:
     b = sub.add_parser("batched")
     b.add_argument("--tokens", type=int, default=64)
     b.add_argument("--calls", type=int, default=10)
+    m = sub.add_parser("multi")
+    m.add_argument("--copies", type=int, default=16)
     q = sub.add_parser("ep")
     q.add_argument("--steps", type=int, default=64)
     args = ap.parse_args()
     _lib.load()
     if args.what == "decode":
         probe_decode(args.steps, args.copies)
+    elif args.what == "multi":
+        probe_multi(args.copies)
     elif args.what == "ep":
         probe_ep(args.steps)
     elif args.what == "batched":
