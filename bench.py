@@ -439,6 +439,40 @@ def run_prefill_only(args) -> None:
     print(json.dumps({"prefill": bench_prefill(backend, 0, dev, peaks, peak_kind)}), flush=True)
 
 
+def check_last_step(runner, steps: int) -> float:
+    """Max relative error of the last timed step's output (runner.y) against
+    the exact fp32 engine (every weight dequantised bit-exactly, fp32 FMA;
+    pinned to the oracle by the tests) on the same token and layer; under
+    torchrun the exact engine runs expert-parallel with NCCL collectives
+    (all-gather, held experts, reduce-scatter, own shared expert).  Max over
+    ranks."""
+    import torch
+    from flash_moe_b200 import _lib
+    from flash_moe_b200 import ep as EP
+    i = steps - 1
+    layer = runner.layers[i % len(runner.layers)]
+    x = runner.tokens[i % runner.tokens.shape[0]].view(1, -1)
+    got = runner.y.clone()
+    want = torch.empty_like(got)
+    be = runner.be
+    if runner.world == 1:
+        be.forward_layer_device(layer, x, want, flags=_lib.EXACT)
+    else:
+        H = x.shape[1]
+        xa = torch.empty((runner.world, H), dtype=torch.float32, device=x.device)
+        yp, yr, ys = torch.empty_like(xa), torch.empty_like(got), torch.empty_like(got)
+        EP.ep_exchange_step(
+            x, lambda a, p: be.forward_layer_device(layer, a, p, flags=_lib.EXACT | _lib.NO_SHARED),
+            lambda a, p: be.forward_layer_device(layer, a, p, flags=_lib.EXACT | _lib.SHARED_ONLY),
+            xa, yp, yr, ys, want)
+    torch.cuda.synchronize()
+    err = ((got - want).abs().max() / want.abs().max().clamp_min(1e-30)).view(1)
+    if runner.world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    return float(err.item())
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -550,6 +584,8 @@ def run_gpu(args) -> None:
             "kernel": ("k_decode_fused (all steps in one launch)" if launch_mode.startswith("one")
                        else runner.kernel_name)}
 
+    max_err = check_last_step(runner, args.steps)
+
     # end to end through the public API: pinned host token in, host result out
     e2e = runner.e2e(args.steps, args.warmup)
 
@@ -588,6 +624,8 @@ def run_gpu(args) -> None:
             "roofline": roof,
             "e2e": e2e,
             "gpu_launches": launches,
+            "max_rel_err": float(f"{max_err:.3e}"),
+            "max_rel_err_vs": "exact fp32 engine, last timed step (max over ranks)",
             "clocks": clk.summary(),
         }
         if cpu is not None:

@@ -160,8 +160,8 @@ MOE_B200_API int moe_b200_decode_workspace(const moe_b200_layer* layer, int32_t 
  * NULL.  Experts outside [expert_begin, expert_begin + expert_count)
  * contribute zero (expert-parallel partial output).
  * Replaces run_moe_layer (src/flash_moe/moe_layer.py:39-107) with the
- * router of src/flash_moe/router.py:241-271 and the shared expert of
- * src/flash_moe/shared_expert.py:416-446, for each token. */
+ * router of src/flash_moe/router.py:140-170 and the shared expert of
+ * src/flash_moe/shared_expert.py:221-251, for each token. */
 MOE_B200_API int moe_b200_decode(const moe_b200_layer* layer, const float* x, int32_t tokens,
                     float* y, int32_t* topk_ids, float* topk_weights,
                     void* workspace, size_t workspace_bytes, void* stream);
@@ -216,7 +216,7 @@ MOE_B200_API int moe_b200_decode_kernels(const moe_b200_layer* layer, int32_t to
  * run_moe_sequence (reference src/flash_moe/moe_layer.py:110-195, whose
  * per-expert batches go through ExpertBackend.forward_batch,
  * src/flash_moe/backend_ov.py:357-431, and SharedExpert.forward_batch,
- * src/flash_moe/shared_expert.py:395-414).  No single reference function
+ * src/flash_moe/shared_expert.py:200-219).  No single reference function
  * has this signature: it is the device-resident prefill export the B200
  * library adds beside the per-expert ones.
  *

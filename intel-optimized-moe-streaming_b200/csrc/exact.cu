@@ -11,7 +11,7 @@
 //
 //  k_gateup: one CTA per (token, slot, 16-row tile); one warp per row pair
 //            computes g and u, then the SwiGLU activation (reference
-//            moe_quant_dot.cpp:196-206, shared expert shared_expert.py:442-443).
+//            moe_quant_dot.cpp:196-206, shared expert shared_expert.py:247-249).
 //  k_down:   one CTA per (token, 8-row tile); one warp per output row sums
 //            weight_k * down_k(a_k) over the slots in top-k order, then adds
 //            sigmoid-gate * shared_down(a_s) (moe_layer.py:70-105).
@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(256) k_gateup(ExactPlan p) {
         if (lane == 0) {
             float a;
             if (shared) {
-                // _sigmoid of the reference shared expert (shared_expert.py:250-257)
+                // _sigmoid of the reference shared expert (shared_expert.py:55-62)
                 float sgm;
                 if (g >= 0.f) {
                     sgm = 1.0f / (1.0f + expf(-g));

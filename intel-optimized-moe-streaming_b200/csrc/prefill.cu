@@ -5,7 +5,7 @@
 // (token, slot) pairs by expert, run each expert's SwiGLU FFN over its group
 // (the reference batches them through forward_batch, backend_ov.py:357-431),
 // weight the outputs by the routing weights and add the sigmoid-gated shared
-// expert (shared_expert.py:395-414).
+// expert (shared_expert.py:200-219).
 //
 // Arithmetic.  The expert weights are dequantised to fp16 in shared memory
 // with the same value the reference's f16 dequantisation gives

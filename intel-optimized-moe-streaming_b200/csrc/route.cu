@@ -1,8 +1,8 @@
 // route.cu -- router scores, top-k selection and routing weights.
 //
 // Device form of ExpertRouter.scores/route (reference
-// src/flash_moe/router.py:241-271) for a batch of tokens, plus the
-// shared-expert gate sigmoid(x . w_inp) (src/flash_moe/shared_expert.py:437).
+// src/flash_moe/router.py:140-170) for a batch of tokens, plus the
+// shared-expert gate sigmoid(x . w_inp) (src/flash_moe/shared_expert.py:242).
 //
 //  k_scores: one warp per (token, expert) fp32 dot product over H, 16-byte
 //            loads of the [E x H] router rows; + the optional bias.

@@ -1,7 +1,7 @@
 // topk.cuh -- top-k selection and routing weights of one token, one warp.
 //
 // Same selection and arithmetic as ExpertRouter.route (reference
-// src/flash_moe/router.py:252-271): the k highest scores in descending order
+// src/flash_moe/router.py:151-170): the k highest scores in descending order
 // (ties to the lower expert id), a float64 softmax over those k only with
 // numpy's summation order for the denominator (np.add.reduce pairwise sum),
 // uniform weights if the sum is not finite or not positive, and the weights
@@ -160,7 +160,7 @@ __device__ __forceinline__ void topk_select_warp(uint32_t (&k)[8], int (&id)[8],
 }
 
 // Routing weights of the K selections lanes 0..K-1 hold (topk_select_warp):
-// the float64 softmax over those k only (router.py:258-269), written to
+// the float64 softmax over those k only (router.py:158-168), written to
 // ids[lane] / w[lane].  All 32 lanes must call.
 __device__ __forceinline__ void topk_weights_warp(uint32_t my_k, int my_id, int K, int* ids,
                                                   float* w) {
@@ -262,7 +262,7 @@ __device__ __forceinline__ bool load_score_words(const uint64_t* words, int E, u
 
 #undef MOE_CSWAP
 
-// sigmoid of the reference shared-expert gate (shared_expert.py:250-257).
+// sigmoid of the reference shared-expert gate (shared_expert.py:55-62).
 __device__ __forceinline__ float shared_sigmoid(float v) {
     if (v >= 0.f) return 1.0f / (1.0f + expf(-v));
     const float e = expf(v);

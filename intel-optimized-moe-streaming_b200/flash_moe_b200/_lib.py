@@ -58,6 +58,15 @@ class Step(C.Structure):
     ]
 
 
+def exports(lib: C.CDLL, name: str) -> bool:
+    """Whether the loaded library exports `name`."""
+    try:
+        getattr(lib, name)
+    except AttributeError:
+        return False
+    return True
+
+
 def _bind(lib: C.CDLL) -> None:
     i, i64, vp, f = C.c_int, C.c_int64, C.c_void_p, C.c_float
     sigs = {
@@ -99,6 +108,8 @@ def _bind(lib: C.CDLL) -> None:
         "moe_b200_version": (i, []),
     }
     for name, (res, args) in sigs.items():
+        if not exports(lib, name):
+            continue
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
@@ -109,9 +120,23 @@ def library_path() -> Path:
     return LIB
 
 
-def load(build_if_missing: bool = True) -> C.CDLL:
-    """Load (building first when sources are newer and nvcc is present)."""
+_extra: dict[str, C.CDLL] = {}
+
+
+def load(build_if_missing: bool = True, path: str | Path | None = None) -> C.CDLL:
+    """Load (building first when sources are newer and nvcc is present).
+
+    ``path`` names another build of the library (same exports) instead of
+    the in-tree one; it is loaded once per resolved path."""
     global _lib
+    if path is not None and Path(path).resolve() != LIB.resolve():
+        key = str(Path(path).resolve())
+        with _lock:
+            if key not in _extra:
+                other = C.CDLL(key)
+                _bind(other)
+                _extra[key] = other
+            return _extra[key]
     with _lock:
         if _lib is not None:
             return _lib

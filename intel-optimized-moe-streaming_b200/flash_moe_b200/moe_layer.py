@@ -1,77 +1,58 @@
-"""The MoE layer entry points, with the reference's signatures.
+"""The MoE layer entry points of the B200 backend, with the reference's
+signatures (``src/flash_moe/moe_layer.py:39-47`` and ``:110-118``).
 
-``run_moe_layer`` and ``run_moe_sequence`` take the arguments of their
-reference counterparts (``src/flash_moe/moe_layer.py:39-47`` and
-``:110-118``).  When the backend offers ``forward_layer`` (the B200 backend
-does) the whole layer -- routing with the layer's resident router, the top-k
-experts, the weighted sum in top-k order and the sigmoid-gated shared expert
--- runs as one device call per batch of tokens, and the ``router`` and
-``shared_expert`` arguments only have to agree with the resident layer.
-Otherwise the reference algorithm runs unchanged: route, ``backend.forward``
-per selected expert on the backend's executor, ``combined += w * out`` in
-top-k order, then ``+ shared_expert.forward``.
+On this backend a layer is ONE device call for a batch of tokens: routing
+with the layer's resident router, the top-k experts, the weighted sum in
+top-k order and the sigmoid-gated shared expert all run inside the kernels
+(``B200ExpertBackend.forward_layer``).  The ``router`` and ``shared_expert``
+arguments are therefore not called; they are checked against the resident
+layer instead: the shapes and ``top_k`` must agree, and the router's gate
+must be kept in fp32 (``gate_dtype`` float32), because the resident router
+is the fp32 ``ffn_gate_inp`` tensor -- the reference's default gate
+rounding to fp16 (``src/flash_moe/router.py:43``) would select experts from
+different scores.
+
+For a backend without ``forward_layer`` (one that serves single experts
+only), use the reference's own ``run_moe_layer`` / ``run_moe_sequence``: they
+drive ``B200ExpertBackend.forward`` one expert at a time unchanged.
 """
 from __future__ import annotations
 
-from concurrent.futures import ThreadPoolExecutor
 from typing import Any
 
 import numpy as np
 
-from .key import ExpertKey
 
-
-def _fused(backend) -> bool:
-    return callable(getattr(backend, "forward_layer", None))
-
-
-def _check_router(backend, layer, router, hidden_size, intermediate_size):
+def _resident_layer(backend, layer: int, router, hidden_size: int, intermediate_size: int):
+    """The resident layer's weights after checking the call against them."""
+    if not callable(getattr(backend, "forward_layer", None)):
+        raise TypeError("this entry point needs a backend with forward_layer (the B200 "
+                        "backend); per-expert backends run under the reference's run_moe_layer")
     lw = backend.store.layer(layer).weights
-    if hidden_size != lw.hidden or intermediate_size != lw.inter:
+    if (hidden_size, intermediate_size) != (lw.hidden, lw.inter):
         raise ValueError(f"layer {layer} is resident as {lw.hidden}x{lw.inter}, "
                          f"called with {hidden_size}x{intermediate_size}")
-    top_k = getattr(router, "top_k", lw.top_k)
-    if top_k != lw.top_k:
-        raise ValueError(f"router top_k {top_k} differs from the resident layer's {lw.top_k}")
+    if router is not None:
+        wanted = {"top_k": lw.top_k, "num_experts": lw.n_experts, "hidden_size": lw.hidden}
+        for attr, value in wanted.items():
+            got = getattr(router, attr, value)
+            if got != value:
+                raise ValueError(f"router {attr} {got} differs from the resident layer's {value}")
+        gate_dtype = getattr(router, "gate_dtype", np.dtype(np.float32))
+        if np.dtype(gate_dtype) != np.float32:
+            raise ValueError(f"router gate kept as {np.dtype(gate_dtype)}: the resident router "
+                             "is fp32 (construct ExpertRouter with gate_dtype=np.float32)")
+    return lw
 
 
 def run_moe_layer(layer: int, activation, router, backend: Any, hidden_size: int,
                   intermediate_size: int, shared_expert: Any = None) -> np.ndarray:
     """One token through one MoE layer; returns fp32 [hidden_size]."""
-    if _fused(backend):
-        _check_router(backend, layer, router, hidden_size, intermediate_size)
-        return backend.forward_layer(layer, np.asarray(activation, dtype=np.float32).reshape(-1))
-
-    expert_ids, weights = router.route(activation)
-    keys = [ExpertKey(layer, e) for e in expert_ids]
-    prefetch = getattr(backend, "prefetch_weights", None)
-    if prefetch is not None:
-        prefetch(keys)
-    combined = np.zeros(hidden_size, dtype=np.float32)
-    executor = getattr(backend, "_moe_executor", None)
-    own = executor is None
-    if own:
-        executor = ThreadPoolExecutor(max_workers=max(1, len(keys)))
-    try:
-        futures = [executor.submit(backend.forward, k, activation, hidden_size, intermediate_size)
-                   for k in keys]
-        try:
-            for fut, w in zip(futures, weights):
-                combined += w * np.asarray(fut.result(), dtype=np.float32)
-        finally:
-            for fut in futures:
-                try:
-                    fut.result()
-                except Exception:
-                    pass
-    finally:
-        if own:
-            executor.shutdown(wait=True)
-    if shared_expert is not None:
-        shared_out = shared_expert.forward(layer, activation)
-        if shared_out is not None:
-            combined = combined + shared_out
-    return combined
+    _resident_layer(backend, layer, router, hidden_size, intermediate_size)
+    x = np.asarray(activation, dtype=np.float32).reshape(-1)
+    if x.size != hidden_size:
+        raise ValueError(f"activation has {x.size} elements, expected {hidden_size}")
+    return backend.forward_layer(layer, x)
 
 
 def run_moe_sequence(layer: int, activations: np.ndarray, router, backend: Any,
@@ -81,8 +62,5 @@ def run_moe_sequence(layer: int, activations: np.ndarray, router, backend: Any,
     if activations.ndim != 2 or activations.shape[1] != hidden_size:
         raise ValueError(f"MoE activations must have shape (tokens, {hidden_size}), "
                          f"got {activations.shape}")
-    if _fused(backend):
-        _check_router(backend, layer, router, hidden_size, intermediate_size)
-        return backend.forward_layer(layer, activations)
-    return np.stack([run_moe_layer(layer, a, router, backend, hidden_size, intermediate_size,
-                                   shared_expert) for a in activations])
+    _resident_layer(backend, layer, router, hidden_size, intermediate_size)
+    return backend.forward_layer(layer, activations)

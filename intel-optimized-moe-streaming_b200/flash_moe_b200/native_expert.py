@@ -1,23 +1,25 @@
-"""Drop-in for the reference's ctypes binding of the native expert kernel
-(``src/flash_moe/native_expert.py``), backed by ``libmoe_b200.so``.
+"""The reference's native-kernel Python API over ``libmoe_b200.so``.
 
-``NativeExpert(path).forward(tensors, kinds, activation, hidden, inter)``
-has the reference's arguments, result and error behaviour: the three packed
-byte buffers go to ``moe_quant_expert`` (here the sm_100a kernel), a nonzero
-status raises ``RuntimeError("native expert failed with status N")``.  Like
-the reference it passes ``fp16_graph=1`` unless told otherwise.
+The reference binds its CPU DLL with ctypes in ``src/flash_moe/native_expert.py``
+(``NativeExpert`` :13-37, ``load_native_expert`` :40-75, ``NativeDelta``
+:78-101).  That binding works unchanged against this library, which exports
+the same C functions; this module is the package's own form of the same
+API, built on ``_lib``:
 
-``NativeDelta(library).forward(state, q, k, v, beta, gate)`` is the
-reference's DeltaNet binding (``native_expert.py:76-98``) over the sm_100a
-``moe_delta_heads``: same shapes, checks, in-place state update and
-``RuntimeError("native DeltaNet failed with status N")``.  ``NativeExpert``
-exposes it as ``.delta`` like the reference (``native_expert.py:21``).
+* ``NativeExpert(path=None, fp16_graph=1).forward(tensors, kinds,
+  activation, hidden, intermediate)`` -> fp32 [hidden]: one routed expert
+  through ``moe_quant_expert``.  Buffers may be ``bytes``, ``bytearray``,
+  ``memoryview`` or uint8 arrays; the reference passes ``fp16_graph=1``.
+* ``NativeDelta(library=None).forward(state, q, k, v, beta, gate)``: the
+  DeltaNet step ``moe_delta_heads`` on host arrays (state updated in place),
+  and ``forward_device`` on CUDA tensors (``moe_b200_delta_heads``).
+* ``load_native_expert(mode, library, device, tensor_types)``: the
+  ``auto|native|openvino`` selection, with this library's requirement -- a
+  CUDA device -- in place of the reference's AVX2/FMA/F16C CPU check.
 
-``load_native_expert(mode, library, device, tensor_types)`` keeps the
-reference's ``auto|native|openvino`` policy (``native_expert.py:40-75``): the
-gate is a visible CUDA device instead of a CPU with AVX2/FMA/F16C, and
-``native`` raises ``RuntimeError`` with the reason when the library cannot
-run.
+A nonzero status raises ``RuntimeError("native expert failed with status
+N")`` (``"native DeltaNet failed ..."``), the messages the reference's
+callers and tests match.
 """
 from __future__ import annotations
 
@@ -29,61 +31,70 @@ import numpy as np
 from . import _lib
 from .formats import SUPPORTED_TYPES
 
+EXPERT_TENSORS = ("gate", "up", "down")
+
+
+def _u8(buf) -> np.ndarray:
+    """A flat uint8 view of a packed tensor (no copy for bytes-like input)."""
+    if isinstance(buf, (bytes, bytearray, memoryview)):
+        return np.frombuffer(buf, dtype=np.uint8)
+    return np.ascontiguousarray(buf, dtype=np.uint8).reshape(-1)
+
+
+def _status(what: str, code: int) -> None:
+    if code != 0:
+        raise RuntimeError(f"native {what} failed with status {code}")
+
 
 class NativeExpert:
-    def __init__(self, path: Path | None = None, fp16_graph: int = 1):
-        if path is None:
-            self.library = _lib.load()
-        else:
-            self.library = C.CDLL(str(Path(path).resolve()))
-            _lib._bind(self.library)
-        self.function = self.library.moe_quant_expert
+    """One quantised SwiGLU expert per call on the B200 (``moe_quant_expert``)."""
+
+    def __init__(self, path: str | Path | None = None, fp16_graph: int = 1):
+        self.library = _lib.load(path=path)
         self.fp16_graph = int(fp16_graph)
-        self.delta = NativeDelta(self.library) if hasattr(self.library, "moe_delta_heads") else None
+        self.delta = NativeDelta(self.library) if _lib.exports(self.library,
+                                                               "moe_delta_heads") else None
+
+    @property
+    def function(self):
+        return self.library.moe_quant_expert
 
     def forward(self, tensors, kinds, activation, hidden, intermediate):
-        arrays = [np.frombuffer(tensors[name], np.uint8) if isinstance(tensors[name], (bytes, bytearray))
-                  else np.ascontiguousarray(tensors[name], dtype=np.uint8).reshape(-1)
-                  for name in ("gate", "up", "down")]
-        args = []
-        for name, raw in zip(("gate", "up", "down"), arrays):
-            args.extend((kinds[name], raw.ctypes.data, raw.nbytes))
+        views = {name: _u8(tensors[name]) for name in EXPERT_TENSORS}
         x = np.ascontiguousarray(activation, dtype=np.float32).reshape(-1)
         if x.size != hidden:
             raise ValueError("native expert activation shape mismatch")
-        out = np.empty(hidden, np.float32)
-        code = self.function(*args, x.ctypes.data, hidden, intermediate,
-                             out.ctypes.data, self.fp16_graph)
-        if code:
-            raise RuntimeError(f"native expert failed with status {code}")
-        return out
+        y = np.empty(hidden, dtype=np.float32)
+        triples = [v for name in EXPERT_TENSORS
+                   for v in (kinds[name], views[name].ctypes.data, views[name].size)]
+        _status("expert", self.function(*triples, x.ctypes.data, hidden, intermediate,
+                                        y.ctypes.data, self.fp16_graph))
+        return y
 
 
 class NativeDelta:
-    """All-head fp32 DeltaNet state update on the GPU (``moe_delta_heads``)."""
+    """The DeltaNet decode recurrence of every head in one call."""
 
     def __init__(self, library=None):
         self.library = library if library is not None else _lib.load()
-        self.function = self.library.moe_delta_heads
-        self.function.argtypes = [C.c_void_p] * 7 + [C.c_int] * 3
-        self.function.restype = C.c_int
+
+    @staticmethod
+    def _shapes(heads: int, key_dim: int, value_dim: int):
+        return [(heads, key_dim), (heads, key_dim), (heads, value_dim), (heads,), (heads,)]
 
     def forward(self, state, q, k, v, beta, gate):
-        """Host arrays, as the reference: ``state`` (heads, value_dim,
-        key_dim) fp32 C-contiguous, updated in place; returns the
-        (heads, value_dim) output."""
+        """Host arrays: ``state`` (heads, value_dim, key_dim) fp32,
+        C-contiguous, updated in place; returns the (heads, value_dim)
+        output."""
         if state.dtype != np.float32 or not state.flags.c_contiguous:
             raise ValueError("DeltaNet state must be contiguous FP32")
-        nv, dv, dk = state.shape
-        arrays = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v, beta, gate)]
-        shapes = [(nv, dk), (nv, dk), (nv, dv), (nv,), (nv,)]
-        if any(a.shape != shape for a, shape in zip(arrays, shapes)):
+        heads, value_dim, key_dim = state.shape
+        ins = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v, beta, gate)]
+        if [a.shape for a in ins] != self._shapes(heads, key_dim, value_dim):
             raise ValueError("DeltaNet native input shape mismatch")
-        out = np.empty((nv, dv), np.float32)
-        pointers = [state.ctypes.data] + [a.ctypes.data for a in arrays] + [out.ctypes.data]
-        code = self.function(*pointers, nv, dk, dv)
-        if code:
-            raise RuntimeError(f"native DeltaNet failed with status {code}")
+        out = np.empty((heads, value_dim), dtype=np.float32)
+        ptrs = [state.ctypes.data, *(a.ctypes.data for a in ins), out.ctypes.data]
+        _status("DeltaNet", self.library.moe_delta_heads(*ptrs, heads, key_dim, value_dim))
         return out
 
     def forward_device(self, state, q, k, v, beta, gate, out=None, status=None, stream=None):
@@ -95,23 +106,20 @@ class NativeDelta:
         import torch
         if state.dtype != torch.float32 or not state.is_contiguous() or not state.is_cuda:
             raise ValueError("DeltaNet state must be a contiguous FP32 CUDA tensor")
-        nv, dv, dk = state.shape
+        heads, value_dim, key_dim = state.shape
         ins = [t.contiguous() for t in (q, k, v, beta, gate)]
-        shapes = [(nv, dk), (nv, dk), (nv, dv), (nv,), (nv,)]
-        for t, shape in zip(ins, shapes):
+        for t, shape in zip(ins, self._shapes(heads, key_dim, value_dim)):
             if tuple(t.shape) != shape or t.dtype != torch.float32 or t.device != state.device:
                 raise ValueError("DeltaNet device input shape, dtype or device mismatch")
         if status is not None and (status.dtype != torch.int32 or status.numel() < 2
                                    or not status.is_cuda):
             raise ValueError("DeltaNet status must be an int32 CUDA tensor of two elements")
         if out is None:
-            out = torch.empty((nv, dv), dtype=torch.float32, device=state.device)
-        handle = (stream if stream is not None else torch.cuda.current_stream(state.device)).cuda_stream
-        code = self.library.moe_b200_delta_heads(
-            state.data_ptr(), *(t.data_ptr() for t in ins), out.data_ptr(), nv, dk, dv,
-            status.data_ptr() if status is not None else None, handle)
-        if code:
-            raise RuntimeError(f"native DeltaNet failed with status {code}")
+            out = torch.empty((heads, value_dim), dtype=torch.float32, device=state.device)
+        stream = stream if stream is not None else torch.cuda.current_stream(state.device)
+        _status("DeltaNet", self.library.moe_b200_delta_heads(
+            state.data_ptr(), *(t.data_ptr() for t in ins), out.data_ptr(), heads, key_dim,
+            value_dim, status.data_ptr() if status is not None else None, stream.cuda_stream))
         return out
 
 
@@ -123,28 +131,41 @@ def cuda_device_count() -> int:
         return 0
 
 
+_MODES = ("auto", "native", "openvino")
+
+
+def _why_not(device, tensor_types) -> str | None:
+    """The first reason this library cannot serve the experts, or None."""
+    name = str(device).split(":")[0].upper() if device is not None else "CUDA"
+    checks = (
+        (name in ("CUDA", "GPU"), f"the B200 expert kernels need a CUDA device, not {device}"),
+        (cuda_device_count() > 0, "no CUDA device is visible"),
+        (bool(tensor_types) and all(kinds.get(t) in SUPPORTED_TYPES
+                                    for kinds in tensor_types.values() for t in EXPERT_TENSORS),
+         "expert quantization is unsupported"),
+    )
+    return next((reason for ok, reason in checks if not ok), None)
+
+
 def load_native_expert(mode, library, device, tensor_types):
-    if mode not in ("auto", "native", "openvino"):
+    """``NativeExpert`` over `library` (default: the in-tree build) when it
+    can serve `tensor_types` on `device`; None for ``openvino`` and for
+    ``auto`` when it cannot; ``native`` raises ``RuntimeError(reason)``."""
+    if mode not in _MODES:
         raise ValueError("native_decode must be auto, native, or openvino")
     if mode == "openvino":
         return None
-    reason = None
-    if cuda_device_count() < 1:
-        reason = "native experts require a CUDA device (B200)"
-    elif not tensor_types or any(
-        kinds.get(name) not in SUPPORTED_TYPES
-        for kinds in tensor_types.values() for name in ("gate", "up", "down")
-    ):
-        reason = "expert quantization is unsupported"
+    reason = _why_not(device, tensor_types)
+    expert = None
     if reason is None:
         try:
-            result = NativeExpert(library)
+            expert = NativeExpert(library)
         except (OSError, AttributeError, RuntimeError) as error:
             reason = f"kernel unavailable ({error})"
-        else:
-            print("[Experts] native quantized B200 decode")
-            print("[DeltaNet] native FP32 decode recurrence (B200)")
-            return result
+    if expert is not None:
+        print("[Experts] native quantized B200 decode; DeltaNet "
+              + ("native" if expert.delta is not None else "NumPy"))
+        return expert
     if mode == "native":
         raise RuntimeError(reason)
     print(f"[Experts] OpenVINO decode: {reason}")

@@ -11,15 +11,16 @@ Two layers:
   ``kquant_oracle.c``), plus ``ReferenceLibrary`` for the reference's own
   sources compiled in place into ``_ref/`` (``make ref``).
 * numpy restatements of the Python MoE layer the native kernel sits in:
-  ``route`` (``src/flash_moe/router.py:241-271``), ``run_moe_layer``
+  ``route`` (``src/flash_moe/router.py:140-170``), ``run_moe_layer``
   (``src/flash_moe/moe_layer.py:39-107``), ``run_moe_sequence``
-  (``moe_layer.py:110-195``), the shared expert (``shared_expert.py:395-446``)
+  (``moe_layer.py:110-195``), the shared expert (``shared_expert.py:200-251``)
   and RMSNorm (``norm.py:21-30``).  They perform the same numpy operations in
   the same order, so on one host they give the reference's bits.
 """
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
@@ -43,13 +44,21 @@ def build_oracle(force: bool = False) -> Path:
     return ORACLE_LIB
 
 
-def build_reference(ref_root: str | Path = "/root/reference") -> Path | None:
+def reference_root() -> Path:
+    """The reference checkout: ``$FLASH_MOE_REFERENCE_ROOT``, else a sibling
+    directory ``reference`` of this repository."""
+    env = os.environ.get("FLASH_MOE_REFERENCE_ROOT")
+    return Path(env) if env else HERE.parent.parent / "reference"
+
+
+def build_reference(ref_root: str | Path | None = None) -> Path | None:
     """Compile the reference's own ``cpp/moe_quant_dot.cpp`` into ``_ref/``.
 
     Returns None when the reference sources are not present (GPU boxes only
     carry the already-built library)."""
     if REF_LIB.exists():
         return REF_LIB
+    ref_root = reference_root() if ref_root is None else ref_root
     if not (Path(ref_root) / "cpp" / "moe_quant_dot.cpp").exists():
         return None
     subprocess.run(["make", "-C", str(HERE), "ref", f"REF={ref_root}"],
@@ -143,7 +152,7 @@ class ReferenceLibrary(_KQuantLib):
 def route(x: np.ndarray, gate_he: np.ndarray, top_k: int, bias: np.ndarray | None = None):
     """Top-k ids and softmax weights of one token.
 
-    Restates ``ExpertRouter.scores/route`` (``src/flash_moe/router.py:241-271``):
+    Restates ``ExpertRouter.scores/route`` (``src/flash_moe/router.py:140-170``):
     fp32 ``x @ W`` with W laid out (hidden, experts), ``argsort`` ascending,
     the last k reversed, a float64 softmax over those k only.  ``bias`` (an
     fp32 per-expert logit offset, the popularity skew of the batched-decode
@@ -164,7 +173,7 @@ def route(x: np.ndarray, gate_he: np.ndarray, top_k: int, bias: np.ndarray | Non
 
 
 def sigmoid(x: np.ndarray) -> np.ndarray:
-    """Restates ``_sigmoid`` (``src/flash_moe/shared_expert.py:250-257``)."""
+    """Restates ``_sigmoid`` (``src/flash_moe/shared_expert.py:55-62``)."""
     out = np.empty_like(x)
     pos = x >= 0
     out[pos] = 1.0 / (1.0 + np.exp(-x[pos]))
@@ -174,11 +183,11 @@ def sigmoid(x: np.ndarray) -> np.ndarray:
 
 
 def shared_forward(x: np.ndarray, w: dict) -> np.ndarray:
-    """Restates ``SharedExpert.forward`` (``shared_expert.py:416-446``).
+    """Restates ``SharedExpert.forward`` (``shared_expert.py:221-251``).
 
     ``w`` holds fp32 arrays ``gate_inp`` [H], ``gate``/``up`` [I, H] and
     ``down`` [H, I] (the reference keeps them as fp16-rounded values promoted
-    to fp32, ``shared_expert.py:339-344,380-390``)."""
+    to fp32, ``shared_expert.py:157-195 and the fp32 views at :242-249``)."""
     x = np.asarray(x, dtype=np.float32).reshape(-1)
     gate = sigmoid((x @ np.asarray(w["gate_inp"], dtype=np.float32)).reshape(()))
     g = x @ np.asarray(w["gate"], dtype=np.float32).T
@@ -188,7 +197,7 @@ def shared_forward(x: np.ndarray, w: dict) -> np.ndarray:
 
 
 def shared_forward_batch(x: np.ndarray, w: dict) -> np.ndarray:
-    """Restates ``SharedExpert.forward_batch`` (``shared_expert.py:395-414``)."""
+    """Restates ``SharedExpert.forward_batch`` (``shared_expert.py:200-219``)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     gate = sigmoid(x @ np.asarray(w["gate_inp"], dtype=np.float32).reshape(-1))
     g = x @ np.asarray(w["gate"], dtype=np.float32).T
@@ -201,7 +210,7 @@ def shared_weights_from_packed(lib: _KQuantLib, packed: dict, kinds: dict,
                                hidden: int, inter: int, gate_inp) -> dict:
     """fp32 shared-expert weights as the reference loads them: dequantised to
     binary16 by ``dequant_k(..., want_f16=1)`` then promoted to fp32
-    (``shared_expert.py:380-390`` and ``:341-344``)."""
+    (``shared_expert.py:157-195`` and the fp32 views at ``:242-249``)."""
     shapes = {"gate": (inter, hidden), "up": (inter, hidden), "down": (hidden, inter)}
     out = {"gate_inp": np.asarray(gate_inp, dtype=np.float32).reshape(-1)}
     for role, shape in shapes.items():
@@ -292,7 +301,7 @@ def stack_block(x: np.ndarray, moe_fn, eps: float = 1e-6) -> np.ndarray:
 
 
 def max_relative_error(actual: np.ndarray, reference: np.ndarray) -> float:
-    """``max|a - r| / max|r|`` (``src/flash_moe/dequant.py:221-225``)."""
+    """``max|a - r| / max|r|`` (``src/flash_moe/dequant.py:198-202``)."""
     reference = np.asarray(reference, dtype=np.float64)
     scale = float(np.abs(reference).max()) if reference.size else 0.0
     if scale == 0.0:

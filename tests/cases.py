@@ -74,7 +74,7 @@ def layer_digest(lw, xs) -> str:
 
 def oracle_shared_weights(lib, lw):
     """fp32 shared-expert weights as the reference loads them (binary16
-    rounding, ``shared_expert.py:380-390``), or None."""
+    rounding, ``shared_expert.py:157-195``), or None."""
     if not lw.shared_inter:
         return None
     return O.shared_weights_from_packed(lib, lw.shared(), lw.shared_kinds, lw.hidden,
@@ -101,6 +101,26 @@ def oracle_layer(lib, lw, xs, fp16_graph: int = 0, selections=None):
         ids.append(e)
         ws.append(w)
     return np.stack(ys), np.array(ids), np.array(ws)
+
+
+def check_block(oracle, lw, x, y_dev, ids_dev, w_dev, tol: float = 1e-3, tie: float = 2e-5):
+    """One identity-mixer block (h = x + rmsnorm16(x); y = h +
+    f16(MoE(rmsnorm16(h)))) against the oracle, fed with the device's own
+    input x; a near tie resolved differently by the device is re-routed with
+    the device's selection.  Returns the max relative error."""
+    h = x + O.rmsnorm_f16(x).astype(np.float32)
+    n2 = O.rmsnorm_f16(h).astype(np.float32)
+    want_moe, want_ids, _ = oracle_layer(oracle, lw, n2[None])
+    if not np.array_equal(ids_dev, want_ids[0]):
+        s = np.sort(O.route(n2, lw.gate_he(), lw.top_k, lw.router_bias)[2])[::-1]
+        k = lw.top_k
+        assert abs(s[k - 1] - s[k]) <= tie * max(abs(s[k - 1]), 1e-30), (ids_dev, want_ids[0])
+        sel = [(list(map(int, ids_dev)), [float(v) for v in w_dev])]
+        want_moe, _, _ = oracle_layer(oracle, lw, n2[None], selections=sel)
+    want = h + want_moe[0].astype(np.float16).astype(np.float32)
+    err = O.max_relative_error(y_dev, want)
+    assert err <= tol, err
+    return err
 
 
 # DeltaNet step cases: name -> (seed, heads, key_dim, value_dim, steps).

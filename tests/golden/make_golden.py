@@ -1,9 +1,11 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Run in a container that has the reference project at /root/reference and the
-reference library built from its own sources (``make -C oracle ref``):
+Run in a container that has the reference project checked out (by default
+the directory ``reference`` beside this repository, or
+``$FLASH_MOE_REFERENCE_ROOT``) and the reference library built from its own
+sources (``make -C oracle ref``):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <reference checkout>]
 
 What produces the expected values:
   * dequantised blocks: ``gguf.quants.dequantize`` (gguf-py 0.19.0, the
@@ -234,12 +236,16 @@ def golden_layers(ref) -> None:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None,
+                    help="reference checkout (default: $FLASH_MOE_REFERENCE_ROOT or the "
+                         "sibling directory 'reference')")
     ap.add_argument("--only", nargs="*", default=None,
                     help="regenerate only these fixture groups "
                          "(delta dequant expert_small expert_cfg1 layers)")
     args = ap.parse_args()
     import oracle as O
+    if args.reference is None:
+        args.reference = str(O.reference_root())
     O.build_oracle()
     if O.build_reference(args.reference) is None:
         print("reference sources not found", file=sys.stderr)

@@ -11,13 +11,12 @@ import numpy as np
 import pytest
 
 import oracle as O
-from cases import oracle_layer
+from cases import check_block, oracle_layer
 from flash_moe_b200 import synth
 from flash_moe_b200.formats import Q4_K, Q8_0
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
-TIE = 2e-5
 
 SPEC = dict(hidden=1024, inter=256, n_experts=16, top_k=6, gate_type=Q4_K, up_type=Q4_K,
             down_type=Q8_0, shared_inter=512)
@@ -58,23 +57,6 @@ def test_independent_steps_equal_single_calls():
     assert be.device_errors() == 0
 
 
-def _check_block(oracle, lw, x, y_dev, ids_dev, w_dev):
-    """One block against the oracle; a near tie resolved differently by the
-    device is re-routed with the device's selection."""
-    h = x + O.rmsnorm_f16(x).astype(np.float32)
-    n2 = O.rmsnorm_f16(h).astype(np.float32)
-    want_moe, want_ids, _ = oracle_layer(oracle, lw, n2[None])
-    if not np.array_equal(ids_dev, want_ids[0]):
-        s = np.sort(O.route(n2, lw.gate_he(), lw.top_k, lw.router_bias)[2])[::-1]
-        k = lw.top_k
-        assert abs(s[k - 1] - s[k]) <= TIE * max(abs(s[k - 1]), 1e-30), (ids_dev, want_ids[0])
-        sel = [(list(map(int, ids_dev)), [float(v) for v in w_dev])]
-        want_moe, _, _ = oracle_layer(oracle, lw, n2[None], selections=sel)
-    want = h + want_moe[0].astype(np.float16).astype(np.float32)
-    err = O.max_relative_error(y_dev, want)
-    assert err <= TOL, err
-
-
 @pytest.mark.parametrize("n_layers", [1, 4])
 def test_block_chain_matches_oracle_layer_by_layer(oracle, n_layers):
     import torch
@@ -95,7 +77,7 @@ def test_block_chain_matches_oracle_layer_by_layer(oracle, n_layers):
     yh, ih, wh = ys.cpu().numpy(), ids.cpu().numpy(), ws.cpu().numpy()
     x = x0[0].cpu().numpy()
     for l in range(n_layers):
-        _check_block(oracle, lws[l], x, yh[l], ih[l], wh[l])
+        check_block(oracle, lws[l], x, yh[l], ih[l], wh[l])
         x = yh[l]
 
 
@@ -169,7 +151,7 @@ def test_stack_batch_layer_by_layer_matches_oracle(oracle):
         xh, yh = cur.cpu().numpy(), y.cpu().numpy()
         ih, wh = ids.cpu().numpy(), w.cpu().numpy()
         for t in range(0, T, 5):
-            _check_block(oracle, lws[l], xh[t], yh[t], ih[t], wh[t])
+            check_block(oracle, lws[l], xh[t], yh[t], ih[t], wh[t])
         cur = y
     # decode_stack_batch runs the same kernels; the prefill combine adds the
     # routed outputs with fp32 reductions in no fixed order, and that

@@ -5,8 +5,11 @@ memory is all reserved by its own pool, or a thread that must not enter the
 CUDA allocator while other work runs.  Its scratch is a fixed array inside
 the library.  This test calls it through the C ABI, twice in a row with
 different tokens, and checks each result against the allocating entry point
-(moe_quant_expert on the same device buffers) with the expert tests'
-tolerance.  It runs last in the suite and also passes on its own in a fresh
+(moe_quant_expert on the same device buffers) and against the CPU oracle's
+moe_quant_expert (the restatement of cpp/moe_quant_dot.cpp:171-214), with
+the expert tests' tolerance: the oracle catches an error the two device
+paths would share, such as in the plan the no-allocation entry fills in
+itself.  It runs last in the suite and also passes on its own in a fresh
 process.
 """
 from __future__ import annotations
@@ -36,7 +39,7 @@ def _args(kinds, dev):
 
 @pytest.mark.parametrize("case", ["triple", "config1"])
 @pytest.mark.parametrize("fg", [0, 1])
-def test_noalloc_matches_allocating_entry_point(lib, case, fg):
+def test_noalloc_matches_allocating_entry_point(lib, oracle, case, fg):
     import torch
     if case == "triple":
         tensors, x0 = small_expert_inputs(TRIPLES[1], 1)
@@ -61,7 +64,12 @@ def test_noalloc_matches_allocating_entry_point(lib, case, fg):
                                          stream.cuda_stream)
         assert rc == 0
         torch.cuda.synchronize()
-        err = O.max_relative_error(got.cpu().numpy(), want.cpu().numpy())
+        got_h = got.cpu().numpy()
+        err = O.max_relative_error(got_h, want.cpu().numpy())
+        assert err <= TOL[fg], err
+        rc, ref = oracle.expert(tensors, kinds, x, hidden, inter, fg)
+        assert rc == 0
+        err = O.max_relative_error(got_h, ref)
         assert err <= TOL[fg], err
 
 
