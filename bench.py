@@ -40,7 +40,15 @@ import threading
 import time
 from pathlib import Path
 
-import numpy as np
+# BLAS thread policy of the reference's entry point (chat.py:50-56): one
+# BLAS thread per process unless FLASH_MOE_BLAS_THREADS says otherwise, set
+# before NumPy loads, so the CPU arms run the same way with and without
+# torchrun (which sets OMP_NUM_THREADS=1)
+_BLAS_THREADS = os.environ.get("FLASH_MOE_BLAS_THREADS", "1")
+for _v in ("OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS", "BLIS_NUM_THREADS"):
+    os.environ[_v] = _BLAS_THREADS
+
+import numpy as np  # noqa: E402
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "intel-optimized-moe-streaming_b200"))
@@ -119,52 +127,160 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------- CPU arms
+#
+# The reference's CPU implementation of the path, timed on this host: its own
+# AVX2 kernels (cpp/moe_quant_dot.cpp, dequant_k.cpp, compiled from its
+# sources into oracle/_ref; the scalar oracle port if that build is absent)
+# driven by the numpy restatement of its Python layer (router, combine,
+# shared expert, run_moe_sequence: oracle/oracle.py, pinned bit for bit to the
+# reference's own Python by tests/golden).  The reference's Python itself
+# cannot travel to the GPU box.
 
-def cpu_reference_step_fn(lw, threads: int):
-    """One token through the layer with the reference's CPU implementation:
-    the reference AVX2 kernel per routed expert (oracle/_ref) on a thread
-    pool, numpy router/combine/shared expert.  Falls back to the scalar
-    oracle port when the reference library was not built."""
-    from concurrent.futures import ThreadPoolExecutor
+REF_WORKERS = 4  # the reference's expert pool (src/flash_moe/backend_ov.py:107,160)
+
+
+def _cpu_lib():
     import oracle as O
     try:
-        lib, kind = O.ReferenceLibrary(), "reference"
+        return O.ReferenceLibrary(), "reference"
     except FileNotFoundError:
-        lib, kind = O.KQuantOracle(), "port"
-    shared = O.shared_weights_from_packed(lib, lw.shared(), lw.shared_kinds, lw.hidden,
-                                          lw.shared_inter, lw.shared_gate_inp)
-    gate_he = lw.gate_he()
-    pool = ThreadPoolExecutor(max_workers=threads)
-    experts = [lw.expert(e) for e in range(lw.n_experts)]
+        return O.KQuantOracle(), "port"
 
-    def expert_fn(e, x):
-        rc, y = lib.expert(experts[e], lw.kinds, x, lw.hidden, lw.inter, 0)
+
+class CpuLayer:
+    """One MoE layer run on the host the way the reference's decode runs it:
+    route, the top-k native experts on a pool of `workers` threads
+    (moe_quant_expert, fp16_graph=0), the fp32 combine in top-k order, the
+    shared expert with binary16-rounded weights (numpy, BLAS threads as set
+    above)."""
+
+    def __init__(self, lw):
+        import oracle as O
+        self.O, self.lw = O, lw
+        self.lib, self.kind = _cpu_lib()
+        self.shared = (O.shared_weights_from_packed(self.lib, lw.shared(), lw.shared_kinds, lw.hidden,
+                                                    lw.shared_inter, lw.shared_gate_inp)
+                       if lw.shared_inter else None)
+        self.gate_he = lw.gate_he()
+        self.experts = [lw.expert(e) for e in range(lw.n_experts)]
+
+    def expert(self, e, x):
+        rc, y = self.lib.expert(self.experts[e], self.lw.kinds, x, self.lw.hidden, self.lw.inter, 0)
         if rc:
             raise RuntimeError(f"native expert failed with status {rc}")
         return y
 
-    def step(x):
-        ids, w, _ = O.route(x, gate_he, lw.top_k)
-        outs = list(pool.map(lambda e: expert_fn(e, x), ids))
-        comb = np.zeros(lw.hidden, np.float32)
+    def token(self, x, pool):
+        ids, w, _ = self.O.route(x, self.gate_he, self.lw.top_k, self.lw.router_bias)
+        outs = list(pool.map(lambda e: self.expert(e, x), ids))
+        comb = np.zeros(self.lw.hidden, np.float32)
         for o, wk in zip(outs, w):
             comb += wk * o
-        return comb + O.shared_forward(x, shared)
-    return step, kind, pool
+        return comb + self.O.shared_forward(x, self.shared) if self.shared is not None else comb
+
+    def experts_f32(self, e):
+        """(gate, up, down) fp32 of expert e through the reference's dequant_k."""
+        lw = self.lw
+        t = self.experts[e]
+        out = []
+        for name, rows, cols in (("gate", lw.inter, lw.hidden), ("up", lw.inter, lw.hidden),
+                                 ("down", lw.hidden, lw.inter)):
+            rc, w = self.lib.dequant(lw.kinds[name], t[name], rows * cols)
+            assert rc == 0
+            out.append(w.reshape(rows, cols))
+        return out
 
 
-def time_cpu(lw, tokens, threads, min_seconds=10.0, max_tokens=2000):
-    step, kind, pool = cpu_reference_step_fn(lw, threads)
-    step(tokens[0])
+def time_tokens(fn, tokens, min_seconds: float, max_tokens: int = 4000):
+    """Mean seconds per call of fn(token) over at least `min_seconds`."""
+    fn(tokens[0])
     n, t0 = 0, time.perf_counter()
     while True:
-        step(tokens[n % len(tokens)])
+        fn(tokens[n % len(tokens)])
         n += 1
         el = time.perf_counter() - t0
-        if (el >= min_seconds and n >= 8) or n >= max_tokens:
-            break
-    pool.shutdown()
-    return el / n, n, kind
+        if (el >= min_seconds and n >= 4) or n >= max_tokens:
+            return el / n, n
+
+
+def cpu_layer_baseline(lw, tokens, seconds: float) -> dict:
+    """Config 2 on the host: us per token with the reference's 4 expert
+    workers and with one worker per host thread; `value` is the faster."""
+    from concurrent.futures import ThreadPoolExecutor
+    cl = CpuLayer(lw)
+    threads = os.cpu_count() or 1
+    res = {}
+    for workers in sorted({REF_WORKERS, threads}):
+        with ThreadPoolExecutor(max_workers=workers) as pool:
+            per, n = time_tokens(lambda x: cl.token(x, pool), tokens, seconds / 2)
+        res[workers] = (per, n)
+    best = min(res, key=lambda k: res[k][0])
+    per, n = res[best]
+    return {"value": round(step_bytes(8) / per / 1e9, 4), "unit": UNIT, "cores": best,
+            "kind": cl.kind, "us_per_token": round(per * 1e6, 1),
+            "us_per_token_by_workers": {str(k): round(v[0] * 1e6, 1) for k, v in res.items()},
+            "blas_threads": int(_BLAS_THREADS),
+            "sample": f"{n} tokens of the config-2 layer with {best} expert workers "
+                      f"(reference default {REF_WORKERS}); {cpu_model()}, {threads} host threads"}
+
+
+def cpu_expert_baseline(seconds: float) -> dict:
+    """Config 1 on the host: one Q4_K expert per call, single thread, the
+    reference's moe_quant_expert (fp16_graph=0, the parity mode; the stock
+    product passes 1, timed beside it)."""
+    from flash_moe_b200 import synth
+    lib, kind = _cpu_lib()
+    tensors, kinds, x = synth.make_expert_q4k(seed=1)
+    out = {}
+    for fg in (0, 1):
+        def call(xv):
+            lib.expert(tensors, kinds, xv, 2048, 512, fg)
+        per, n = time_tokens(call, [x], seconds / 2)
+        out[fg] = (per, n)
+    per, n = out[0]
+    return {"us_per_call": round(per * 1e6, 1), "us_per_call_fp16_graph": round(out[1][0] * 1e6, 1),
+            "gbs": round(1_769_472 / per / 1e9, 4), "cores": 1, "kind": kind,
+            "sample": f"{n} calls, one thread, {cpu_model()}"}
+
+
+def cpu_sequence_baseline(lw, xs, sample_experts: int | None = None) -> dict:
+    """Many tokens through one layer on the host: the reference's
+    run_moe_sequence (src/flash_moe/moe_layer.py:110-195) with forward_batch =
+    the reference's dequant_k to fp32 + NumPy BLAS matmuls on all host cores
+    (its OpenVINO prefill graph is not available here), the shared expert
+    batched.  With `sample_experts`, only that many of the touched experts
+    run and the expert time is scaled to all of them."""
+    from threadpoolctl import threadpool_limits
+    cl = CpuLayer(lw)
+    O = cl.O
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    ids = []
+    for x in xs:
+        ids.append(O.route(x, cl.gate_he, lw.top_k, lw.router_bias)[0])
+    ids = np.array(ids)
+    t_route = time.perf_counter() - t0
+    uniq = np.unique(ids)
+    run = uniq if sample_experts is None else uniq[:sample_experts]
+    with threadpool_limits(limits=threads, user_api="blas"):
+        t0 = time.perf_counter()
+        for e in run:
+            rows = np.nonzero((ids == e).any(axis=1))[0]
+            g, u, d = cl.experts_f32(int(e))
+            xe = xs[rows]
+            gx, ux = xe @ g.T, xe @ u.T
+            _ = ((gx * O.sigmoid(gx)) * ux) @ d.T
+        t_exp = (time.perf_counter() - t0) * len(uniq) / max(len(run), 1)
+        t0 = time.perf_counter()
+        if cl.shared is not None:
+            _ = O.shared_forward_batch(xs, cl.shared)
+        t_sh = time.perf_counter() - t0
+    total = t_route + t_exp + t_sh
+    return {"s_per_step": round(total, 4), "tokens_per_s": round(len(xs) / total, 1),
+            "cores": threads, "kind": cl.kind, "unique_experts": int(len(uniq)),
+            "sample": f"{len(xs)} tokens; {len(run)} of {len(uniq)} touched experts run and "
+                      f"scaled; forward_batch = reference dequant_k f32 + NumPy BLAS "
+                      f"({threads} threads); {cpu_model()}"}
 
 
 def cpu_model() -> str:
@@ -177,34 +293,75 @@ def cpu_model() -> str:
     return "unknown"
 
 
+def cpu_stack_baseline(lw, H: int) -> dict:
+    """Config 5 on the host: batch 1 through 40 identity-mixer blocks (RMSNorm
+    f16 + residual around each layer, the reference's decode per layer; the
+    same layer's weights for every block: the CPU time does not depend on
+    which), 3 tokens; batch 32 through one block with run_moe_sequence's
+    forward_batch path (dequant_k f32 + BLAS), times 40."""
+    from concurrent.futures import ThreadPoolExecutor
+    from flash_moe_b200 import synth
+    cl = CpuLayer(lw)
+    O = cl.O
+    threads = os.cpu_count() or 1
+    xs = synth.make_tokens(7000, 3, H)
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        t0 = time.perf_counter()
+        for x in xs:
+            for _ in range(40):
+                h = x + O.rmsnorm_f16(x).astype(np.float32)
+                m = cl.token(O.rmsnorm_f16(h).astype(np.float32), pool)
+                x = h + m.astype(np.float16).astype(np.float32)
+        per1 = (time.perf_counter() - t0) / len(xs)
+    b32 = cpu_sequence_baseline(lw, synth.make_tokens(7001, 32, H))
+    return {"batch1_ms_per_token": round(per1 * 1e3, 2),
+            "batch1_gbs": round(40 * step_bytes(8) / per1 / 1e9, 4),
+            "batch32_ms_per_step": round(40 * b32["s_per_step"] * 1e3, 1), "cores": threads,
+            "kind": cl.kind,
+            "sample": f"batch 1: {len(xs)} tokens x 40 blocks, {threads} expert workers; batch 32: "
+                      f"one block's run_moe_sequence x 40 ({b32['sample']})"}
+
+
 def run_reference_arm(args) -> None:
+    """The reference's CPU implementation of config 2 on the host cores
+    (rank 0 only under torchrun): `--steps` tokens after `--warmup`, with the
+    reference's 4 expert workers and with one per host thread; the line
+    reports the faster, both per-token times beside it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    from concurrent.futures import ThreadPoolExecutor
     from flash_moe_b200 import synth
     lw = synth.make_layer(seed=0)
     tokens = synth.make_tokens(0, 64, lw.hidden)
+    cl = CpuLayer(lw)
     threads = os.cpu_count() or 1
-    step, kind, pool = cpu_reference_step_fn(lw, threads)
-    for i in range(args.warmup):
-        step(tokens[i % 64])
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        step(tokens[i % 64])
-    el = time.perf_counter() - t0
-    pool.shutdown()
-    per = el / args.steps
+    res = {}
+    for workers in sorted({REF_WORKERS, threads}):
+        with ThreadPoolExecutor(max_workers=workers) as pool:
+            for i in range(args.warmup):
+                cl.token(tokens[i % 64], pool)
+            t0 = time.perf_counter()
+            for i in range(args.steps):
+                cl.token(tokens[i % 64], pool)
+            res[workers] = (time.perf_counter() - t0) / args.steps
+    best = min(res, key=res.get)
+    per = res[best]
     gbs = step_bytes(8) / per / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(per * 1e3, 4), "us_per_token": round(per * 1e6, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (reference AVX2 kernels, fp16_graph=0; numpy layer)",
         "data": "synthetic (seeded, config-2 shapes and distributions)",
         "config": {"workload": "config 2: one MoE layer decode, 1 token/step, 256 experts top-8, "
                                "Q3_K/Q3_K/Q4_K experts + Q8_0 shared expert", "tokens_per_step": 1},
-        "cpu_baseline": {"value": round(gbs, 4), "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": f"{args.steps} tokens, {cpu_model()}"},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": UNIT, "cores": best, "kind": cl.kind,
+                         "us_per_token_by_workers": {str(k): round(v * 1e6, 1) for k, v in res.items()},
+                         "blas_threads": int(_BLAS_THREADS),
+                         "sample": f"{args.steps} tokens, {best} expert workers (reference default "
+                                   f"{REF_WORKERS}), {cpu_model()}, {threads} host threads"},
         "e2e": {"value": round(gbs, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -229,6 +386,67 @@ def _time_calls(fn, n: int, warmup: int = 3) -> float:
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / n
+
+
+def bench_expert(dev, peaks: dict, peak_kind: str, cpu_seconds: float | None) -> dict:
+    """Config 1: one Q4_K SwiGLU expert (hidden 2048, intermediate 512) for
+    one token through moe_quant_expert, the reference's C entry point: with
+    host buffers (the reference's unchanged ctypes caller: the 1,769,472
+    packed bytes cross PCIe every call) and with device buffers (weights
+    resident; calls rotate over 160 expert copies, 283 MB > 2x L2).  Each
+    call is synchronous, timed by the host clock over many calls."""
+    import torch
+    from flash_moe_b200 import _lib, synth
+    lib = _lib.load()
+    tensors, kinds, x = synth.make_expert_q4k(seed=1)
+    out = np.empty(2048, np.float32)
+    hbufs = {k: np.ascontiguousarray(v) for k, v in tensors.items()}
+
+    def host_call():
+        st = lib.moe_quant_expert(kinds["gate"], hbufs["gate"].ctypes.data, hbufs["gate"].size,
+                                  kinds["up"], hbufs["up"].ctypes.data, hbufs["up"].size,
+                                  kinds["down"], hbufs["down"].ctypes.data, hbufs["down"].size,
+                                  x.ctypes.data, 2048, 512, out.ctypes.data, 0)
+        assert st == 0, st
+    copies = 160
+    dev_t = {k: torch.from_numpy(v).to(dev).repeat(copies, 1) for k, v in
+             ((k, v.reshape(1, -1)) for k, v in hbufs.items())}
+    xd = torch.from_numpy(x).to(dev)
+    yd = torch.empty(2048, dtype=torch.float32, device=dev)
+    ctr = [0]
+
+    def dev_call():
+        i = ctr[0] % copies
+        ctr[0] += 1
+        g, u, d = dev_t["gate"][i], dev_t["up"][i], dev_t["down"][i]
+        st = lib.moe_quant_expert(kinds["gate"], g.data_ptr(), g.numel(), kinds["up"], u.data_ptr(),
+                                  u.numel(), kinds["down"], d.data_ptr(), d.numel(), xd.data_ptr(),
+                                  2048, 512, yd.data_ptr(), 0)
+        assert st == 0, st
+
+    res = {}
+    for name, fn, n in (("host_buffers", host_call, 400), ("device_buffers", dev_call, 2000)):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            fn()
+        res[name] = (time.perf_counter() - t0) / n
+    peak = peaks["hbm_gbs"]
+    gbs = 1_769_472 / res["device_buffers"] / 1e9
+    obj = {"config": "config 1: one Q4_K expert (2048 x 512), 1 token per call, moe_quant_expert "
+                     "(fp16_graph=0), synchronous",
+           "us_per_call_host_buffers": round(res["host_buffers"] * 1e6, 1),
+           "us_per_call_device_buffers": round(res["device_buffers"] * 1e6, 1),
+           "reference_published_ms": "0.607-0.750 (README.md:98-99, the reference's CPU kernel)",
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                        "note": "device buffers; a synchronous call per expert is launch-bound"}}
+    if cpu_seconds:
+        obj["cpu_baseline"] = cpu_expert_baseline(cpu_seconds)
+    del dev_t
+    return obj
 
 
 def bench_prefill(backend, layer: int, dev, peaks: dict, peak_kind: str) -> dict:
@@ -256,14 +474,20 @@ def bench_prefill(backend, layer: int, dev, peaks: dict, peak_kind: str) -> dict
             "kernels_per_call": backend.prefill_kernels(layer, T), "device_error": err}
 
 
-def bench_batched(dev, peaks: dict, peak_kind: str) -> dict:
+def with_cpu(obj: dict, fn, enabled: bool) -> dict:
+    if enabled:
+        obj["cpu_baseline"] = fn()
+    return obj
+
+
+def bench_batched(dev, peaks: dict, peak_kind: str, lw=None) -> dict:
     """Config 3: 64 concurrent tokens on the config-2 layer with a Zipf(1.1)
     router bias, one GPU: the fp32 decode engine and the tensor-core path."""
     import torch
     from flash_moe_b200 import synth
     from flash_moe_b200.backend import B200ExpertBackend
     from flash_moe_b200.store import ExpertArena
-    lw = synth.make_layer(seed=0, zipf_s=1.1)
+    lw = lw if lw is not None else synth.make_layer(seed=0, zipf_s=1.1)
     arena = ExpertArena(dev)
     arena.add_layer(0, lw)
     be = B200ExpertBackend(arena)
@@ -473,6 +697,66 @@ def check_last_step(runner, steps: int) -> float:
     return float(err.item())
 
 
+DECODE_STAMPS = ["entry", "x_ready", "router_rows", "scores_out", "topk", "shared_gu",
+                 "chunk0", "gate_up", "act_gathered", "act_quantised", "down_rows", "down",
+                 "step_end"]
+
+
+def run_trace(args) -> None:
+    """Phase timeline of the fused single-token kernel (config-2 layer): the
+    middle step of one multi-step launch, independent steps over `--copies`
+    layer copies and a chained 40-block stack, from the kernel's trace
+    stamps (%globaltimer, 32 ns ticks); us since the first CTA began the
+    step, median / max over the CTAs.  A diagnostic: nothing of it is a
+    bench value."""
+    import ctypes as C
+    import torch
+    from flash_moe_b200 import _lib, synth
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    from flash_moe_b200.ep import DecodeRunner
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lw = synth.make_layer(seed=0)
+    arena = ExpertArena(dev)
+    arena.add_layer(0, lw)
+    for c in range(1, args.copies):
+        arena.add_device_layer(c, arena.layer(0).clone())
+    be = B200ExpertBackend(arena)
+    G = torch.cuda.get_device_properties(dev).multi_processor_count
+    H = lw.hidden
+    toks = torch.from_numpy(synth.make_tokens(3, 64, H)).to(dev)
+    runner = DecodeRunner(be, list(range(args.copies)), toks)
+    steps = max(args.steps, 8)
+    ind = runner.step_tables(steps)
+    x1 = toks[:1]
+    tmp = torch.empty((2, H), dtype=torch.float32, device=dev)
+    y1 = torch.empty_like(x1)
+    rows = [(i % args.copies, _lib.STEP_BLOCK | (_lib.STEP_CHAIN if i else 0),
+             x1[0] if i == 0 else None, y1[0] if i == steps - 1 else tmp[i % 2], None, None)
+            for i in range(steps)]
+    chain = (be.layer_table(list(range(args.copies))), be.step_table(rows))
+    out = {}
+    for name, tabs in (("independent", ind), ("chained_blocks", chain)):
+        fn = lambda: be.decode_steps_device(tabs[0], tabs[1], steps, 0)  # noqa: E731
+        ms = _time_calls(fn, 3)
+        buf = torch.zeros(G * 32, dtype=torch.int64, device=dev)
+        be.lib.moe_b200_set_trace(C.c_void_p(buf.data_ptr()), G)
+        try:
+            fn()
+            torch.cuda.synchronize()
+        finally:
+            be.lib.moe_b200_set_trace(None, 0)
+        t = buf.view(G, 32).cpu().numpy()[:, :len(DECODE_STAMPS)].astype(np.float64)
+        t0 = t[:, 0][t[:, 0] > 0].min()
+        t = np.where(t > 0, (t - t0) / 1e3, np.nan)
+        stamps = {nm: [round(float(np.nanmedian(t[:, i])), 2), round(float(np.nanmax(t[:, i])), 2)]
+                  for i, nm in enumerate(DECODE_STAMPS) if np.isfinite(t[:, i]).any()}
+        out[name] = {"us_per_step": round(ms * 1e3 / steps, 2), "stamps_median_max_us": stamps}
+    out["device_error"] = be.device_errors()
+    print(json.dumps({"trace": out}), flush=True)
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -591,19 +875,24 @@ def run_gpu(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        per_tok, n, kind = time_cpu(lw, synth.make_tokens(1000, 64, H), os.cpu_count() or 1,
-                                    min_seconds=args.cpu_seconds)
-        cpu = {"value": round(step_bytes(8) / per_tok / 1e9, 4), "unit": UNIT,
-               "cores": os.cpu_count() or 1, "kind": kind,
-               "sample": f"{n} tokens of the same layer ({per_tok * 1e6:.0f} us/token), {cpu_model()}"}
+        cpu = cpu_layer_baseline(lw, synth.make_tokens(1000, 64, H), args.cpu_seconds)
     launches = 1 if tables is not None else runner.launches_per_step * args.steps
     graph = None
     tables = None
     extra = {}
     if rank == 0 and world == 1 and not args.no_extra:
-        extra["prefill"] = bench_prefill(backend, 0, dev, peaks, peak_kind)
-        extra["batched_decode"] = bench_batched(dev, peaks, peak_kind)
-        extra["stack"] = bench_stack(backend, 0, dev, peaks, peak_kind)
+        cpu_on = not args.no_cpu
+        extra["expert"] = bench_expert(dev, peaks, peak_kind, args.cpu_seconds if cpu_on else None)
+        extra["prefill"] = with_cpu(
+            bench_prefill(backend, 0, dev, peaks, peak_kind),
+            lambda: cpu_sequence_baseline(lw, synth.make_tokens(404, 4096, H), sample_experts=24),
+            cpu_on)
+        lwz = synth.make_layer(seed=0, zipf_s=1.1)
+        extra["batched_decode"] = with_cpu(
+            bench_batched(dev, peaks, peak_kind, lwz),
+            lambda: cpu_sequence_baseline(lwz, synth.make_tokens(3000, 64, H)), cpu_on)
+        extra["stack"] = with_cpu(bench_stack(backend, 0, dev, peaks, peak_kind),
+                                  lambda: cpu_stack_baseline(lw, H), cpu_on)
         extra["delta"] = bench_delta(dev, peaks, peak_kind, cpu=not args.no_cpu)
     if rank == 0:
         line = {
@@ -652,8 +941,9 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak", type=float, default=0.5)
-    ap.add_argument("--only", choices=["prefill", "delta"], default=None,
-                    help="run only the config-4 prefill measurement (for profiling)")
+    ap.add_argument("--only", choices=["prefill", "delta", "trace"], default=None,
+                    help="run only one measurement: the config-4 prefill or the DeltaNet step "
+                         "(for profiling), or the decode kernel's phase timeline")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the prefill and batched-decode measurements (N = 1)")
     args = ap.parse_args()
@@ -663,6 +953,8 @@ def main() -> None:
         run_reference_arm(args)
     elif args.only == "prefill":
         run_prefill_only(args)
+    elif args.only == "trace":
+        run_trace(args)
     elif args.only == "delta":
         import torch
         dev = torch.device("cuda", 0)

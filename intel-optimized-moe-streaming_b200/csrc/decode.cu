@@ -45,9 +45,11 @@
 
 namespace moeb200 {
 
-constexpr int kMaxChunks = 8;  // routed gate/up copy chunks (mbarriers 3..10)
-constexpr int kXBar = 3 + kMaxChunks;  // mbarrier of the prefetched token
-constexpr int kGatherPairs = 8;  // exchange-word pairs a lane has in flight per poll round
+constexpr int kMaxChunks = 8;             // routed gate/up copy chunks (mbarriers 3..10)
+constexpr int kXBar = 3 + kMaxChunks;      // mbarrier of the prefetched token
+constexpr int kSdBar = kXBar + 1;          // mbarrier of the shared-expert down rows
+constexpr int kNumBars = kSdBar + 1;
+constexpr int kGatherWords = 10;           // exchange words a thread has in flight per poll round
 
 struct FusedParams {
     moe_b200_layer L;        // shapes and block formats of every step's layer
@@ -60,19 +62,20 @@ struct FusedParams {
     int n_steps;
     float eps;               // RMSNorm epsilon of MOE_B200_STEP_BLOCK steps
     uint32_t* ctr;           // counters, error word at ctr[C_ERROR]
-    uint64_t* scores;        // [2][E]       exchange words (buffer = step parity)
+    uint64_t* scores;        // [2][S]       exchange words (buffer = step parity)
     uint64_t* act_r;         // [2][K x I]
     uint64_t* act_s;         // [2][Imax]
-    uint64_t* sg;            // [2]
+    uint64_t* yw;            // [2][H]       the layer output of a step a CHAIN step reads
     uint64_t* trace;         // [G x 32] phase timestamps of step n_steps / 2 (ns), or null
     int* err_out;            // null, or a host-visible word that receives (and clears) the
                              // error word at exit
     int G;
+    int S;                   // score slots: max(E, G), so every CTA writes one each step
     int with_shared;
     int max_router_rows, max_sgu_rows, max_out_rows, max_rgu_rows;
     int lpr_h, lpr_i, lpr_is;
     int chunk_rows;
-    uint32_t o_x32, o_h32, o_xq, o_router, o_sgate, o_sup, o_sdown, o_rgate, o_rup, o_rdown;
+    uint32_t o_x32, o_h32, o_xq, o_router, o_ginp, o_sgate, o_sup, o_sdown, o_rgate, o_rup, o_rdown;
     uint32_t o_act, o_aq, o_misc, total;
 };
 
@@ -85,7 +88,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     const moe_b200_layer& L0 = p.L;
     const int c = blockIdx.x, G = p.G, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nw = kFusedThreads / 32;
-    const int H = L0.hidden, I = L0.intermediate, E = L0.n_experts, K = L0.top_k;
+    const int H = L0.hidden, I = L0.intermediate, E = L0.n_experts, K = L0.top_k, S = p.S;
     const int Is = p.with_shared ? L0.shared_intermediate : 0;
     const int ebeg = L0.expert_begin, ecnt = L0.expert_count;
     const int64_t rb_gate = row_bytes(L0.gate_type, H), rb_up = row_bytes(L0.up_type, H);
@@ -95,86 +98,96 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     const int64_t rb_su = Is ? row_bytes(L0.shared_up_type, H) : 0;
     const int64_t rb_sd = Is ? row_bytes(L0.shared_down_type, Is) : 0;
     const int Imax = max(I, Is);
-    const bool tagged = E >= G;
     const uint32_t seq0 = ld_acquire(p.ctr + C_SEQ);
 
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + p.o_misc);       // [kXBar + 1]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + p.o_misc);       // [kNumBars]
     int* s_ids = reinterpret_cast<int*>(sm + p.o_misc + 128);          // [16]
     float* s_w = reinterpret_cast<float*>(sm + p.o_misc + 192);        // [16]
     int* s_act = reinterpret_cast<int*>(sm + p.o_misc + 256);          // [16] active slots
     int* s_nact = reinterpret_cast<int*>(sm + p.o_misc + 320);
     float* s_sg = reinterpret_cast<float*>(sm + p.o_misc + 324);
     float* s_part = reinterpret_cast<float*>(sm + p.o_misc + 384);     // [32] partial sums
-    float* s_scores = reinterpret_cast<float*>(sm + p.o_misc + 512);   // [E]
-    unsigned char* s_taken = reinterpret_cast<unsigned char*>(s_scores + E);
-    float* s_vout = reinterpret_cast<float*>(sm + p.o_misc + 512 + ((5 * E + 15) & ~15));
-    // per activation vector: the tag of the step whose codes it holds
-    volatile uint32_t* s_ready = reinterpret_cast<volatile uint32_t*>(
-        sm + p.o_misc + 512 + ((5 * E + 15) & ~15) + (K + 1) * p.max_out_rows * 4);
+    float* s_scores = reinterpret_cast<float*>(sm + p.o_misc + 512);   // [S]
+    unsigned char* s_taken = reinterpret_cast<unsigned char*>(s_scores + S);
+    float* s_vout = reinterpret_cast<float*>(sm + p.o_misc + 512 + ((5 * S + 15) & ~15));
     float* x32 = reinterpret_cast<float*>(sm + p.o_x32);
     float* h32 = reinterpret_cast<float*>(sm + p.o_h32);
 
-    const int r0 = part(E, c, G), r1 = part(E, c + 1, G);
+    const int r0 = part(S, c, G), r1 = part(S, c + 1, G);  // score slots; rows < E are router rows
+    const int re1 = min(r1, E), nr = max(0, re1 - r0);      // router rows of this CTA
     const int s0 = part(Is, c, G), s1 = part(Is, c + 1, G);
     const int h0 = part(H, c, G), h1 = part(H, c + 1, G);
     const int nh = h1 - h0;
     const int lpr_h = p.lpr_h, sub_h = lane / lpr_h, pr_h = lane % lpr_h;
-    const QVec xq = qvec_at(sm + p.o_xq, H);
 
     auto step_layer = [&](int s) -> const moe_b200_layer* {
         return p.steps ? p.layers + p.steps[s].layer : &p.L;
     };
-    // router rows of step s on bars[0], its shared-expert rows on bars[1]
-    auto issue_phase0 = [&](const moe_b200_layer* Ls) {
-        const float* router = Ls->router;
-        mbar_arrive_expect_tx(&bars[0], (uint32_t)((r1 - r0) * H * 4));
-        if (r1 > r0)
-            bulk_g2s(sm + p.o_router, router + (size_t)r0 * H, (uint32_t)((r1 - r0) * H * 4), &bars[0]);
-        if (Is) {
-            const uint8_t* sgp = Ls->shared_gate;
-            const uint8_t* sup = Ls->shared_up;
-            const uint8_t* sdp = Ls->shared_down;
-            mbar_arrive_expect_tx(&bars[1], (uint32_t)((s1 - s0) * (rb_sg + rb_su) + nh * rb_sd));
-            if (s1 > s0) {
-                bulk_g2s(sm + p.o_sgate, sgp + s0 * rb_sg, (uint32_t)((s1 - s0) * rb_sg), &bars[1]);
-                bulk_g2s(sm + p.o_sup, sup + s0 * rb_su, (uint32_t)((s1 - s0) * rb_su), &bars[1]);
-            }
-            if (nh > 0)
-                bulk_g2s(sm + p.o_sdown, sdp + h0 * rb_sd, (uint32_t)(nh * rb_sd), &bars[1]);
+    // The resident rows of a step, each set on its own mbarrier, so that each
+    // is reissued for the next step as soon as this step is done with it:
+    // router rows + shared gate vector (bars[0]), shared gate/up rows
+    // (bars[1]), shared down rows (bars[kSdBar]).
+    auto issue_router = [&](const moe_b200_layer* Ls) {
+        const uint32_t rbytes = (uint32_t)(nr * H * 4);
+        // the gate vector by TMA when 16-byte aligned, else read in place
+        const uint32_t gbytes = (Is && Ls->shared_gate_inp && (((uintptr_t)Ls->shared_gate_inp) & 15u) == 0)
+                                    ? (uint32_t)(H * 4) : 0u;
+        mbar_arrive_expect_tx(&bars[0], rbytes + gbytes);
+        if (nr > 0) bulk_g2s(sm + p.o_router, Ls->router + (size_t)r0 * H, rbytes, &bars[0]);
+        if (gbytes) bulk_g2s(sm + p.o_ginp, Ls->shared_gate_inp, gbytes, &bars[0]);
+    };
+    auto issue_sgu = [&](const moe_b200_layer* Ls) {
+        mbar_arrive_expect_tx(&bars[1], (uint32_t)((s1 - s0) * (rb_sg + rb_su)));
+        if (s1 > s0) {
+            bulk_g2s(sm + p.o_sgate, Ls->shared_gate + s0 * rb_sg, (uint32_t)((s1 - s0) * rb_sg), &bars[1]);
+            bulk_g2s(sm + p.o_sup, Ls->shared_up + s0 * rb_su, (uint32_t)((s1 - s0) * rb_su), &bars[1]);
         }
+    };
+    auto issue_sdown = [&](const moe_b200_layer* Ls) {
+        mbar_arrive_expect_tx(&bars[kSdBar], (uint32_t)(nh * rb_sd));
+        if (nh > 0) bulk_g2s(sm + p.o_sdown, Ls->shared_down + h0 * rb_sd, (uint32_t)(nh * rb_sd), &bars[kSdBar]);
     };
 
     // A step's token comes by TMA (issued before the step begins) unless it
     // is the previous step's output or not 16-byte aligned.
-    auto step_x = [&](int s) -> const float* { return p.steps ? p.steps[s].x : p.x; };
-    auto x_by_copy = [&](int s) -> bool {
-        const bool chain = p.steps && (p.steps[s].flags & MOE_B200_STEP_CHAIN) && s > 0;
-        return !chain && (((uintptr_t)step_x(s)) & 15u) == 0;
+    auto chained = [&](int s) -> bool {
+        return p.steps && s > 0 && (p.steps[s].flags & MOE_B200_STEP_CHAIN);
     };
+    auto step_x = [&](int s) -> const float* { return p.steps ? p.steps[s].x : p.x; };
+    auto x_by_copy = [&](int s) -> bool { return !chained(s) && (((uintptr_t)step_x(s)) & 15u) == 0; };
     auto issue_x = [&](int s) {
         mbar_arrive_expect_tx(&bars[kXBar], (uint32_t)(H * 4));
         bulk_g2s(x32, step_x(s), (uint32_t)(H * 4), &bars[kXBar]);
     };
+    // bounded wait of every thread on an mbarrier phase (one poller, then the CTA)
+    uint32_t ph = 0;  // parity of the phase each mbarrier is in
+    auto cta_wait = [&](int b) {
+        if (tid == 0 && !mbar_wait(&bars[b], (ph >> b) & 1u, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+        ph ^= 1u << b;
+        __syncthreads();
+    };
 
     if (tid == 0) {
-        for (int i = 0; i <= kXBar; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], 1);
         mbar_fence_init();
     }
-    if (tid <= kMaxTopK) s_ready[tid] = 0u;
     __syncthreads();
     if (tid == 0) {
-        issue_phase0(step_layer(0));
+        const moe_b200_layer* L1 = step_layer(0);
+        issue_router(L1);
+        if (Is) {
+            issue_sgu(L1);
+            issue_sdown(L1);
+        }
         if (x_by_copy(0)) issue_x(0);
     }
-    uint32_t ph = 0;  // parity of the phase each mbarrier is in
 
     for (int s = 0; s < p.n_steps; ++s) {
         uint64_t* trace = (p.trace && s == p.n_steps / 2) ? p.trace + (size_t)c * kTraceSlots : nullptr;
 #define TRACE(i) do { if (trace && tid == 0) trace[i] = global_ns(); } while (0)
         TRACE(0);
         const moe_b200_layer* Ls = step_layer(s);
-        const uint32_t gen = (uint32_t)G * (uint32_t)(s + 1);  // counter value once step s is done
-        const uint32_t tag = seq0 + (uint32_t)s + 1u;             // exchange-word tag of step s
+        const uint32_t tag = seq0 + (uint32_t)s + 1u;  // exchange-word tag of step s
         int sflags = 0;
         const float* xin = p.x;
         float* yout = p.y;
@@ -183,25 +196,48 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
         if (p.steps) {
             const moe_b200_step& st = p.steps[s];
             sflags = st.flags;
-            xin = (sflags & MOE_B200_STEP_CHAIN) && s > 0 ? p.steps[s - 1].y : st.x;
+            xin = st.x;
             yout = st.y;
             ids_out = st.topk_ids;
             w_out = st.topk_weights;
         }
         const int buf = s & 1;
-        uint64_t* scores = p.scores + (size_t)buf * E;
+        uint64_t* scores = p.scores + (size_t)buf * S;
         uint64_t* act_r = p.act_r + (size_t)buf * K * I;
         uint64_t* act_s = p.act_s + (size_t)buf * Imax;
-        uint64_t* sgp = p.sg + buf;
-        const bool chain = (sflags & MOE_B200_STEP_CHAIN) && s > 0;
+        const bool chain = chained(s);
         const bool block = (sflags & MOE_B200_STEP_BLOCK) != 0;
+        const bool next_chains = s + 1 < p.n_steps && chained(s + 1);
+        const moe_b200_layer* Ln = s + 1 < p.n_steps ? step_layer(s + 1) : nullptr;
 
-        // ---- the token (after the previous step, whose output it is, when chained)
+        // ---- the token: the previous step's output words (CHAIN), the
+        // prefetched copy, or direct loads
         if (chain) {
-            if (tid == 0 && !wait_flag(p.ctr + C_DONE, (uint32_t)G * (uint32_t)s, kWaitPolls))
-                set_error(p.ctr, ST_TIMEOUT);
-            __syncthreads();
-            for (int i = tid; i < H; i += kFusedThreads) x32[i] = __ldcg(xin + i);
+            const uint64_t* src = p.yw + (size_t)(buf ^ 1) * H;
+            bool ok = true;
+            for (int j0 = tid; j0 < H; j0 += kFusedThreads * kGatherWords) {
+                uint32_t pend = 0;
+#pragma unroll
+                for (int q = 0; q < kGatherWords; ++q)
+                    if (j0 + kFusedThreads * q < H) pend |= 1u << q;
+                for (uint32_t round = 0; pend != 0u; ++round) {
+                    if (round == kWaitPolls) {
+                        ok = false;
+                        break;
+                    }
+                    uint64_t wv[kGatherWords];
+#pragma unroll
+                    for (int q = 0; q < kGatherWords; ++q)
+                        wv[q] = ((pend >> q) & 1u) ? ld_word_gpu(src + j0 + kFusedThreads * q) : 0ull;
+#pragma unroll
+                    for (int q = 0; q < kGatherWords; ++q)
+                        if (((pend >> q) & 1u) && (uint32_t)(wv[q] >> 32) == tag - 1u) {
+                            pend &= ~(1u << q);
+                            x32[j0 + kFusedThreads * q] = __uint_as_float((uint32_t)wv[q]);
+                        }
+                }
+            }
+            if (!ok) set_error(p.ctr, ST_TIMEOUT);
         } else if (x_by_copy(s)) {
             if (tid == 0 && !mbar_wait(&bars[kXBar], (ph >> kXBar) & 1u, kWaitPolls))
                 set_error(p.ctr, ST_TIMEOUT);
@@ -215,10 +251,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             // (reference TransformerBlock.forward with an identity mixer,
             // src/flash_moe/transformer.py:229-247; RMSNorm norm.py:28-30)
             float ss = 0.f;
+#pragma unroll 1
             for (int i = tid; i < H; i += kFusedThreads) ss = fmaf(x32[i], x32[i], ss);
             ss = block_sum(ss, s_part);
             const float rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)H), p.eps));
             float ss2 = 0.f;
+#pragma unroll 1
             for (int i = tid; i < H; i += kFusedThreads) {
                 const float hv = __fadd_rn(x32[i], round16(__fdiv_rn(x32[i], rms)));
                 h32[i] = hv;
@@ -226,285 +264,274 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
             }
             ss2 = block_sum(ss2, s_part);
             const float rms2 = sqrtf(__fadd_rn(__fdiv_rn(ss2, (float)H), p.eps));
+#pragma unroll 1
             for (int i = tid; i < H; i += kFusedThreads) x32[i] = round16(__fdiv_rn(h32[i], rms2));
             __syncthreads();
         }
         TRACE(1);
 
-        // ---- router scores (rows [r0, r1)): each row split over nw/R warps,
-        // partial sums combined in a fixed order (deterministic)
-        if (tid == 0 && !mbar_wait(&bars[0], ph & 1u, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
-        ph ^= 1u;
-        __syncthreads();
+        // ---- router rows [r0, re1) and the shared gate x . w_inp (every CTA
+        // computes the gate itself: one more row of the same dot), each row
+        // split over nw / R warps, partial sums combined in a fixed order
+        // (deterministic); score slots [re1, r1) carry no score
+        cta_wait(0);
         TRACE(2);
         {
             const float* router_s = reinterpret_cast<const float*>(sm + p.o_router);
+            const bool ginp_tma = ((((uintptr_t)Ls->shared_gate_inp) & 15u) == 0);
+            const float* ginp_s = ginp_tma ? reinterpret_cast<const float*>(sm + p.o_ginp) : Ls->shared_gate_inp;
             const float* bias = Ls->router_bias;
-            const int R = r1 - r0;
-            if (R > 0 && R <= nw) {
-                const int spr = nw / R;
+            const bool with_gate = Is && Ls->shared_gate_inp;
+            // warps 0..nw-2: the router rows (<= nw - 1 of them, fused_plan);
+            // warp nw-1: the gate, lane-strided like the multi-token kernel
+            // (same summation order, so the two kernels' gates agree bit for bit)
+            const int nwr = nw - 1;
+            if (nr > 0) {
+                const int spr = nwr / nr;
                 const int row = warp / spr, sl = warp % spr;
-                if (row < R) {
+                if (warp < nwr && row < nr) {
                     const int cw = (H / spr) & ~3;  // 16-byte aligned slices
                     const int cc0 = sl * cw, cn = (sl == spr - 1) ? H - cc0 : cw;
-                    float acc = dot_f32_warp(router_s + (size_t)row * H + cc0, x32 + cc0, cn, lane);
+                    const float* rp = router_s + (size_t)row * H + cc0;
+                    const float* xp = x32 + cc0;
+                    float acc = 0.f;
+#pragma unroll 2
+                    for (int i = lane; i < (cn >> 2); i += 32) {
+                        const float4 a = reinterpret_cast<const float4*>(rp)[i];
+                        const float4 b = reinterpret_cast<const float4*>(xp)[i];
+                        acc = fmaf(a.x, b.x, acc);
+                        acc = fmaf(a.y, b.y, acc);
+                        acc = fmaf(a.z, b.z, acc);
+                        acc = fmaf(a.w, b.w, acc);
+                    }
+                    acc = warp_sum(acc);
                     if (lane == 0) s_part[warp] = acc;
                 }
-                __syncthreads();
-                if (tid < R) {
-                    float acc = 0.f;
-                    for (int q = 0; q < spr; ++q) acc += s_part[tid * spr + q];
-                    if (bias) acc = __fadd_rn(acc, bias[r0 + tid]);
-                    st_word_gpu(scores + r0 + tid, acc, tag);
-                }
-            } else {
-                for (int rr = warp; rr < R; rr += nw) {
-                    float acc = dot_f32_warp(router_s + (size_t)rr * H, x32, H, lane);
-                    if (lane == 0) {
-                        if (bias) acc = __fadd_rn(acc, bias[r0 + rr]);
-                        st_word_gpu(scores + r0 + rr, acc, tag);
-                    }
-                }
             }
+            if (warp == nw - 1 && with_gate) {
+                float acc = 0.f;
+#pragma unroll 4
+                for (int i = lane; i < H; i += 32) acc = fmaf(x32[i], ginp_s[i], acc);
+                acc = warp_sum(acc);
+                if (lane == 0) *s_sg = shared_sigmoid(acc);
+            }
+            __syncthreads();
+            if (tid < nr) {
+                const int spr = nwr / nr;
+                float acc = 0.f;
+                for (int q = 0; q < spr; ++q) acc += s_part[tid * spr + q];
+                if (bias) acc = __fadd_rn(acc, bias[r0 + tid]);
+                st_word_gpu(scores + r0 + tid, acc, tag);
+            }
+            if (tid >= nr && tid < r1 - r0) st_word_gpu(scores + r0 + tid, 0.f, tag);  // marker slots
+            if (Is && !with_gate && tid == 0) *s_sg = 1.f;
         }
+        // ---- the token quantised for the integer dot products
+#pragma unroll 1
+        for (int b = warp; b < H / 256; b += nw) quantize_block_ool(x32, sm + p.o_xq, H, b);
         __syncthreads();
-        if (tid == 0 && !tagged) red_release_add(p.ctr + C_ROUTER, 1);
+        // router rows, gate vector and the token copy are consumed: the next
+        // step's go out now
+        if (tid == 0 && Ln) {
+            issue_router(Ln);
+            if (x_by_copy(s + 1)) issue_x(s + 1);
+        }
         TRACE(3);
 
-        // ---- the token quantised for the integer dot products; shared gate
-        for (int b = warp; b < H / 256; b += nw) quantize_block_warp(x32, xq, b);
-        TRACE(23);
-        if (Is && c == 0 && warp == nw - 1) {
-            const float* ginp = Ls->shared_gate_inp;
-            float acc = 0.f;
-            for (int i = lane; i < H; i += 32) acc = fmaf(x32[i], ginp[i], acc);
-            acc = warp_sum(acc);
-            if (lane == 0) st_word_gpu(sgp, shared_sigmoid(acc), tag);
-        }
-        __syncthreads();
-        TRACE(24);
-        XLane xl;
-        load_xlane(xl, xq, pr_h >> 2, pr_h & 3);
-        TRACE(25);
-
-        // ---- routing (every CTA, identically): the selection first, so the
-        // routed copies start at once; the weights later, off that path
-        if (!tagged) {
-            if (tid == 0 && !wait_flag(p.ctr + C_ROUTER, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
-            __syncthreads();
-        }
-        TRACE(5);
-        if (E > 256) {
-            bool ok = true;
-            for (int e = tid; e < E; e += kFusedThreads) s_scores[e] = wait_word_gpu(scores + e, tag, kWaitPolls, ok);
-            if (!ok) set_error(p.ctr, ST_TIMEOUT);
-            __syncthreads();
-        }
-        uint32_t sel_k = 0;
-        int sel_id = 0;
+        // ---- warp 0: the routing (every CTA, identically) and the routed
+        // copies; warps 1..: the shared expert's gate/up rows meanwhile
         if (warp == 0) {
-            if (E <= 256) {
+            uint32_t sel_k = 0;
+            int sel_id = 0;
+            {
                 uint32_t kk[8];
                 int kid[8];
-                if (!load_score_words(scores, E, tag, kWaitPolls,
+                if (!load_score_words(scores, E, S, tag, kWaitPolls,
                                       reinterpret_cast<uint32_t*>(s_scores), kk, kid) &&
                     lane == 0)
                     set_error(p.ctr, ST_TIMEOUT);
-                topk_select_warp(kk, kid, K, sel_k, sel_id, trace);
+                topk_select_compact(kk, kid, K, sel_k, sel_id);
                 if (lane < K) s_ids[lane] = sel_id;
-            } else {
-                topk_softmax_warp(s_scores, s_taken, E, K, s_ids, s_w);
             }
             __syncwarp();
+            TRACE(4);
             // the selections this GPU holds, in top-k order
             const int e = lane < K ? s_ids[lane] : -1;
             const bool held = lane < K && e >= ebeg && e < ebeg + ecnt;
             const uint32_t hb = __ballot_sync(0xffffffffu, held);
             if (held) s_act[__popc(hb & ((1u << lane) - 1u))] = lane;
-            if (lane == 0) *s_nact = __popc(hb);
-        }
-        __syncthreads();
-        TRACE(6);
-        const int A = *s_nact;
-        const int f0 = part(A * I, c, G), f1 = part(A * I, c + 1, G);
-
-        // ---- phase-1 copies: routed gate/up rows of [f0, f1) in chunks of CR
-        // rows (one mbarrier each, issued in order so compute can start on the
-        // first chunk), then the routed down rows
-        const int nrows = f1 - f0;
-        const int CR = p.chunk_rows;
-        const int nchunks = (nrows + CR - 1) / CR;
-        // issued by the lanes of warp 0 in parallel: lane q < nchunks chunk q;
-        // the down rows (lane 16 + a: slot a) once the last gate/up chunk has
-        // landed, so they do not compete with the gate/up bytes, which are
-        // needed first
-        auto issue_down = [&]() {
-            if (lane == 16) mbar_arrive_expect_tx(&bars[2], (uint32_t)(A * nh * rb_down));
-            if (lane >= 16 && lane - 16 < A && nh > 0) {
-                const int a = lane - 16;
-                const int64_t e = s_ids[s_act[a]] - ebeg;
-                bulk_g2s(sm + p.o_rdown + (int64_t)a * p.max_out_rows * rb_down,
-                         Ls->down + e * st_down + h0 * rb_down, (uint32_t)(nh * rb_down), &bars[2]);
-            }
-        };
-        if (warp == 0) {
-            const uint8_t* gate = Ls->gate;
-            const uint8_t* up = Ls->up;
+            const int A = __popc(hb);
+            if (lane == 0) *s_nact = A;
+            __syncwarp();
+            // routed gate/up rows of [f0, f1) in chunks of CR rows (one
+            // mbarrier each, in order, so compute starts on the first), lane
+            // q issuing chunk q; the routed down rows (lane 16 + a: slot a)
+            // at the same time
+            const int f0 = part(A * I, c, G), f1 = part(A * I, c + 1, G);
+            const int nrows = f1 - f0, CR = p.chunk_rows;
+            const int nchunks = (nrows + CR - 1) / CR;
             if (lane < nchunks) {
                 const int q = lane, q0 = q * CR, q1 = min(nrows, q0 + CR);
                 mbar_arrive_expect_tx(&bars[3 + q], (uint32_t)((q1 - q0) * (rb_gate + rb_up)));
                 for (int f = f0 + q0; f < f0 + q1;) {
                     const int a = f / I, r = f % I;
                     const int n = min(f0 + q1 - f, I - r);
-                    const int64_t e = s_ids[s_act[a]] - ebeg;
-                    bulk_g2s(sm + p.o_rgate + (int64_t)(f - f0) * rb_gate, gate + e * st_gate + r * rb_gate,
+                    const int64_t ex = s_ids[s_act[a]] - ebeg;
+                    bulk_g2s(sm + p.o_rgate + (int64_t)(f - f0) * rb_gate, Ls->gate + ex * st_gate + r * rb_gate,
                              (uint32_t)(n * rb_gate), &bars[3 + q]);
-                    bulk_g2s(sm + p.o_rup + (int64_t)(f - f0) * rb_up, up + e * st_up + r * rb_up,
+                    bulk_g2s(sm + p.o_rup + (int64_t)(f - f0) * rb_up, Ls->up + ex * st_up + r * rb_up,
                              (uint32_t)(n * rb_up), &bars[3 + q]);
                     f += n;
                 }
             }
+            if (lane == 16) mbar_arrive_expect_tx(&bars[2], (uint32_t)(A * nh * rb_down));
+            __syncwarp();
+            if (lane >= 16 && lane - 16 < A && nh > 0) {
+                const int a = lane - 16;
+                const int64_t ex = s_ids[s_act[a]] - ebeg;
+                bulk_g2s(sm + p.o_rdown + (int64_t)a * p.max_out_rows * rb_down,
+                         Ls->down + ex * st_down + h0 * rb_down, (uint32_t)(nh * rb_down), &bars[2]);
+            }
             // routing weights (float64 softmax over the selections), needed
             // only by the combine
-            if (E <= 256) topk_weights_warp(sel_k, sel_id, K, s_ids, s_w);
+            topk_weights_f32(sel_k, sel_id, K, s_ids, s_w);
             if (c == 0 && lane < K) {
                 if (ids_out) ids_out[lane] = s_ids[lane];
                 if (w_out) w_out[lane] = s_w[lane];
             }
-            TRACE(15);
-        }
-
-        // ---- shared expert gate/up (x is the token), while the routed rows
-        // are in flight; rows go to the last warps first (warp 0 issues the
-        // copies).  Its counter is released with the gate/up one.
-        if (Is) {
+        } else if (Is) {
+            // shared expert gate/up (x is the token): warps 1.. while warp 0
+            // routes; the activations go out as exchange words
             if (!mbar_wait(&bars[1], (ph >> 1) & 1u, kWaitPolls) && lane == 0) set_error(p.ctr, ST_TIMEOUT);
-            ph ^= 2u;
             const int rpw = 32 / lpr_h;
-            for (int rb = (nw - 1 - warp) * rpw; rb < s1 - s0; rb += nw * rpw) {
+#pragma unroll 1
+            for (int rb = (warp - 1) * rpw; rb < s1 - s0; rb += (nw - 1) * rpw) {
                 const int rr = rb + sub_h;
                 const bool ok = rr < s1 - s0;
                 const int rs = ok ? rr : 0;
-                float g = qdot_t<SGU>(L0.shared_gate_type, sm + p.o_sgate + rs * rb_sg, pr_h >> 2, pr_h & 3, xl);
-                float u = qdot_t<SGU>(L0.shared_up_type, sm + p.o_sup + rs * rb_su, pr_h >> 2, pr_h & 3, xl);
-                g = group_sum(g, lpr_h);
-                u = group_sum(u, lpr_h);
+                const float2 gu = qdot2_rows<SGU>(L0.shared_gate_type, sm + p.o_sgate + rs * rb_sg,
+                                                  L0.shared_up_type, sm + p.o_sup + rs * rb_su,
+                                                  sm + p.o_xq, H, pr_h >> 2, pr_h & 3);
+                const float g = group_sum(gu.x, lpr_h), u = group_sum(gu.y, lpr_h);
                 if (ok && pr_h == 0) st_word_gpu(act_s + s0 + rr, (g * shared_sigmoid(g)) * u, tag);
             }
         }
-        TRACE(4);
+        if (Is) ph ^= 2u;
+        __syncthreads();
+        // shared gate/up rows are consumed: the next step's go out now
+        if (tid == 0 && Ln && Is) issue_sgu(Ln);
+        TRACE(5);
+        const int A = *s_nact;
+        const int f0 = part(A * I, c, G), f1 = part(A * I, c + 1, G);
+        const int nrows = f1 - f0;
+        const int CR = p.chunk_rows;
+        const int nchunks = (nrows + CR - 1) / CR;
 
-        // ---- routed gate/up, chunk by chunk
+        // ---- routed gate/up, chunk by chunk (one decoder call site for the
+        // gate and the up row: the loops stay rolled so that the step's code
+        // stays small in the instruction cache)
         {
             const int rpw = 32 / lpr_h;
             int waited = -1;
+#pragma unroll 1
             for (int rb = warp * rpw; rb < nrows; rb += nw * rpw) {
                 const int qlast = min(rb + rpw - 1, nrows - 1) / CR;
                 while (waited < qlast) {
                     ++waited;
                     if (!mbar_wait(&bars[3 + waited], (ph >> (3 + waited)) & 1u, kWaitPolls) && lane == 0)
                         set_error(p.ctr, ST_TIMEOUT);
-                    if (waited < 2) TRACE(16 + waited);
-                    if (warp == 0 && waited == nchunks - 1) issue_down();
+                    if (waited == 0) TRACE(6);
                 }
                 const int rr = rb + sub_h;
                 const bool ok = rr < nrows;
                 const int rs = ok ? rr : 0;
-                float g = qdot_t<GU>(L0.gate_type, sm + p.o_rgate + rs * rb_gate, pr_h >> 2, pr_h & 3, xl);
-                float u = qdot_t<GU>(L0.up_type, sm + p.o_rup + rs * rb_up, pr_h >> 2, pr_h & 3, xl);
-                g = group_sum(g, lpr_h);
-                u = group_sum(u, lpr_h);
+                const float2 gu = qdot2_rows<GU>(L0.gate_type, sm + p.o_rgate + rs * rb_gate, L0.up_type,
+                                                 sm + p.o_rup + rs * rb_up, sm + p.o_xq, H, pr_h >> 2,
+                                                 pr_h & 3);
+                const float g = group_sum(gu.x, lpr_h), u = group_sum(gu.y, lpr_h);
                 if (ok && pr_h == 0) {
                     const float sgm = 1.0f / (1.0f + expf(-g));
                     st_word_gpu(act_r + f0 + rr, (g * sgm) * u, tag);
                 }
-                if (rb == 0) TRACE(18);
             }
             // every chunk barrier must have completed before the CTA moves on
             // (its copies write shared memory)
-            for (int q = waited + 1; q < nchunks; ++q) {
+            for (int q = waited + 1; q < nchunks; ++q)
                 if (!mbar_wait(&bars[3 + q], (ph >> (3 + q)) & 1u, kWaitPolls) && lane == 0)
                     set_error(p.ctr, ST_TIMEOUT);
-                if (warp == 0 && q == nchunks - 1) issue_down();
-            }
-            if (warp == 0 && nchunks == 0) issue_down();
             ph ^= ((1u << nchunks) - 1u) << 3;
         }
         TRACE(7);
-        __syncthreads();
-        TRACE(8);
-        if (tid == 0 && !tagged) {
-            if (Is) red_release_add(p.ctr + C_SHARED, 1);
-            red_release_add(p.ctr + C_GATEUP, 1);
-            if (Is && !wait_flag(p.ctr + C_SHARED, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
-            if (!wait_flag(p.ctr + C_GATEUP, gen, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
-        }
-        __syncthreads();
-        TRACE(9);
 
-        // ---- activations, vector by vector: warp w gathers vector v = w
-        // (+16, ...) -- routed slot v < A (I values) or the shared vector
-        // v == A (Is values and the shared gate) -- from the exchange words,
-        // quantises it and marks it ready (s_ready[v] = tag).  A down item
-        // starts as soon as its vector is ready, so the exchange of the late
-        // vectors overlaps the down rows of the early ones; the shared
-        // vector, whose rows were done first, leads.
+        // ---- activations: every thread polls its share of the A*I routed
+        // and Is shared exchange words (up to kGatherWords loads in flight),
+        // then warp v quantises vector v (routed slots v < A, the shared one
+        // v == A)
         float* act32 = reinterpret_cast<float*>(sm + p.o_act);
         const uint32_t qb = qvec_bytes(Imax);
         const int nvec = A + (Is ? 1 : 0);
-        for (int v = warp; v < nvec; v += nw) {
-            const int n = v < A ? I : Is;
-            const uint64_t* src = v < A ? act_r + (size_t)v * I : act_s;
-            float* dst = act32 + v * Imax;
+        {
+            const int nr_words = A * I, n_words = nr_words + Is;
             bool ok = true;
-            for (int j0 = 2 * lane; j0 < n; j0 += 2 * 32 * kGatherPairs) {
+#pragma unroll 1
+            for (int j0 = tid; j0 < n_words; j0 += kFusedThreads * kGatherWords) {
                 uint32_t pend = 0;
+                const uint64_t* srcw[kGatherWords];
+                int dofs[kGatherWords];  // routed word j -> act32[(j / I) * Imax + j % I]
 #pragma unroll
-                for (int q = 0; q < kGatherPairs; ++q)
-                    if (j0 + 64 * q < n) pend |= 1u << q;
+                for (int q = 0; q < kGatherWords; ++q) {
+                    const int j = j0 + kFusedThreads * q;
+                    if (j < n_words) pend |= 1u << q;
+                    const int v = j < nr_words ? j / I : A;
+                    srcw[q] = j < nr_words ? act_r + j : act_s + (j - nr_words);
+                    dofs[q] = v * Imax + (j < nr_words ? j - v * I : j - nr_words);
+                }
                 for (uint32_t round = 0; pend != 0u; ++round) {
                     if (round == kWaitPolls) {
                         ok = false;
                         break;
                     }
-                    ulonglong2 wv[kGatherPairs];
+                    uint64_t wv[kGatherWords];
 #pragma unroll
-                    for (int q = 0; q < kGatherPairs; ++q)
-                        wv[q] = ((pend >> q) & 1u) ? ld_word2_gpu(src + j0 + 64 * q) : make_ulonglong2(0ull, 0ull);
+                    for (int q = 0; q < kGatherWords; ++q) wv[q] = ((pend >> q) & 1u) ? ld_word_gpu(srcw[q]) : 0ull;
 #pragma unroll
-                    for (int q = 0; q < kGatherPairs; ++q) {
-                        if (((pend >> q) & 1u) && (uint32_t)(wv[q].x >> 32) == tag &&
-                            (uint32_t)(wv[q].y >> 32) == tag) {
+                    for (int q = 0; q < kGatherWords; ++q) {
+                        if (((pend >> q) & 1u) && (uint32_t)(wv[q] >> 32) == tag) {
                             pend &= ~(1u << q);
-                            *reinterpret_cast<float2*>(dst + j0 + 64 * q) =
-                                make_float2(__uint_as_float((uint32_t)wv[q].x), __uint_as_float((uint32_t)wv[q].y));
+                            act32[dofs[q]] = __uint_as_float((uint32_t)wv[q]);
                         }
                     }
                 }
-                if (!ok) break;
             }
-            if (v == A && lane == 0) *s_sg = wait_word_gpu(sgp, tag, kWaitPolls, ok);
-            if (!__all_sync(0xffffffffu, ok) && lane == 0) set_error(p.ctr, ST_TIMEOUT);
-            __syncwarp();
-            if (v == 0) TRACE(19);
-            for (int b = 0; b < n / 256; ++b) quantize_block_warp(dst, qvec_at(sm + p.o_aq + v * qb, n), b);
-            __syncwarp();
-            __threadfence_block();
-            if (lane == 0) s_ready[v] = tag;
-            if (v == 0) TRACE(20);
+            if (!ok) set_error(p.ctr, ST_TIMEOUT);
         }
-        // the down rows of this CTA (every warp checks the copy)
-        if (!mbar_wait(&bars[2], (ph >> 2) & 1u, kWaitPolls) && lane == 0) set_error(p.ctr, ST_TIMEOUT);
+        __syncthreads();
+        TRACE(8);
+        for (int v = warp; v < nvec; v += nw) {
+            const int n = v < A ? I : Is;
+#pragma unroll 1
+            for (int b = 0; b < n / 256; ++b) quantize_block_ool(act32 + v * Imax, sm + p.o_aq + v * qb, n, b);
+        }
+        __syncthreads();
+        TRACE(9);
+        // the routed and shared down rows of this CTA
+        if (tid == 0 && !mbar_wait(&bars[2], (ph >> 2) & 1u, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
         ph ^= 4u;
+        if (Is) {
+            if (tid == 0 && !mbar_wait(&bars[kSdBar], (ph >> kSdBar) & 1u, kWaitPolls)) set_error(p.ctr, ST_TIMEOUT);
+            ph ^= 1u << kSdBar;
+        }
+        __syncthreads();
         TRACE(10);
 
-        // ---- down rows [h0, h1) of every vector: item = (routed vector, pair
-        // of row groups), the activation codes loaded once per item; the
-        // shared vector's row groups come first, one per item
+        // ---- down rows [h0, h1) of every vector: item = (vector, pair of
+        // row groups), the activation codes loaded once per item; the shared
+        // vector's row groups first, one per item
         {
             const int rpw_i = 32 / p.lpr_i, rpw_s = 32 / p.lpr_is;
             const int ng_i = (nh + rpw_i - 1) / rpw_i, ng_s = Is ? (nh + rpw_s - 1) / rpw_s : 0;
             const int np_i = (ng_i + 1) / 2, np_s = ng_s;
+#pragma unroll 1
             for (int it = warp; it < A * np_i + np_s; it += nw) {
                 const bool sh = it < np_s;
                 const int v = sh ? A : (it - np_s) / np_i;
@@ -516,73 +543,60 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                 const int64_t rb = sh ? rb_sd : rb_down;
                 const uint8_t* rows = sh ? sm + p.o_sdown : sm + p.o_rdown + (int64_t)v * p.max_out_rows * rb_down;
                 const int n = sh ? Is : I;
-                {
-                    uint32_t i = 0;
-                    while (s_ready[v] != tag && ++i < kWaitPolls) {
-                    }
-                    if (i == kWaitPolls && lane == 0) set_error(p.ctr, ST_TIMEOUT);
-                    __syncwarp();
-                    __threadfence_block();
-                }
-                XLane xa;
-                load_xlane(xa, qvec_at(sm + p.o_aq + v * qb, n), pr >> 2, pr & 3);
-#pragma unroll
-                for (int gg = 0; gg < 2; ++gg) {
-                    const int gi = sh ? (gg == 0 ? gp : ng) : 2 * gp + gg;
-                    if (gi < ng) {
-                        const int rr = gi * rpw + sub;
-                        const bool ok = rr < nh;
-                        const uint8_t* rowp = rows + (ok ? rr : 0) * rb;
-                        float d = sh ? qdot_t<SDN>(type, rowp, pr >> 2, pr & 3, xa)
-                                     : qdot_t<DN>(type, rowp, pr >> 2, pr & 3, xa);
-                        d = group_sum(d, lpr);
-                        if (ok && pr == 0) s_vout[v * p.max_out_rows + rr] = d;
+                uint8_t* codes = sm + p.o_aq + v * qb;
+                if (sh) {
+                    const int rr = gp * rpw + sub;
+                    const bool ok = rr < nh;
+                    float d = qdot1_row<SDN>(type, rows + (ok ? rr : 0) * rb, codes, n, pr >> 2, pr & 3);
+                    d = group_sum(d, lpr);
+                    if (ok && pr == 0) s_vout[v * p.max_out_rows + rr] = d;
+                } else {
+                    const int ra = 2 * gp * rpw + sub, rb2 = ra + rpw;
+                    const bool oka = ra < nh, okb = rb2 < nh;
+                    const float2 d = qdot2_rows<DN>(type, rows + (oka ? ra : 0) * rb, type,
+                                                    rows + (okb ? rb2 : 0) * rb, codes, n, pr >> 2, pr & 3);
+                    const float da = group_sum(d.x, lpr), db = group_sum(d.y, lpr);
+                    if (pr == 0) {
+                        if (oka) s_vout[v * p.max_out_rows + ra] = da;
+                        if (okb) s_vout[v * p.max_out_rows + rb2] = db;
                     }
                 }
-                if (it == 0) TRACE(21);
-                if (it == nw) TRACE(22);
             }
         }
         __syncthreads();
+        // shared down rows are consumed: the next step's go out now
+        if (tid == 0 && Ln && Is) issue_sdown(Ln);
         TRACE(11);
         // ---- weighted sum in top-k order, + shared (moe_layer.py:85-86, 102-105);
         // block steps add the residual h to the binary16-rounded MoE output
-        // (transformer.py:192-204, 229-247)
-        for (int rr = tid; rr < nh; rr += kFusedThreads) {
-            float comb = 0.f;
-            int a = 0;
-            for (int k = 0; k < K; ++k) {
-                if (a < A && s_act[a] == k) {
-                    comb = __fadd_rn(comb, __fmul_rn(s_w[k], s_vout[a * p.max_out_rows + rr]));
-                    ++a;
+        // (transformer.py:192-204, 229-247).  A chained next step reads the
+        // rows as exchange words.
+        {
+            uint64_t* ywn = p.yw + (size_t)buf * H;
+            for (int rr = tid; rr < nh; rr += kFusedThreads) {
+                float comb = 0.f;
+                int a = 0;
+                for (int k = 0; k < K; ++k) {
+                    if (a < A && s_act[a] == k) {
+                        comb = __fadd_rn(comb, __fmul_rn(s_w[k], s_vout[a * p.max_out_rows + rr]));
+                        ++a;
+                    }
                 }
+                if (Is) comb = __fadd_rn(comb, __fmul_rn(*s_sg, s_vout[A * p.max_out_rows + rr]));
+                if (block) comb = __fadd_rn(h32[h0 + rr], round16(comb));
+                if (next_chains) st_word_gpu(ywn + h0 + rr, comb, tag);
+                if (yout) yout[h0 + rr] = comb;
             }
-            if (Is) comb = __fadd_rn(comb, __fmul_rn(*s_sg, s_vout[A * p.max_out_rows + rr]));
-            if (block) comb = __fadd_rn(h32[h0 + rr], round16(comb));
-            yout[h0 + rr] = comb;
         }
         __syncthreads();
         TRACE(12);
 #undef TRACE
-        if (tid == 0) {
-            red_release_add(p.ctr + C_DONE, 1);
-            // the router and shared-expert regions are free: the next step's
-            // rows load while this CTA waits for the others
-            if (s + 1 < p.n_steps) {
-                issue_phase0(step_layer(s + 1));
-                if (x_by_copy(s + 1)) issue_x(s + 1);
-            }
-        }
     }
-    // ---- exit: the last CTA resets the counters for the next launch
+    // ---- exit: the last CTA advances the sequence word for the next launch
     if (tid == 0) {
         __threadfence();
         const uint32_t t = atomicAdd(p.ctr + C_EXIT, 1u);
         if (t == (uint32_t)G - 1) {
-            p.ctr[C_ROUTER] = 0;
-            p.ctr[C_SHARED] = 0;
-            p.ctr[C_GATEUP] = 0;
-            p.ctr[C_DONE] = 0;
             p.ctr[C_EXIT] = 0;
             p.ctr[C_SEQ] = seq0 + (uint32_t)p.n_steps;
             if (p.err_out) {
@@ -603,6 +617,8 @@ static int lanes_per_row(int cols) {
     return pairs;  // 4, 8, 16 or 32 (checked by fused_plan)
 }
 
+static bool fused_plan(const moe_b200_layer* L, bool shared, int G, FusedParams& p);
+
 bool fused_supported(const moe_b200_layer* L, int T, int flags) {
     if (T != 1 || (flags & (MOE_B200_EXACT | MOE_B200_FP16_GRAPH | MOE_B200_SHARED_ONLY))) return false;
     auto ok_cols = [](int cols) {
@@ -621,15 +637,17 @@ bool fused_supported(const moe_b200_layer* L, int T, int flags) {
     if (shared && (!rb16(L->shared_gate_type, L->hidden) || !rb16(L->shared_up_type, L->hidden) ||
                    !rb16(L->shared_down_type, L->shared_intermediate)))
         return false;
-    return true;
+    FusedParams p;
+    return fused_plan(L, shared, sm_count(), p);
 }
 
 size_t fused_workspace_bytes(const moe_b200_layer* L) {
     const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate : L->intermediate;
-    // counters, then two buffers (step parity) of scores, routed and shared
-    // activations and the shared gate
-    return 256 + align_up((size_t)2 * L->n_experts * 8) +
-           align_up((size_t)2 * L->top_k * L->intermediate * 8) + align_up((size_t)2 * Imax * 8) + 256;
+    const int S = L->n_experts > sm_count() ? L->n_experts : sm_count();
+    // counters, then two buffers (step parity) of score slots, routed and
+    // shared activations and the layer output words
+    return 256 + align_up((size_t)2 * S * 8) + align_up((size_t)2 * L->top_k * L->intermediate * 8) +
+           align_up((size_t)2 * Imax * 8) + align_up((size_t)2 * L->hidden * 8);
 }
 
 static bool fused_plan(const moe_b200_layer* L, bool shared, int G, FusedParams& p) {
@@ -637,8 +655,9 @@ static bool fused_plan(const moe_b200_layer* L, bool shared, int G, FusedParams&
     const int Is = shared ? L->shared_intermediate : 0;
     const int Imax = Is > I ? Is : I;
     p.G = G;
+    p.S = E > G ? E : G;
     p.with_shared = shared ? 1 : 0;
-    p.max_router_rows = (E + G - 1) / G;
+    p.max_router_rows = (p.S + G - 1) / G;
     p.max_sgu_rows = Is ? (Is + G - 1) / G : 0;
     p.max_out_rows = (H + G - 1) / G;
     p.max_rgu_rows = (K * I + G - 1) / G;
@@ -657,6 +676,7 @@ static bool fused_plan(const moe_b200_layer* L, bool shared, int G, FusedParams&
     p.o_h32 = take((uint64_t)H * 4);
     p.o_xq = take(qvec_bytes(H));
     p.o_router = take((uint64_t)p.max_router_rows * H * 4);
+    p.o_ginp = take(Is ? (uint64_t)H * 4 : 0);
     p.o_sgate = take(Is ? (uint64_t)p.max_sgu_rows * row_bytes(L->shared_gate_type, H) : 0);
     p.o_sup = take(Is ? (uint64_t)p.max_sgu_rows * row_bytes(L->shared_up_type, H) : 0);
     p.o_sdown = take(Is ? (uint64_t)p.max_out_rows * row_bytes(L->shared_down_type, Is) : 0);
@@ -665,9 +685,11 @@ static bool fused_plan(const moe_b200_layer* L, bool shared, int G, FusedParams&
     p.o_rdown = take((uint64_t)K * p.max_out_rows * row_bytes(L->down_type, I));
     p.o_act = take((uint64_t)(K + 1) * Imax * 4);
     p.o_aq = take((uint64_t)(K + 1) * qvec_bytes(Imax));
-    p.o_misc = take(512 + ((5 * E + 15) & ~15) + (uint64_t)(K + 1) * p.max_out_rows * 4 +
-                    4 * (kMaxTopK + 1));
+    p.o_misc = take(512 + ((5 * p.S + 15) & ~15) + (uint64_t)(K + 1) * p.max_out_rows * 4);
     p.total = o;
+    // one warp-level top-k over at most 256 score slots; the router rows of
+    // a CTA fit one pass of all warps but one
+    if (p.S > 256 || p.max_router_rows > kFusedThreads / 32 - 1) return false;
     return p.total <= 227 * 1024;
 }
 
@@ -746,12 +768,12 @@ static cudaError_t fused_prepare(const moe_b200_layer* L, int flags, const float
     const int Imax = L->shared_intermediate > L->intermediate ? L->shared_intermediate : L->intermediate;
     size_t off = 256;
     p.scores = reinterpret_cast<uint64_t*>(base + off);
-    off += align_up((size_t)2 * L->n_experts * 8);
+    off += align_up((size_t)2 * p.S * 8);
     p.act_r = reinterpret_cast<uint64_t*>(base + off);
     off += align_up((size_t)2 * L->top_k * L->intermediate * 8);
     p.act_s = reinterpret_cast<uint64_t*>(base + off);
     off += align_up((size_t)2 * Imax * 8);
-    p.sg = reinterpret_cast<uint64_t*>(base + off);
+    p.yw = reinterpret_cast<uint64_t*>(base + off);
     p.trace = (tl_trace && tl_trace_cap >= G) ? tl_trace : nullptr;
     *ok = true;
     return cudaSuccess;

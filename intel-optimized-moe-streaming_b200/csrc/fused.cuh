@@ -40,6 +40,14 @@ __device__ __forceinline__ float dot_f32_warp(const float* row, const float* x, 
     return warp_sum(acc);
 }
 
+// The same dot for a row with no alignment guarantee (scalar loads).
+__device__ __forceinline__ float dot_f32_warp_any(const float* row, const float* x, int n, int lane) {
+    if ((((uintptr_t)row) & 15u) == 0) return dot_f32_warp(row, x, n, lane);
+    float acc = 0.f;
+    for (int i = lane; i < n; i += 32) acc = fmaf(row[i], x[i], acc);
+    return warp_sum(acc);
+}
+
 // Sum of v over the CTA in a fixed order (warp trees, then warps in order);
 // every thread gets the result.  `part` holds 32 floats.
 __device__ __forceinline__ float block_sum(float v, float* part) {

@@ -111,6 +111,11 @@ __device__ __forceinline__ void quantize_block_warp(const float* v, QVec q, int 
     quantize_block_vals(vals, q, b);
 }
 
+// The same, out of line (one copy per kernel that needs a small step).
+static __device__ __noinline__ void quantize_block_ool(const float* v, uint8_t* codes, int n, int b) {
+    quantize_block_warp(v, qvec_at(codes, n), b);
+}
+
 // Block b of an fp32 vector in global memory written by other CTAs of this
 // launch (read through L2).
 __device__ __forceinline__ void quantize_block_gmem(const float* v, QVec q, int b) {
@@ -387,6 +392,29 @@ __device__ __forceinline__ float qdot_t(int rt, const uint8_t* row, int b, int o
         else if constexpr (T == Q6_K) return qdot_q6k(bp, o, x);
         else return qdot_q8_0(bp, o, x);
     }
+}
+
+// Out-of-line dots of one lane's pair (b, o) of one or two rows with the
+// activation codes at `codes` (a QVec of n values), the codes loaded
+// inside.  Each kernel that calls these holds one copy of each decoder, so
+// a step that runs every phase once stays small in the instruction cache
+// (an inlined decoder at every call site made the single-token decode
+// kernel's step ~200 KB of code, fetched again from L2 every step).
+template <int T>
+static __device__ __noinline__ float2 qdot2_rows(int rt0, const uint8_t* row0, int rt1,
+                                                 const uint8_t* row1, uint8_t* codes, int n,
+                                                 int b, int o) {
+    XLane x;
+    load_xlane(x, qvec_at(codes, n), b, o);
+    return make_float2(qdot_t<T>(rt0, row0, b, o, x), qdot_t<T>(rt1, row1, b, o, x));
+}
+
+template <int T>
+static __device__ __noinline__ float qdot1_row(int rt, const uint8_t* row, uint8_t* codes, int n,
+                                               int b, int o) {
+    XLane x;
+    load_xlane(x, qvec_at(codes, n), b, o);
+    return qdot_t<T>(rt, row, b, o, x);
 }
 
 // Sum over the `lpr` consecutive lanes of a row group (lpr a power of two).

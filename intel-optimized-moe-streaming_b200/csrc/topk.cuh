@@ -38,7 +38,7 @@ __device__ __forceinline__ double np_sum(const double* v, int n) {
 
 // scores: E floats in shared memory; taken: E bytes of shared scratch.
 // Writes ids[K] / w[K] (lane 0).  All 32 lanes must call.
-__device__ __forceinline__ void topk_softmax_warp(const float* scores, unsigned char* taken, int E,
+static __device__ __noinline__ void topk_softmax_warp(const float* scores, unsigned char* taken, int E,
                                                   int K, int* ids, float* w) {
     const int lane = threadIdx.x & 31;
     for (int e = lane; e < E; e += 32) taken[e] = 0;
@@ -188,6 +188,59 @@ __device__ __forceinline__ void topk_weights_warp(uint32_t my_k, int my_id, int 
     __syncwarp();
 }
 
+// Compact top-k of E <= 256 keys held 8 per lane (lane l: experts
+// 8l..8l+7, absent ones key 0 / id 0x7fffffff), for kernels whose whole
+// step must stay small in the instruction cache: K rounds of a warp
+// arg-max over (key, lower id first) composites, the winner cleared where
+// it sits.  Same selection, in the same order, as topk_select_warp.  Lane r
+// (r < K) ends with selection r: its key in my_k, its expert in my_id.
+__device__ __forceinline__ void topk_select_compact(const uint32_t (&k)[8], const int (&id)[8],
+                                                    int K, uint32_t& my_k, int& my_id) {
+    const int lane = threadIdx.x & 31;
+    uint64_t cmp[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cmp[i] = ((uint64_t)k[i] << 32) | (uint32_t)~(uint32_t)id[i];
+    my_k = 0;
+    my_id = 0;
+#pragma unroll 1
+    for (int r = 0; r < K; ++r) {
+        uint64_t b = cmp[0];
+#pragma unroll
+        for (int i = 1; i < 8; ++i) b = cmp[i] > b ? cmp[i] : b;
+        const uint32_t bh = (uint32_t)(b >> 32);
+        const uint32_t m = __reduce_max_sync(0xffffffffu, bh);
+        const uint32_t ml = __reduce_max_sync(0xffffffffu, bh == m ? (uint32_t)b : 0u);
+        const uint64_t win = ((uint64_t)m << 32) | ml;
+        if (lane == r) {
+            my_k = m;
+            my_id = (int)~ml;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cmp[i] = cmp[i] == win ? 0ull : cmp[i];
+    }
+}
+
+// Routing weights of the K selections lanes 0..K-1 hold, in fp32: the
+// softmax over those k only (router.py:158-168; the reference's float64
+// weights differ from these by about one fp32 ulp), uniform weights when
+// the sum is not finite or not positive.  Written to ids[lane] / w[lane].
+// All 32 lanes must call.
+__device__ __forceinline__ void topk_weights_f32(uint32_t my_k, int my_id, int K, int* ids, float* w) {
+    const int lane = threadIdx.x & 31;
+    const float v = lane < K ? fkey_inv(my_k) : 0.f;
+    const float mx = __shfl_sync(0xffffffffu, v, 0);  // selection 0 is the maximum
+    const float ex = lane < K ? expf(v - mx) : 0.f;
+    float tot = ex;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    if (lane < K) {
+        const bool uniform = !isfinite(tot) || tot <= 0.f;
+        ids[lane] = my_id;
+        w[lane] = uniform ? 1.0f / (float)K : ex / tot;
+    }
+    __syncwarp();
+}
+
 // Fast form of topk_softmax_warp for E <= 256 with the scores in global
 // memory written by other CTAs (read through L2).  Identical results to
 // topk_softmax_warp.
@@ -216,22 +269,23 @@ __device__ __forceinline__ void topk_softmax_warp_fast(const float* gscores, int
 
 // Lane l's keys for topk_select_warp (experts 8l..8l+7 of E <= 256) from
 // exchange words (st_word_gpu: the fp32 score and the step tag in one 64-bit
-// word), polled until every word carries `tag`.  The polling loads are
-// coalesced: lane l reads words l + 32 i, so a warp's load is 256 contiguous
-// bytes (8 sectors, not 32 at a 64-byte lane stride) -- every CTA of the
-// grid polls the same E words, and the sectors per round are what the L2
-// slices serve.  Only the words still missing are read again.  The keys are
-// staged in shared memory (`stage`, E uint32) and each lane then takes its
-// own experts from there.  At most `limit` rounds; false (the same in every
-// lane) when it gave up.
-__device__ __forceinline__ bool load_score_words(const uint64_t* words, int E, uint32_t tag,
-                                                           uint32_t limit, uint32_t* stage,
-                                                           uint32_t (&k)[8], int (&id)[8]) {
+// word), polled until every one of the first S >= E words carries `tag`
+// (words E..S-1 carry no score: they only show that their writer has reached
+// this step).  The polling loads are coalesced: lane l reads words l + 32 i,
+// so a warp's load is 256 contiguous bytes -- every CTA of the grid polls
+// the same words, and the sectors per round are what the L2 slices serve.
+// Only the words still missing are read again.  The keys are staged in
+// shared memory (`stage`, S uint32) and each lane then takes its own
+// experts from there.  At most `limit` rounds; false (the same in every
+// lane) when it gave up.  S <= 256.
+__device__ __forceinline__ bool load_score_words(const uint64_t* words, int E, int S, uint32_t tag,
+                                                 uint32_t limit, uint32_t* stage,
+                                                 uint32_t (&k)[8], int (&id)[8]) {
     const int lane = threadIdx.x & 31;
     uint32_t pend = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-        if (lane + 32 * i < E) pend |= 1u << i;
+        if (lane + 32 * i < S) pend |= 1u << i;
     bool ok = true;
     for (uint32_t round = 0; __any_sync(0xffffffffu, pend != 0u); ++round) {
         if (round == limit) {

@@ -11,7 +11,8 @@ distinct layers (the step-parity buffers are reused every other step), and
 a chain of transformer blocks, every step's output, routing ids and weights
 checked.  Tolerance: max|y - ref| / max|ref| <= 1e-3; ids equal except at
 a near tie (k-th and (k+1)-th scores within 1e-5 relative), where the
-oracle is re-run with the device's selection."""
+oracle is re-run with the device's selection; routing weights within 1e-5
+relative."""
 from __future__ import annotations
 
 import numpy as np
@@ -51,7 +52,10 @@ def _check_token(oracle, lw, x, y, ids, w):
         assert abs(s[k - 1] - s[k]) <= 1e-5 * max(abs(s[k - 1]), 1e-30), (ids, want_ids[0])
         sel = [(list(map(int, ids)), [float(v) for v in w])]
         want_y, _, want_w = oracle_layer(oracle, lw, x[None], selections=sel)
-    np.testing.assert_allclose(w, want_w[0], rtol=1e-6, atol=1e-7)
+    # the scores are fp32 dots in another summation order than numpy's BLAS;
+    # a routing weight's relative error is the absolute error of the score
+    # differences, a few 1e-6 at this layer's score magnitudes (~1)
+    np.testing.assert_allclose(w, want_w[0], rtol=1e-5, atol=1e-7)
     err = O.max_relative_error(y, want_y[0])
     assert err <= TOL, err
     return err
