@@ -649,6 +649,156 @@ def bench_stack(backend, base_layer: int, dev, peaks: dict, peak_kind: str) -> d
             "device_error": err}
 
 
+# ------------------------------------------------------- multi-GPU objects
+
+def _time_ranks(fn, n: int, warmup: int = 3) -> float:
+    """Device milliseconds per fn() call, CUDA events on each rank after a
+    barrier, the maximum over ranks."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / n], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _rel_err_ranks(got, want) -> float:
+    import torch
+    import torch.distributed as dist
+    e = ((got - want).abs().max() / want.abs().max().clamp_min(1e-30)).view(1)
+    dist.all_reduce(e, op=dist.ReduceOp.MAX)
+    return float(e.item())
+
+
+def bench_allreduce(backend, layers, dev, world: int, rank: int, steps: int, peaks: dict,
+                    peak_kind: str) -> dict:
+    """The batch-1 alternative to the all-to-all: the token is replicated on
+    every rank; each rank decodes it through the experts it holds (the fused
+    single-token kernel over its expert range, the shared expert on rank 0
+    only) and one 8 KB all-reduce sums the partial outputs.  `steps` steps
+    over the resident layer copies in one CUDA graph (the fused launch and the
+    NCCL all-reduce per step); device time max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from flash_moe_b200 import _lib, synth
+    lw = backend.store.layer(layers[0]).weights
+    H = lw.hidden
+    xs = torch.from_numpy(synth.make_tokens(2000, 64, H)).to(dev)  # same tokens on every rank
+    ys = torch.empty((steps, H), dtype=torch.float32, device=dev)
+    ids = torch.full((steps, lw.top_k), -1, dtype=torch.int32, device=dev)
+    flags = backend.flags | (_lib.NO_SHARED if rank else 0)
+
+    def step(i):
+        backend.forward_layer_device(layers[i % len(layers)], xs[i % 64].view(1, -1), ys[i:i + 1],
+                                     topk_ids=ids[i:i + 1], flags=flags)
+        dist.all_reduce(ys[i])
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize()
+    g, mode = None, "CUDA graph of the steps"
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                step(i)
+        run = g.replay
+    except RuntimeError:  # capture refused: the same steps as stream launches
+        g, mode = None, "stream launches"
+        torch.cuda.synchronize()
+        dist.barrier()
+
+        def run():
+            for i in range(steps):
+                step(i)
+    ms = _time_ranks(run, 3, warmup=2) / steps
+    # the last step against the exact fp32 engine, decomposed the same way
+    i = steps - 1
+    want = torch.empty((1, H), dtype=torch.float32, device=dev)
+    backend.forward_layer_device(layers[i % len(layers)], xs[i % 64].view(1, -1), want,
+                                 flags=_lib.EXACT | (_lib.NO_SHARED if rank else 0))
+    dist.all_reduce(want)
+    err = _rel_err_ranks(ys[i:i + 1], want)
+    del g
+    uniq = [len(np.unique(r)) for r in ids.cpu().numpy()]
+    byts = sum(uniq) * lw.expert_bytes + steps * (lw.shared_bytes + lw.router.nbytes + H * 4)
+    gbs = byts / steps / (ms / 1e3) / 1e9
+    return {"config": f"config 2, batch 1 replicated on {world} GPUs: each rank its {lw.n_experts // world} "
+                      "experts of the top-8 (fused single-token kernel), rank 0 the shared expert, "
+                      f"one NCCL all-reduce of 8 KB per layer; {mode}",
+            "us_per_token": round(ms * 1e3, 2), "gbs_union": round(gbs, 1),
+            "frac_of_one_gpu_hbm": round(gbs / peaks["hbm_gbs"], 4),
+            "peak_source": f"{peak_kind} hbm_gbs", "max_rel_err": float(f"{err:.3e}")}
+
+
+def bench_sequence_ep(backend, layer: int, dev, world: int, rank: int, tokens: int, name: str,
+                      peaks: dict, peak_kind: str, use_prefill: bool, bound: str = "tensor") -> dict:
+    """A many-token layer expert-parallel: the `tokens` tokens split evenly
+    over the ranks; per call an all-gather of the tokens (NCCL), the rank's
+    experts over all of them (tensor-core path, or the decode engine), a
+    reduce-scatter of the partial outputs, and the shared expert of the
+    rank's own tokens.  Device time max over ranks; the output against the
+    one-call exact fp32 reference on the same rank's tokens."""
+    import torch
+    from flash_moe_b200 import _lib, synth
+    from flash_moe_b200.ep import ep_exchange_step
+    lw = backend.store.layer(layer).weights
+    H = lw.hidden
+    per = tokens // world
+    x_all_host = synth.make_tokens(404 if use_prefill else 3000, tokens, H)
+    xo = torch.from_numpy(x_all_host[rank * per:(rank + 1) * per]).to(dev)
+    x_all = torch.empty((tokens, H), dtype=torch.float32, device=dev)
+    y_part = torch.empty_like(x_all)
+    y_r, y_s, y = (torch.empty((per, H), dtype=torch.float32, device=dev) for _ in range(3))
+    ids = torch.empty((tokens, lw.top_k), dtype=torch.int32, device=dev)
+    if use_prefill:
+        routed = lambda xa, yp: backend.prefill_device(layer, xa, yp, ids, flags=_lib.NO_SHARED)  # noqa: E731
+        shared = lambda xx, ys: backend.prefill_device(layer, xx, ys, flags=_lib.SHARED_ONLY)  # noqa: E731
+    else:
+        routed = lambda xa, yp: backend.forward_layer_device(layer, xa, yp, ids,  # noqa: E731
+                                                             flags=backend.flags | _lib.NO_SHARED)
+        shared = lambda xx, ys: backend.forward_layer_device(layer, xx, ys,  # noqa: E731
+                                                             flags=backend.flags | _lib.SHARED_ONLY)
+
+    def call():
+        ep_exchange_step(xo, routed, shared, x_all, y_part, y_r, y_s, y)
+    ms = _time_ranks(call, 5)
+    # reference: the exact engine through the same decomposition
+    want = torch.empty_like(y)
+    ep_exchange_step(
+        xo, lambda xa, yp: backend.forward_layer_device(layer, xa, yp, flags=_lib.EXACT | _lib.NO_SHARED),
+        lambda xx, ys: backend.forward_layer_device(layer, xx, ys, flags=_lib.EXACT | _lib.SHARED_ONLY),
+        x_all, y_part, y_r, y_s, want)
+    call()
+    err = _rel_err_ranks(y, want)
+    uniq = int(np.unique(ids.cpu().numpy()).size)
+    out = {"config": f"{name}: {tokens} tokens split over {world} GPUs ({per} per rank), "
+                     f"{lw.n_experts // world} experts per rank; all-gather, "
+                     f"{'tensor-core prefill path' if use_prefill else 'decode engine'} on the "
+                     "held experts, reduce-scatter, own shared expert",
+           "us_per_step": round(ms * 1e3, 1), "tokens_per_s": round(tokens / (ms / 1e3)),
+           "unique_experts_touched": uniq, "max_rel_err_vs_exact": float(f"{err:.3e}")}
+    if bound == "tensor":
+        tf = PREFILL_FLOPS_PER_TOKEN * tokens / (ms / 1e3) / 1e12
+        out["tflops"] = round(tf, 1)
+        out["frac_of_world_tensor_peak"] = round(tf / (peaks.get("bf16_tflops", 1590.0) * world), 4)
+    else:
+        algo = uniq * lw.expert_bytes + lw.shared_bytes + lw.router.nbytes + tokens * 2 * H * 4
+        gbs = algo / (ms / 1e3) / 1e9
+        out["gbs_union"] = round(gbs, 1)
+        out["frac_of_world_hbm"] = round(gbs / (peaks["hbm_gbs"] * world), 4)
+    out["peak_source"] = f"{peak_kind} peaks x {world} GPUs"
+    return out
+
+
 def run_prefill_only(args) -> None:
     """The config-4 prefill measurement alone (one GPU), for profiling."""
     import torch
@@ -853,7 +1003,11 @@ def run_gpu(args) -> None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
         dist.all_reduce(bytes_t, op=dist.ReduceOp.SUM)
     ms_max = float(ms_t.item())
-    total_bytes = float(bytes_t.item())
+    rank_sum_bytes = float(bytes_t.item())
+    # the job's bytes: the distinct experts all ranks' tokens select per step,
+    # router and shared expert once (the replicated copies each rank reads
+    # are not counted again)
+    total_bytes = float(runner.union_bytes(args.steps))
     per_step_ms = ms_max / args.steps
     gbs = total_bytes / (ms_max / 1e3) / 1e9
 
@@ -880,6 +1034,18 @@ def run_gpu(args) -> None:
     graph = None
     tables = None
     extra = {}
+    if world > 1 and not args.no_extra:
+        # every rank takes part; rank 0 prints
+        extra["allreduce"] = bench_allreduce(backend, list(range(args.copies)), dev, world, rank,
+                                             min(args.steps, 64), peaks, peak_kind)
+        extra["prefill"] = bench_sequence_ep(backend, 0, dev, world, rank, 4096,
+                                             "config 4 prefill", peaks, peak_kind, True)
+        lwz = synth.make_layer(seed=0, zipf_s=1.1)
+        arena.add_layer(5000, lwz, expert_begin=begin, expert_count=per)
+        extra["batched_decode"] = bench_sequence_ep(backend, 5000, dev, world, rank, 64,
+                                                    "config 3 batched decode (Zipf 1.1)", peaks,
+                                                    peak_kind, True, bound="hbm")
+        arena.drop_layer(5000)
     if rank == 0 and world == 1 and not args.no_extra:
         cpu_on = not args.no_cpu
         extra["expert"] = bench_expert(dev, peaks, peak_kind, args.cpu_seconds if cpu_on else None)
@@ -900,7 +1066,10 @@ def run_gpu(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 6),
             "us_per_token": round(per_step_ms * 1e3 / 1, 3),
             "hbm_frac_of_8tbs": round(gbs / (8000.0 * world), 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "s16 x packed GGUF codes (activations quantised to 16-bit fixed point per "
+                     "256-value block as two int8 planes, dp4a int32 sums; fp32 router, block "
+                     "scales, SwiGLU and combine)",
             "data": "synthetic (seeded, config-2 shapes and distributions)",
             "config": {"workload": "config 2: one MoE layer decode, 1 token/step/GPU, 256 experts "
                                    "top-8, Q3_K/Q3_K/Q4_K experts + Q8_0 shared expert",
@@ -909,7 +1078,11 @@ def run_gpu(args) -> None:
                              f"({args.copies * step_bytes(8) / 1e6:.0f} MB touched per rotation > 2x L2)",
                        "parallelism": f"ep{world}" if world > 1 else "single",
                        "engine": args.engine, "launch": launch_mode,
-                       "algorithmic_bytes_per_token": step_bytes(8)},
+                       "algorithmic_bytes_per_token": step_bytes(8),
+                       "bytes_counted": "union per step: distinct experts of all ranks' tokens + "
+                                        "router + shared expert + gate vector once",
+                       "union_bytes_per_step": round(total_bytes / args.steps),
+                       "rank_sum_bytes_per_step": round(rank_sum_bytes / args.steps)},
             "roofline": roof,
             "e2e": e2e,
             "gpu_launches": launches,

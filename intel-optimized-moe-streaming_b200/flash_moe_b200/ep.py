@@ -235,6 +235,20 @@ class DecodeRunner:
 
     # ------------------------------------------------------------ accounting
 
+    def union_bytes(self, steps: int) -> int:
+        """Bytes the job's steps must read on any number of GPUs: per step
+        the distinct experts all ranks' tokens select, and the router, the
+        shared expert and the gate vector once (what one device decoding the
+        same tokens reads).  The same on every rank (the routing of every
+        gathered token is recorded)."""
+        lw = self.lw
+        ids = self.ids[:min(steps, self.max_steps)].cpu().numpy()
+        total = 0
+        for step_ids in ids:
+            total += len(np.unique(step_ids[step_ids >= 0])) * lw.expert_bytes
+        total += steps * (lw.shared_bytes + lw.router.nbytes + lw.hidden * 4)
+        return int(total)
+
     def algorithmic_bytes(self, steps: int) -> int:
         """Packed weight + router + gate-vector bytes this rank's steps must
         read: the distinct held experts each step's tokens select, the
