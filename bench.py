@@ -449,6 +449,34 @@ def bench_expert(dev, peaks: dict, peak_kind: str, cpu_seconds: float | None) ->
     return obj
 
 
+def bench_fp16_graph(backend, layer: int, dev) -> dict:
+    """The reference product's stock mode, fp16_graph=1 (binary16 rounding of
+    x, the weights, the gate/up products and the SwiGLU activation,
+    cpp/moe_quant_dot.cpp:36,160,192-209; src/flash_moe/native_expert.py:33-34):
+    the fused engines compute in fp32 activations, so a layer call with
+    FP16_GRAPH runs the exact route-plus-expert engine.  Its cost at 1 and 64
+    tokens on the config-2 layer, beside the fused engines' fp32-mode time."""
+    import torch
+    from flash_moe_b200 import _lib, synth
+    lw = backend.store.layer(layer).weights
+    out = {}
+    for T in (1, 64):
+        x = torch.from_numpy(synth.make_tokens(5100, T, lw.hidden)).to(dev)
+        y = torch.empty_like(x)
+        ms16 = _time_calls(lambda: backend.forward_layer_device(
+            layer, x, y, flags=backend.flags | _lib.FP16_GRAPH), 10)
+        ms32 = _time_calls(lambda: backend.forward_layer_device(layer, x, y), 10)
+        out[f"tokens_{T}"] = {"us_fp16_graph_exact_engine": round(ms16 * 1e3, 1),
+                              "us_default_call": round(ms32 * 1e3, 1),
+                              "kernels_default": backend.kernels_per_call(layer, T),
+                              "kernels_fp16_graph": backend.kernels_per_call(
+                                  layer, T, backend.flags | _lib.FP16_GRAPH)}
+    out["config"] = ("config-2 layer, moe_b200_decode with MOE_B200_FP16_GRAPH (the exact engine) "
+                     "against the default call (1 token: the fused kernel, 1 launch; 64 tokens: "
+                     "the fp32 exact engine), one call per step")
+    return out
+
+
 def bench_prefill(backend, layer: int, dev, peaks: dict, peak_kind: str) -> dict:
     """Config 4: 4096 bf16 tokens through the config-2 layer on the tensor
     cores (moe_b200_prefill).  The packed weights (382 MB) exceed L2, so each
@@ -799,8 +827,89 @@ def bench_sequence_ep(backend, layer: int, dev, world: int, rank: int, tokens: i
     return out
 
 
+def run_e2e_breakdown(args) -> None:
+    """Where the time of one synchronous host-buffer decode call goes (config
+    2, one token, one GPU): host wall-clock per call, mean over many calls,
+    of (a) a ctypes call of a trivial export (the binding's fixed cost),
+    (b) the public host-buffer call (moe_b200_decode_host: pinned staging,
+    one graph launch, completion wait, copy out), (c) a device-buffer call
+    followed by a stream synchronisation, and the device time of (d) one
+    single-step launch (CUDA events, back to back)."""
+    import torch
+    from flash_moe_b200 import synth
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lw = synth.make_layer(seed=0)
+    arena = ExpertArena(dev)
+    arena.add_layer(0, lw)
+    be = B200ExpertBackend(arena)
+    H = lw.hidden
+    xs = synth.make_tokens(11, 1, H)
+    hx = torch.from_numpy(xs).pin_memory()
+    hy = torch.empty((1, H), dtype=torch.float32).pin_memory()
+    xd = hx.to(dev)
+    yd = torch.empty_like(xd)
+    stream = torch.cuda.current_stream(dev)
+    n = 2000
+
+    def wall(fn):
+        for _ in range(50):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            fn()
+        return (time.perf_counter() - t0) / n * 1e6
+    lib = be.lib
+    out = {"ctypes_call_us": round(wall(lambda: lib.moe_b200_version()), 2)}
+    out["host_buffer_call_us"] = round(wall(lambda: be.decode_host_ptrs(
+        0, hx.data_ptr(), 1, hy.data_ptr(), stream_handle=stream.cuda_stream)), 2)
+
+    def dev_sync():
+        be.forward_layer_device(0, xd, yd)
+        stream.synchronize()
+    out["device_call_plus_sync_us"] = round(wall(dev_sync), 2)
+    out["device_call_us_back_to_back"] = round(_time_calls(lambda: be.forward_layer_device(0, xd, yd), n) * 1e3, 2)
+    out["config"] = "config-2 layer, 1 token per call, one GPU, host wall clock (perf_counter) per call"
+    print(json.dumps({"e2e_breakdown": out}), flush=True)
+
+
+PREFILL_ROLES = ["producer_waits_stage", "raw_producer_waits_slot", "dequant_waits_raw",
+                 "dequant_waits_stage", "mma_waits_full", "mma_waits_accumulator",
+                 "epilogue_waits", "epilogue_busy"]
+
+
+def prefill_role_counters(backend, layer: int, x, y) -> dict:
+    """Per-role wait counters of the expert GEMMs of one prefill call: the
+    kernels' trace slots (clock64 cycles each role spent waiting, per CTA),
+    as shares of the CTA's cycles, mean over CTAs.  A diagnostic."""
+    import ctypes as C
+    import torch
+    G = torch.cuda.get_device_properties(x.device).multi_processor_count
+    buf = torch.zeros(G * 32, dtype=torch.int64, device=x.device)
+    backend.lib.moe_b200_set_trace(C.c_void_p(buf.data_ptr()), G)
+    try:
+        backend.prefill_device(layer, x, y)
+        torch.cuda.synchronize()
+    finally:
+        backend.lib.moe_b200_set_trace(None, 0)
+    a = buf.view(G, 32).cpu().numpy().astype(np.float64)
+    out = {}
+    for mode, name in enumerate(["router", "gate_up", "down"]):
+        blk = a[:, mode * 10: mode * 10 + 10]
+        cyc = blk[:, 8].mean()
+        if cyc <= 0:
+            continue
+        out[name] = {"cycles_per_cta": round(cyc), "units_per_cta": round(blk[:, 9].mean(), 2)}
+        out[name].update({r: round(blk[:, i].mean() / cyc * 100, 1) for i, r in enumerate(PREFILL_ROLES)})
+    return out
+
+
 def run_prefill_only(args) -> None:
-    """The config-4 prefill measurement alone (one GPU), for profiling."""
+    """The config-4 prefill and the config-3 tensor-core call alone (one
+    GPU), with the GEMMs' per-role wait counters, for profiling."""
     import torch
     from flash_moe_b200 import synth
     from flash_moe_b200.backend import B200ExpertBackend
@@ -808,9 +917,20 @@ def run_prefill_only(args) -> None:
     dev = torch.device("cuda", 0)
     arena = ExpertArena(dev)
     arena.add_layer(0, synth.make_layer(seed=0))
+    lwz = synth.make_layer(seed=0, zipf_s=1.1)
+    arena.add_layer(1, lwz)
     backend = B200ExpertBackend(arena)
     peaks, peak_kind = measured_peaks()
-    print(json.dumps({"prefill": bench_prefill(backend, 0, dev, peaks, peak_kind)}), flush=True)
+    out = {"prefill": bench_prefill(backend, 0, dev, peaks, peak_kind)}
+    x = torch.from_numpy(synth.make_tokens(404, 4096, 2048)).to(dev).to(torch.bfloat16)
+    y = torch.empty((4096, 2048), dtype=torch.float32, device=dev)
+    out["prefill"]["role_counters_pct"] = prefill_role_counters(backend, 0, x, y)
+    x64 = torch.from_numpy(synth.make_tokens(3000, 64, 2048)).to(dev)
+    y64 = torch.empty_like(x64)
+    ms = _time_calls(lambda: backend.prefill_device(1, x64, y64), 20)
+    out["batched_tensor_path"] = {"us_per_call_64_tokens": round(ms * 1e3, 1),
+                                  "role_counters_pct": prefill_role_counters(backend, 1, x64, y64)}
+    print(json.dumps(out), flush=True)
 
 
 def check_last_step(runner, steps: int) -> float:
@@ -1049,6 +1169,7 @@ def run_gpu(args) -> None:
     if rank == 0 and world == 1 and not args.no_extra:
         cpu_on = not args.no_cpu
         extra["expert"] = bench_expert(dev, peaks, peak_kind, args.cpu_seconds if cpu_on else None)
+        extra["fp16_graph"] = bench_fp16_graph(backend, 0, dev)
         extra["prefill"] = with_cpu(
             bench_prefill(backend, 0, dev, peaks, peak_kind),
             lambda: cpu_sequence_baseline(lw, synth.make_tokens(404, 4096, H), sample_experts=24),
@@ -1114,7 +1235,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak", type=float, default=0.5)
-    ap.add_argument("--only", choices=["prefill", "delta", "trace"], default=None,
+    ap.add_argument("--only", choices=["prefill", "delta", "trace", "e2e"], default=None,
                     help="run only one measurement: the config-4 prefill or the DeltaNet step "
                          "(for profiling), or the decode kernel's phase timeline")
     ap.add_argument("--no-extra", action="store_true",
@@ -1128,6 +1249,8 @@ def main() -> None:
         run_prefill_only(args)
     elif args.only == "trace":
         run_trace(args)
+    elif args.only == "e2e":
+        run_e2e_breakdown(args)
     elif args.only == "delta":
         import torch
         dev = torch.device("cuda", 0)

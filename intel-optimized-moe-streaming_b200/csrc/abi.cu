@@ -5,6 +5,7 @@
 // per-thread stream, so concurrent callers (the reference fans experts out
 // over a ThreadPoolExecutor, src/flash_moe/moe_layer.py:76-97) never share
 // device state and each call is deterministic.
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <new>
@@ -572,18 +573,41 @@ int moe_b200_decode_host(const moe_b200_layer* L, const float* x, int32_t T, flo
     // synchronisation, and the result is copied out on the host
     if (T == 1 && fused_supported(L, T, L->flags)) {
         memcpy(hs.x, x, xb);
-        *hs.err = 0;
+        // the kernel's last CTA replaces this with the error word once every
+        // result row is in host memory (system-scope release): the host
+        // polls it instead of waking up from a stream synchronisation, for
+        // at most kHostPollSeconds, then synchronises the stream (which also
+        // reports a failed launch)
+        constexpr int kPending = 0x7fffffff;
+        constexpr double kHostPollSeconds = 2.0;
+        volatile int* done = hs.err;
+        *done = kPending;
         bool launched = false;
         e = launch_decode_fused_host(L, L->flags, hs.x, xd, hs.y, hs.ids, hs.w, hs.err, workspace,
                                      s, &launched);
         if (e != cudaSuccess) return fail(e, ST_CUDA);
         if (launched) {
-            e = cudaStreamSynchronize(s);
-            if (e != cudaSuccess) return fail(e, ST_CUDA);
+            const auto t0 = std::chrono::steady_clock::now();
+            bool seen = false;
+            for (uint32_t i = 0;; ++i) {
+                if (*done != kPending) {
+                    seen = true;
+                    break;
+                }
+                if ((i & 255u) == 0 &&
+                    std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() >
+                        kHostPollSeconds)
+                    break;
+            }
+            if (!seen) {
+                e = cudaStreamSynchronize(s);
+                if (e != cudaSuccess) return fail(e, ST_CUDA);
+                if (*done == kPending) return ST_TIMEOUT;
+            }
             memcpy(y, hs.y, xb);
             if (topk_ids) memcpy(topk_ids, hs.ids, kb);
             if (topk_weights) memcpy(topk_weights, hs.w, kb);
-            return *hs.err;
+            return *done;
         }
     }
     int* word_h = hs.err;

@@ -593,15 +593,21 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
 #undef TRACE
     }
     // ---- exit: the last CTA advances the sequence word for the next launch
+    // With a host-visible error word (the synchronous host-buffer call) the
+    // word is also the completion signal the host waits on: every CTA's
+    // writes to host memory are ordered before its exit count at system
+    // scope, and the last CTA releases the word after seeing every count.
     if (tid == 0) {
-        __threadfence();
+        if (p.err_out) __threadfence_system();
+        else __threadfence();
         const uint32_t t = atomicAdd(p.ctr + C_EXIT, 1u);
         if (t == (uint32_t)G - 1) {
             p.ctr[C_EXIT] = 0;
             p.ctr[C_SEQ] = seq0 + (uint32_t)p.n_steps;
             if (p.err_out) {
-                *p.err_out = atomicExch(reinterpret_cast<int*>(p.ctr + C_ERROR), 0);
+                const int err = atomicExch(reinterpret_cast<int*>(p.ctr + C_ERROR), 0);
                 __threadfence_system();
+                st_release_sys(reinterpret_cast<uint32_t*>(p.err_out), (uint32_t)err);
             }
             __threadfence();
         }
