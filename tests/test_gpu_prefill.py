@@ -231,3 +231,35 @@ def test_few_tokens_both_expert_gemm_paths(oracle, name, tokens):
     check_prefill(oracle, lw, xs, y0, ids0, w0)
     check_prefill(oracle, lw, xs, y1, ids1, w1)
     assert O.max_relative_error(y0, y1) <= 2e-4
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_prefill_expert_parallel_rank_shapes(world):
+    """The shapes one expert-parallel rank runs in the multi-GPU benchmark,
+    on one GPU: a 1/world expert slice of a 64-expert layer, the tensor-core
+    path over 64 gathered tokens without the shared expert, and the shared
+    expert alone over the rank's 64/world own tokens; each partial against
+    the exact fp32 engine with the same slice and flags."""
+    import torch
+    from flash_moe_b200 import _lib
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    lw = synth.make_layer(seed=36, n_experts=64, zipf_s=1.1)
+    per = lw.n_experts // world
+    xs = synth.make_tokens(36, 64, lw.hidden)
+    x = torch.from_numpy(xs).cuda()
+    for rank in (0, world - 1):
+        arena = ExpertArena()
+        arena.add_layer(0, lw, expert_begin=rank * per, expert_count=per)
+        be = B200ExpertBackend(arena)
+        own = x[rank * (64 // world):(rank + 1) * (64 // world)]
+        for xin, flags in ((x, _lib.NO_SHARED), (own, _lib.SHARED_ONLY)):
+            y = torch.empty_like(xin)
+            want = torch.empty_like(xin)
+            be.prefill_device(0, xin, y, flags=flags)
+            be.forward_layer_device(0, xin, want, flags=_lib.EXACT | flags)
+            torch.cuda.synchronize()
+            assert be.prefill_errors() == 0
+            err = O.max_relative_error(y.cpu().numpy(), want.cpu().numpy())
+            assert err <= TOL, (rank, flags, err)
+        be.close()
