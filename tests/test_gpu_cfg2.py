@@ -150,3 +150,46 @@ def test_cfg2_block_chain(oracle, cfg2):
     for i in range(n):
         check_block(oracle, lws[i % 4], x, yh[i], ih[i], wh[i])
         x = yh[i]
+
+
+@pytest.mark.parametrize("extra", [1, 12])
+def test_expert_count_just_above_the_sm_count(oracle, extra):
+    """E = SMs + 1 and SMs + 12 (every CTA owns at least one router row, some
+    two): independent and chained steps in one launch, every step against
+    the oracle."""
+    import torch
+    from flash_moe_b200 import _lib
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    E = sms + extra
+    lws = [synth.make_layer(seed=60 + extra + i, n_experts=E, inter=256) for i in range(2)]
+    arena = ExpertArena()
+    for i, lw in enumerate(lws):
+        arena.add_layer(i, lw)
+    be = B200ExpertBackend(arena)
+    assert be.kernels_per_call(0, 1) == 1
+    H, K, n = lws[0].hidden, lws[0].top_k, 6
+    xs = synth.make_tokens(210 + extra, n, H)
+    xd = torch.from_numpy(xs).to(be.device)
+    ys = torch.empty((n, H), dtype=torch.float32, device=be.device)
+    ids = torch.empty((n, K), dtype=torch.int32, device=be.device)
+    ws = torch.empty((n, K), dtype=torch.float32, device=be.device)
+    rows = [(i % 2, 0, xd[i], ys[i], ids[i], ws[i]) for i in range(n)]
+    be.decode_steps_device(be.layer_table([0, 1]), be.step_table(rows), n, 0)
+    torch.cuda.synchronize()
+    assert be.device_errors() == 0
+    yh, ih, wh = ys.cpu().numpy(), ids.cpu().numpy(), ws.cpu().numpy()
+    for i in range(n):
+        _check_token(oracle, lws[i % 2], xs[i], yh[i], ih[i], wh[i])
+    rows = [(i % 2, _lib.STEP_BLOCK | (_lib.STEP_CHAIN if i else 0), xd[0] if i == 0 else None,
+             ys[i], ids[i], ws[i]) for i in range(n)]
+    be.decode_steps_device(be.layer_table([0, 1]), be.step_table(rows), n, 0)
+    torch.cuda.synchronize()
+    assert be.device_errors() == 0
+    yh, ih, wh = ys.cpu().numpy(), ids.cpu().numpy(), ws.cpu().numpy()
+    x = xs[0]
+    for i in range(n):
+        check_block(oracle, lws[i % 2], x, yh[i], ih[i], wh[i])
+        x = yh[i]
+    be.close()
