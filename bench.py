@@ -767,6 +767,112 @@ def bench_allreduce(backend, layers, dev, world: int, rank: int, steps: int, pea
             "peak_source": f"{peak_kind} hbm_gbs", "max_rel_err": float(f"{err:.3e}")}
 
 
+def bench_stack_ep(backend, base_layer: int, dev, world: int, rank: int, peaks: dict,
+                   peak_kind: str) -> dict:
+    """Config 5 sharded over the ranks: 40 distinct identity-mixer blocks,
+    each rank holding 256/N experts of every layer.  Batch 1: the token
+    replicated on every rank; per block the RMSNorm kernels, the fused
+    single-token kernel over the rank's experts (the shared expert on rank 0)
+    and one 8 KB NCCL all-reduce; the 40 blocks in one CUDA graph.  Batch 32:
+    the 32 tokens split over the ranks; per block the norms, the expert-
+    parallel exchange around the tensor-core path, the residual.  Device
+    time max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from flash_moe_b200 import _lib, synth
+    from flash_moe_b200.ep import ep_exchange_step
+    arena = backend.store
+    base = arena.layer(base_layer)
+    ids = []
+    for l in range(40):
+        lid = 1000 + l
+        arena.add_device_layer(lid, base.reshuffled(5000 + l) if l else base)
+        ids.append(lid)
+    H = base.weights.hidden
+    lib = backend.lib
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    x1 = torch.from_numpy(synth.make_tokens(7000, 1, H)).to(dev)
+    h, n, m = (torch.empty_like(x1) for _ in range(3))
+    outs = [torch.empty_like(x1) for _ in range(2)]
+    flags = backend.flags | (_lib.NO_SHARED if rank else 0)
+
+    def chain1(layer_flags):
+        src = x1
+        for i, lid in enumerate(ids):
+            _lib.check(lib.moe_b200_block_prepare(src.data_ptr(), h.data_ptr(), n.data_ptr(), 1, H,
+                                                  1e-6, stream), "moe_b200_block_prepare")
+            backend.forward_layer_device(lid, n, m, flags=layer_flags)
+            dist.all_reduce(m)
+            dst = outs[i % 2]
+            _lib.check(lib.moe_b200_block_finish(h.data_ptr(), m.data_ptr(), dst.data_ptr(), 1, H,
+                                                 stream), "moe_b200_block_finish")
+            src = dst
+        return src
+    chain1(flags)
+    torch.cuda.synchronize()
+    mode = "CUDA graph of the 40 blocks"
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            last = chain1(flags)
+        run1 = g.replay
+    except RuntimeError:
+        g, mode = None, "stream launches"
+        torch.cuda.synchronize()
+        dist.barrier()
+        run1 = lambda: chain1(flags)  # noqa: E731
+        last = outs[1]
+    ms1 = _time_ranks(run1, 5, warmup=2)
+    # the last block against the exact engine on the same input (a 40-block
+    # chain is compared block by block: one near-tied routing that flips in
+    # an early block changes everything after it)
+    x39, y_fast = outs[0].clone(), last.clone()
+    _lib.check(lib.moe_b200_block_prepare(x39.data_ptr(), h.data_ptr(), n.data_ptr(), 1, H, 1e-6,
+                                          stream), "moe_b200_block_prepare")
+    backend.forward_layer_device(ids[-1], n, m, flags=_lib.EXACT | (_lib.NO_SHARED if rank else 0))
+    dist.all_reduce(m)
+    y_exact = torch.empty_like(x1)
+    _lib.check(lib.moe_b200_block_finish(h.data_ptr(), m.data_ptr(), y_exact.data_ptr(), 1, H, stream),
+               "moe_b200_block_finish")
+    err1 = _rel_err_ranks(y_fast, y_exact)
+    del g
+    # batch 32, tokens split over the ranks
+    T = 32
+    per = T // world
+    xs = torch.from_numpy(synth.make_tokens(7001, T, H)[rank * per:(rank + 1) * per]).to(dev)
+    hb, nb, mb, yb = (torch.empty_like(xs) for _ in range(4))
+    x_all = torch.empty((T, H), dtype=torch.float32, device=dev)
+    y_part = torch.empty_like(x_all)
+    y_r, y_s = torch.empty_like(xs), torch.empty_like(xs)
+
+    def chain32():
+        src = xs
+        for lid in ids:
+            _lib.check(lib.moe_b200_block_prepare(src.data_ptr(), hb.data_ptr(), nb.data_ptr(), per,
+                                                  H, 1e-6, stream), "moe_b200_block_prepare")
+            ep_exchange_step(
+                nb, lambda xa, yp, lid=lid: backend.prefill_device(lid, xa, yp, flags=_lib.NO_SHARED),
+                lambda xx, ys, lid=lid: backend.prefill_device(lid, xx, ys, flags=_lib.SHARED_ONLY),
+                x_all, y_part, y_r, y_s, mb)
+            _lib.check(lib.moe_b200_block_finish(hb.data_ptr(), mb.data_ptr(), yb.data_ptr(), per, H,
+                                                 stream), "moe_b200_block_finish")
+            src = yb
+    ms32 = _time_ranks(chain32, 2, warmup=1)
+    for lid in ids:
+        arena.drop_layer(lid)
+    per_tok = 40 * step_bytes(8)
+    gbs = per_tok / (ms1 / 1e3) / 1e9
+    return {"config": f"config 5 sharded over {world} GPUs: 40 blocks, {base.weights.n_experts // world} "
+                      "experts per layer per GPU; batch 1 replicated (fused kernel on the own "
+                      f"experts + 8 KB NCCL all-reduce per block, {mode}); batch 32 split "
+                      f"({per} per GPU), expert-parallel tensor-core path per block",
+            "batch1_us_per_token": round(ms1 * 1e3, 1), "batch1_us_per_layer": round(ms1 * 1e3 / 40, 2),
+            "batch1_gbs_union": round(gbs, 1),
+            "batch1_last_block_max_rel_err_vs_exact": float(f"{err1:.3e}"),
+            "batch32_ms_per_step": round(ms32, 3), "batch32_tokens_per_s": round(T / (ms32 / 1e3)),
+            "peak_source": f"{peak_kind} hbm_gbs"}
+
+
 def bench_sequence_ep(backend, layer: int, dev, world: int, rank: int, tokens: int, name: str,
                       peaks: dict, peak_kind: str, use_prefill: bool, bound: str = "tensor") -> dict:
     """A many-token layer expert-parallel: the `tokens` tokens split evenly
@@ -1166,6 +1272,7 @@ def run_gpu(args) -> None:
                                                     "config 3 batched decode (Zipf 1.1)", peaks,
                                                     peak_kind, True, bound="hbm")
         arena.drop_layer(5000)
+        extra["stack"] = bench_stack_ep(backend, 0, dev, world, rank, peaks, peak_kind)
     if rank == 0 and world == 1 and not args.no_extra:
         cpu_on = not args.no_cpu
         extra["expert"] = bench_expert(dev, peaks, peak_kind, args.cpu_seconds if cpu_on else None)
