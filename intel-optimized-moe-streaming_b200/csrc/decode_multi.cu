@@ -176,18 +176,35 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
             for (int i = tid; i < ep.tq * H; i += kFusedThreads) st_word_sys(dst + i, ep.x_own[i], seq);
             TRACE(1);
         }
+        // word pairs pi = tid + u * kFusedThreads, all kXPairs of a thread's
+        // round in flight (one poll round trip for all of them, not one per
+        // word); only the pairs still missing are read again
+        constexpr int kXPairs = 8;
         bool ok = true;
-        for (int i0 = tid; i0 < T * H; i0 += 4 * kFusedThreads) {
-            float v[4];
+        const int n_pairs = T * H / 2;
+        for (int p0 = tid; p0 < n_pairs && ok; p0 += kXPairs * kFusedThreads) {
+            uint32_t pend = 0;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int i = i0 + u * kFusedThreads;
-                if (i < T * H) v[u] = wait_word_sys(ep.xs + i, seq, kWaitPolls, ok);
-            }
+            for (int u = 0; u < kXPairs; ++u)
+                if (p0 + u * kFusedThreads < n_pairs) pend |= 1u << u;
+            for (uint32_t round = 0; pend != 0u; ++round) {
+                if (round == kWaitPolls) {
+                    ok = false;
+                    break;
+                }
+                ulonglong2 wv[kXPairs];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int i = i0 + u * kFusedThreads;
-                if (i < T * H) x32[i] = v[u];
+                for (int u = 0; u < kXPairs; ++u)
+                    wv[u] = ((pend >> u) & 1u) ? ld_word2_sys(ep.xs + 2 * (p0 + u * kFusedThreads))
+                                               : make_ulonglong2(0ull, 0ull);
+#pragma unroll
+                for (int u = 0; u < kXPairs; ++u)
+                    if (((pend >> u) & 1u) && (uint32_t)(wv[u].x >> 32) == seq &&
+                        (uint32_t)(wv[u].y >> 32) == seq) {
+                        pend &= ~(1u << u);
+                        *reinterpret_cast<float2*>(x32 + 2 * (p0 + u * kFusedThreads)) =
+                            make_float2(__uint_as_float((uint32_t)wv[u].x), __uint_as_float((uint32_t)wv[u].y));
+                    }
             }
         }
         if (!ok) set_error(p.ctr, ST_TIMEOUT);
@@ -483,16 +500,47 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_multi(const __grid_
         // CTA c of every rank sends rows [h0, h1) of its partials; the own
         // tokens' rows are the sum over ranks in rank order
         TRACE(11);
+        // every (rank, own token, row) word polled at once into shared
+        // memory (the partial-output rows are free: the loop above has read
+        // them), then each own row summed over the ranks in rank order
+        __syncthreads();
+        float* s_comb = s_vout;  // [world][tq * nh]
+        const int per = ep.tq * nh, n_words = ep.world * per;
         bool ok = true;
-        for (int i = tid; i < ep.tq * nh; i += kFusedThreads) {
-            const int j = i / nh, rr = i % nh;
-            float acc = 0.f;
-            for (int r = 0; r < ep.world; ++r)
-                acc = __fadd_rn(acc, wait_word_sys(ep.yp + ((size_t)r * ep.tq + j) * H + h0 + rr, seq,
-                                                   kWaitPolls, ok));
-            ep.y_own[(size_t)j * H + h0 + rr] = acc;
+        for (int i0 = tid; i0 < n_words && ok; i0 += 4 * kFusedThreads) {
+            uint32_t pend = 0;
+            const uint64_t* src[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kFusedThreads;
+                if (i < n_words) pend |= 1u << u;
+                const int r = i / per, rem = i - r * per, j = rem / nh, rr = rem - j * nh;
+                src[u] = ep.yp + ((size_t)r * ep.tq + j) * H + h0 + rr;
+            }
+            for (uint32_t round = 0; pend != 0u; ++round) {
+                if (round == kWaitPolls) {
+                    ok = false;
+                    break;
+                }
+                uint64_t wv[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) wv[u] = ((pend >> u) & 1u) ? ld_word_sys(src[u]) : 0ull;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (((pend >> u) & 1u) && (uint32_t)(wv[u] >> 32) == seq) {
+                        pend &= ~(1u << u);
+                        s_comb[i0 + u * kFusedThreads] = __uint_as_float((uint32_t)wv[u]);
+                    }
+            }
         }
         if (!ok) set_error(p.ctr, ST_TIMEOUT);
+        __syncthreads();
+        for (int i = tid; i < per; i += kFusedThreads) {
+            const int j = i / nh, rr = i - j * nh;
+            float acc = 0.f;
+            for (int r = 0; r < ep.world; ++r) acc = __fadd_rn(acc, s_comb[r * per + i]);
+            ep.y_own[(size_t)j * H + h0 + rr] = acc;
+        }
         TRACE(12);
     }
 

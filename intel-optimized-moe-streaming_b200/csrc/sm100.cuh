@@ -143,6 +143,14 @@ __device__ __forceinline__ uint64_t ld_word_sys(const uint64_t* p) {
     return w;
 }
 
+// Two consecutive system-scope exchange words (p 16-byte aligned) in one
+// load; each 64-bit element is read whole.
+__device__ __forceinline__ ulonglong2 ld_word2_sys(const uint64_t* p) {
+    ulonglong2 w;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    return w;
+}
+
 // Payload of the exchange word at p once it carries step `seq`; at most
 // `limit` polls while *ok (cleared when the limit is hit, so a thread that
 // gave up once stops waiting).

@@ -4,7 +4,8 @@ the oracle restatement of the reference's run_moe_layer.
 Routing: the device's top-k ids must equal the oracle's, except where the
 k-th and (k+1)-th scores are within 1e-5 relative (a near tie that fp32
 summation order can flip); then the oracle is re-run with the device's
-selection.  Outputs: max|y - ref| / max|ref| <= 1e-3."""
+selection.  Routing weights within 1e-5 relative.  Outputs:
+max|y - ref| / max|ref| <= 1e-3."""
 from __future__ import annotations
 
 import numpy as np
@@ -38,7 +39,10 @@ def check_layer(oracle, lw, xs, y, ids, w, fp16_graph=0, tol=TOL):
                 f"token {t}: routing differs without a near tie: {ids[t]} vs {want_ids[t]}"
         sel = [(list(map(int, ids[t])), [float(v) for v in w[t]]) for t in range(len(xs))]
         want_y, _, want_w = oracle_layer(oracle, lw, xs, fp16_graph, selections=sel)
-    np.testing.assert_allclose(np.asarray(w), want_w, rtol=1e-6, atol=1e-7)
+    # fp32 scores summed in another order than the host's BLAS (whose kernel,
+    # and so order, depends on the CPU): a weight's relative error is the
+    # absolute error of the score differences, a few 1e-6 at scores ~1
+    np.testing.assert_allclose(np.asarray(w), want_w, rtol=1e-5, atol=1e-7)
     err = O.max_relative_error(y, want_y)
     assert err <= tol, err
     return err
