@@ -72,14 +72,18 @@ __device__ __forceinline__ void quantize_block_vals(const float (&vals)[8], QVec
     float m = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(vals[e]));
-    m = warp_max(m);
+    // the magnitudes are non-negative, so their bit patterns order like the
+    // values: one redux.sync instead of five shuffle rounds
+    m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
     float iv;
     if (!(m <= 3.0e38f)) {  // inf / nan in the block: propagate as nan
         iv = 0.f;
         if (lane == 0) q.s[b] = __int_as_float(0x7fc00000);
     } else {
-        iv = m > 0.f ? 32512.f / m : 0.f;
-        if (lane == 0) q.s[b] = m / 32512.f;
+        // fast division: a code may be off by one unit; the scale stored
+        // with the codes is what the dot products use
+        iv = m > 0.f ? (m < 1e37f ? __fdividef(32512.f, m) : 32512.f / m) : 0.f;
+        if (lane == 0) q.s[b] = m * (1.0f / 32512.f);
     }
     int sh = 0, sl = 0;
     uint32_t ph[2] = {0, 0}, pl[2] = {0, 0};
