@@ -51,7 +51,7 @@ class B200ExpertBackend:
 
     def __init__(self, arena: ExpertArena, expert_workers: int = 4,
                  fp16_graph: bool = False, exact: bool = False,
-                 prefill_min_tokens: int = 32):
+                 prefill_min_tokens: int | None = None):
         if expert_workers < 1:
             raise ValueError("thread and worker counts must be positive")
         self.lib = _lib.load()
@@ -64,8 +64,9 @@ class B200ExpertBackend:
         self._native_enabled = False
         self._tls = threading.local()
         # forward_layer uses the tensor-core prefill kernels from this many
-        # tokens on (when the layer's shapes and formats allow it)
-        self.prefill_min_tokens = int(prefill_min_tokens)
+        # tokens on (when the layer's shapes and formats allow it); None: for
+        # every token count the single-launch decode kernels do not take
+        self.prefill_min_tokens = None if prefill_min_tokens is None else int(prefill_min_tokens)
 
     # ---------------------------------------------------------------- policy
 
@@ -178,6 +179,19 @@ class B200ExpertBackend:
         _lib.check(self.lib.moe_b200_prefill_kernels(C.byref(s), tokens, C.byref(n)),
                    "moe_b200_prefill_kernels")
         return n.value
+
+    def uses_tensor_path(self, layer: int, tokens: int) -> bool:
+        """Whether forward_layer runs these tokens on the tensor-core prefill
+        path.  With the default threshold that is every token count the
+        one-launch decode kernels (fused, multi-token) do not take: from there
+        on the decode engine is four launches with a pass over the routed rows
+        per token, 1.7-2.6x the tensor path's time for 9 to 31 tokens of a
+        256-expert layer on a B200."""
+        if not self.prefill_supported(layer):
+            return False
+        if self.prefill_min_tokens is not None:
+            return tokens >= self.prefill_min_tokens
+        return self.kernels_per_call(layer, tokens) > 1
 
     def kernels_per_call(self, layer: int, tokens: int, flags: int | None = None) -> int:
         """Kernels one forward_layer_device call launches (from the library)."""
@@ -401,7 +415,7 @@ class B200ExpertBackend:
         squeeze = x.ndim == 1
         x = x.reshape(-1, self.store.layer(layer).weights.hidden)
         k = self.store.layer(layer).weights.top_k
-        if not (x.shape[0] >= self.prefill_min_tokens and self.prefill_supported(layer)):
+        if not self.uses_tensor_path(layer, x.shape[0]):
             # decode: one synchronous call with the host arrays
             t = x.shape[0]
             y = np.empty_like(x)
@@ -416,15 +430,12 @@ class B200ExpertBackend:
             yd = torch.empty_like(xd)
             ids = torch.empty((x.shape[0], k), dtype=torch.int32, device=self.device)
             w = torch.empty((x.shape[0], k), dtype=torch.float32, device=self.device)
-            if x.shape[0] >= self.prefill_min_tokens and self.prefill_supported(layer):
-                self.prefill_device(layer, xd, yd, ids, w)
-                err = self.prefill_errors()
-                if err == -10:   # an activation outside fp16: fp32 engine instead
-                    self.forward_layer_device(layer, xd, yd, ids, w)
-                elif err:
-                    _lib.check(err, "moe_b200_prefill")
-            else:
+            self.prefill_device(layer, xd, yd, ids, w)
+            err = self.prefill_errors()
+            if err == -10:   # an activation outside fp16: fp32 engine instead
                 self.forward_layer_device(layer, xd, yd, ids, w)
+            elif err:
+                _lib.check(err, "moe_b200_prefill")
             y = yd.cpu().numpy()
             routing = (ids.cpu().numpy(), w.cpu().numpy())
         y = y[0] if squeeze else y

@@ -204,6 +204,21 @@ def test_forward_layer_uses_prefill_and_falls_back_on_fp16_overflow(oracle):
     assert O.max_relative_error(y2, want2) <= TOL
 
 
+@pytest.mark.parametrize("tokens", [8, 9, 17, 31])
+def test_forward_layer_default_threshold(oracle, tokens):
+    """With the default threshold forward_layer keeps the one-launch decode
+    kernels up to the token count they take (8 here) and hands every larger
+    call to the tensor cores; either way the result meets the oracle."""
+    lw = synth.make_layer(seed=36, n_experts=64)
+    xs = synth.make_tokens(36 + tokens, tokens, lw.hidden)
+    be = _backend(lw)
+    one_launch = be.kernels_per_call(0, tokens) == 1
+    assert be.uses_tensor_path(0, tokens) == (not one_launch)
+    assert one_launch == (tokens <= 8)
+    y, (ids, w) = be.forward_layer(0, xs, return_routing=True)
+    check_prefill(oracle, lw, xs, y, ids, w)
+
+
 def test_prefill_kernel_count():
     from flash_moe_b200 import _lib
     lw, _ = _case("p_h1024")
