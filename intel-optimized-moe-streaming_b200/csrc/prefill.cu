@@ -22,19 +22,25 @@
 //   k_pf_prep_x      per token: power-of-two scale, fp16 hi/lo, shared-gate
 //                    sigmoid, zero the output row
 //   k_pf_prep_router per router row: power-of-two scale, fp16 hi/lo
+//                    (k_pf_router_small instead, fp32 on the CUDA cores, for
+//                    at most 128 tokens)
 //   k_pf_gemm<ROUTER> logits = x . router^T (+ bias)
-//   k_pf_topk        per token: top-k + softmax (topk.cuh), pair counts
-//   k_pf_scatter     per expert: its (token, weight) pairs in token order
+//   k_pf_topk        per token (one warp): top-k + softmax (topk.cuh), pair
+//                    counts per held expert
+//   k_pf_scatter     per pair: its slot in the held expert's pair list
+//                    (expert offsets by a prefix sum of the counts, a slot
+//                    cursor per expert)
 //   k_pf_permute     x rows in pair order (contiguous B rows per expert)
 //   k_pf_gemm<GATEUP> act = silu(x Wg^T) * (x Wu^T) per pair, fp16
 //   k_pf_gemm<DOWN>  y[token] += w * (act Wd^T) per pair (fp32 reductions)
 //
-// The GEMM kernel is persistent (one CTA per SM, 448 threads) and
+// The GEMM kernel is persistent (one CTA per SM, 480 threads) and
 // warp-specialised:
 //   warps 0-3  epilogue: TMEM -> registers -> global (lane = tile row)
 //   warp 4     TMEM allocation; lane 0 issues the MMAs
-//   warp 5     TMA producer of B, the token rows: x rows by token id
-//              (tile::gather4) for gate/up, act rows (2-D boxes) for down
+//   warp 5     TMA producer of B, the token rows of the unit's pairs: the
+//              permuted x rows (gate/up) or the act rows (down), 2-D boxes
+//              of 128 and 16 rows
 //   warps 6-13 dequantisation: raw blocks -> fp16 K-major 128B-swizzled A
 //   warp 14    TMA producer of the packed weight rows (raw bytes, 2-D boxes),
 //              up to four 256-value groups ahead
@@ -153,6 +159,13 @@ __device__ __forceinline__ uint32_t nword(const uint32_t (&w)[NW], int k) {
 // fp32 value of the byte b (0..255) plus 2^23
 __device__ __forceinline__ float magic_f(uint32_t word, int k) {
     return __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540u | (uint32_t)k));
+}
+
+// Position in a ring of n mbarrier-guarded slots: the slot index in the low
+// 16 bits, the phase parity in bit 16 (no division by the run-time ring size
+// on the per-stage path).
+__device__ __forceinline__ uint32_t ring_next(uint32_t it, uint32_t n) {
+    return ((it & 0xFFFFu) + 1u == n) ? ((it & 0x10000u) ^ 0x10000u) : it + 1u;
 }
 
 __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
@@ -404,7 +417,7 @@ __device__ __forceinline__ bool dq_unit(const PfParams& p, const PfUnit& un, uin
     const int groups = p.side[un.side].K / GV;
     const uint8_t* raw0 = smem + (size_t)p.stages * p.stage_bytes + rofs;
     for (int g = 0; g < groups; ++g) {
-        const uint32_t slot = it_r % p.raw_slots, rph = (it_r / p.raw_slots) & 1u;
+        const uint32_t slot = it_r & 0xFFFFu, rph = it_r >> 16;
         if (!pf_wait_t(&rfull[slot], rph, abort, p.err, t_rfull)) return false;
         const uint8_t* rr = raw0 + (size_t)slot * p.raw_slot_bytes;
         uint32_t src[NSW];
@@ -418,7 +431,7 @@ __device__ __forceinline__ bool dq_unit(const PfParams& p, const PfUnit& un, uin
         }
         __syncwarp();
         if ((threadIdx.x & 31) == 0) mbar_arrive(&rempty[slot]);
-        ++it_r;
+        it_r = ring_next(it_r, p.raw_slots);
         // normalise: word i = bytes o + 4i .. o + 4i + 3 of the window
         const int o = (g * GB) & 15;
         uint32_t w[NW];
@@ -437,13 +450,13 @@ __device__ __forceinline__ bool dq_unit(const PfParams& p, const PfUnit& un, uin
             for (int i = 0; i < NW; ++i) w[i] = __funnelshift_r(src[i], src[i + 1], b);
         }
         auto stage = [&](auto s_c) -> bool {
-            const uint32_t st = it_s % p.stages, ph = (it_s / p.stages) & 1u;
+            const uint32_t st = it_s & 0xFFFFu, ph = it_s >> 16;
             if (!pf_wait_t(&empty[st], ph ^ 1u, abort, p.err, t_empty)) return false;
             dq_store<T, decltype(s_c)::value>(smem + (size_t)st * p.stage_bytes, trow, h, w);
             fence_async_smem();
             __syncwarp();
             if ((threadIdx.x & 31) == 0) mbar_arrive(&full[st]);
-            ++it_s;
+            it_s = ring_next(it_s, p.stages);
             return true;
         };
         if (!stage(std::integral_constant<int, 0>{})) return false;
@@ -585,7 +598,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 const int kst = p.H / 64;
                 for (int k = 0; k < p.segs * kst && ok; ++k) {
                     const int seg = k / kst, kk = (k % kst) * 64;
-                    const uint32_t st = it_s % S, ph = (it_s / S) & 1u;
+                    const uint32_t st = it_s & 0xFFFFu, ph = it_s >> 16;
                     int good = 1;
                     if (lane == 0) {
                         good = pf_wait_t(&empty[st], ph ^ 1u, s_abort, p.err, p.trace ? &c0 : nullptr);
@@ -600,7 +613,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                         tma_load_2d(smem + (size_t)st * p.stage_bytes + p.a_bytes + 16 * lane * 128,
                                     &p.rbmap[seg == 2], kk, un.tok0 + 16 * lane,
                                     &full[st]);
-                    ++it_s;
+                    it_s = ring_next(it_s, S);
                 }
                 continue;
             }
@@ -615,7 +628,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
             const uint64_t keep = l2_evict_last();
             const int nk = p.side[un.side].K / 64;
             for (int k = 0; k < nk && ok; ++k) {
-                const uint32_t st = it_s % S, ph = (it_s / S) & 1u;
+                const uint32_t st = it_s & 0xFFFFu, ph = it_s >> 16;
                 int good = 1;
                 if (lane == 0) {
                     good = pf_wait_t(&empty[st], ph ^ 1u, s_abort, p.err, p.trace ? &c0 : nullptr);
@@ -632,7 +645,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                     const int r = 128 * nb + 16 * (lane - nb);
                     tma_load_2d_hint(b + r * 128, b16, k0, row0 + r, &full[st], keep);
                 }
-                ++it_s;
+                it_s = ring_next(it_s, S);
             }
         }
     } else if (warp == kPfRawWarp) {
@@ -653,7 +666,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 const uint32_t rbytes =
                     MODE == PF_GATEUP ? 64u * (uint32_t)(W0 + W1) : 128u * (uint32_t)W0;
                 for (int g = 0; g < sd.K / gv; ++g) {
-                    const uint32_t slot = it_r % R, rph = (it_r / R) & 1u;
+                    const uint32_t slot = it_r & 0xFFFFu, rph = it_r >> 16;
                     ok = pf_wait_t(&rempty[slot], rph ^ 1u, s_abort, p.err, p.trace ? &c1 : nullptr);
                     if (!ok) break;
                     uint8_t* rs = smem + (size_t)S * p.stage_bytes + (size_t)slot * p.raw_slot_bytes;
@@ -662,7 +675,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                     if (MODE == PF_GATEUP)
                         tma_load_2d_hint(rs + 64 * W0, wm1, (g * gb1) & ~15, wrow, &rfull[slot],
                                          stream_pol);
-                    ++it_r;
+                    it_r = ring_next(it_r, R);
                 }
             }
         }
@@ -682,7 +695,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 tc_fence_after();
                 const uint32_t dbase = tmem + 256u * b;
                 for (int k = 0; k < nk; ++k) {
-                    const uint32_t st = it_s % S, ph = (it_s / S) & 1u;
+                    const uint32_t st = it_s & 0xFFFFu, ph = it_s >> 16;
                     ok = pf_wait_t(&full[st], ph, s_abort, p.err, p.trace ? &c0 : nullptr);
                     if (!ok) break;
                     tc_fence_after();
@@ -698,7 +711,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                         umma_f16(dbase + dcol, umma_desc_sw128(a0 + 32 * ks),
                                  umma_desc_sw128(b0 + 32 * ks), idesc, (k >= first) || ks != 0);
                     umma_commit(&empty[st]);
-                    ++it_s;
+                    it_s = ring_next(it_s, S);
                 }
                 if (!ok) break;
                 umma_commit(&acc_full[b]);
@@ -1313,6 +1326,7 @@ struct PfPrep {
     float* sg;
     float* y;
     int32_t* counts;
+    int32_t* cursor;
 };
 
 __device__ __forceinline__ float pf_x(const PfPrep& p, size_t i) {
@@ -1328,19 +1342,78 @@ __device__ __forceinline__ int pf_scale_exp(float amax) {
     return max(-126, min(126, 15 - e));
 }
 
-// one block (256 threads) per token; block 0 also clears the pair counts
+// Eight consecutive values of x (fp32 or bf16) from element i (a multiple of
+// 8); `vec`: x is 16-byte aligned, so one or two 16-byte loads do.
+__device__ __forceinline__ void pf_x8(const PfPrep& p, size_t i, bool vec, float (&v)[8]) {
+    if (vec && p.x_bf16) {
+        const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) + i);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            v[2 * q] = __uint_as_float(w[q] << 16);
+            v[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
+        }
+    } else if (vec) {
+        const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + i);
+        const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + i + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = pf_x(p, i + q);
+    }
+}
+
+// Chunks of 8 values a thread of k_pf_prep_x holds in registers: the row is
+// read once (H <= 256 * 8 * kPfPrepChunks).
+constexpr int kPfPrepChunks = 4;
+
+// one block (256 threads) per token; block 0 also clears the pair counts and
+// the pair cursors of the held experts
 __global__ void __launch_bounds__(256) k_pf_prep_x(PfPrep p) {
     __shared__ float s_red[2][8];
     const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (t == 0)
-        for (int i = tid; i < p.n_routed; i += blockDim.x) p.counts[i] = 0;
+        for (int i = tid; i < p.n_routed; i += blockDim.x) {
+            p.counts[i] = 0;
+            p.cursor[i] = 0;
+        }
     const size_t base = (size_t)t * p.H;
+    const int nch = p.H / 8;
+    const bool vx = ((uintptr_t)p.x & 15u) == 0;
+    const bool vg = p.gate_inp && ((uintptr_t)p.gate_inp & 15u) == 0;
+    const bool vy = ((uintptr_t)p.y & 15u) == 0;
+    float v[kPfPrepChunks][8];
     float amax = 0.f, dot = 0.f;
-    for (int i = tid; i < p.H; i += blockDim.x) {
-        const float v = pf_x(p, base + i);
-        amax = fmaxf(amax, fabsf(v));
-        if (p.gate_inp) dot = fmaf(v, p.gate_inp[i], dot);
-        p.y[base + i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPfPrepChunks; ++j) {
+        const int c = tid + 256 * j;
+        if (c >= nch) break;
+        pf_x8(p, base + 8 * (size_t)c, vx, v[j]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) amax = fmaxf(amax, fabsf(v[j][q]));
+        if (p.gate_inp) {
+            float g[8];
+            if (vg) {
+                const float4 a = *reinterpret_cast<const float4*>(p.gate_inp + 8 * c);
+                const float4 b = *reinterpret_cast<const float4*>(p.gate_inp + 8 * c + 4);
+                g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w;
+                g[4] = b.x; g[5] = b.y; g[6] = b.z; g[7] = b.w;
+            } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) g[q] = p.gate_inp[8 * c + q];
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dot = fmaf(v[j][q], g[q], dot);
+        }
+        float* yr = p.y + base + 8 * (size_t)c;
+        if (vy) {
+            reinterpret_cast<float4*>(yr)[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+            reinterpret_cast<float4*>(yr)[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) yr[q] = 0.f;
+        }
     }
     amax = warp_max(amax);
     if (p.gate_inp) dot = warp_sum(dot);
@@ -1353,11 +1426,23 @@ __global__ void __launch_bounds__(256) k_pf_prep_x(PfPrep p) {
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, s_red[0][i]);
     const int k = pf_scale_exp(amax);
     const float sc = ldexpf(1.f, k);
-    for (int i = tid; i < p.H; i += blockDim.x) {
-        const float v = __fmul_rn(pf_x(p, base + i), sc);
-        const __half hi = __float2half_rn(v);
-        p.xh[base + i] = hi;
-        if (p.want_lo) p.xl[base + i] = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+#pragma unroll
+    for (int j = 0; j < kPfPrepChunks; ++j) {
+        const int c = tid + 256 * j;
+        if (c >= nch) break;
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float a = __fmul_rn(v[j][2 * q], sc), b = __fmul_rn(v[j][2 * q + 1], sc);
+            const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+            hw[q] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+            const __half la = __float2half_rn(__fsub_rn(a, __half2float(ha)));
+            const __half lb = __float2half_rn(__fsub_rn(b, __half2float(hb)));
+            lw[q] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+        }
+        *reinterpret_cast<uint4*>(p.xh + base + 8 * (size_t)c) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        if (p.want_lo)
+            *reinterpret_cast<uint4*>(p.xl + base + 8 * (size_t)c) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
     if (tid == 0) {
         p.xs_inv[t] = ldexpf(1.f, -k);
@@ -1370,14 +1455,16 @@ __global__ void __launch_bounds__(256) k_pf_prep_x(PfPrep p) {
     }
 }
 
-// Router logits of a few tokens on the CUDA cores, in fp32: block (x, y)
-// computes the partial dots of experts [32x, 32x + 32) with every token over
-// the hidden slice [128y, 128y + 128); the last block of column x to finish
-// (an arrival counter per column) adds the H/128 partials in slice order
-// (deterministic), adds the bias and writes the logits.  For T <=
-// kPfSmallRouterT, where the tensor-core router would run on a handful of SMs.
+// Router logits of a few tokens on the CUDA cores, in fp32, for T <=
+// kPfSmallRouterT (where the tensor-core router would run on a handful of
+// SMs).  Block (x, y) computes the kRsE x kRsTok dots of experts
+// [kRsE x, +kRsE) with tokens [kRsTok y, +kRsTok): thread i sums the hidden
+// quads i, i + 256, ... (all its loads in flight at once), a warp folds its
+// 32 lanes' partial sums with a butterfly reduce-scatter, and the 8 warps'
+// sums are added in warp order (a fixed order: deterministic); then the
+// bias.  Needs 16-byte aligned router rows and tokens.
 constexpr int kPfSmallRouterT = 128;
-constexpr int kRsE = 32, kRsK = 128, kRsT = 32;
+constexpr int kRsE = 8, kRsTok = 8;
 
 __device__ __forceinline__ float4 pf_x4(const PfPrep& p, size_t i) {  // i a multiple of 4
     if (p.x_bf16) {
@@ -1388,68 +1475,62 @@ __device__ __forceinline__ float4 pf_x4(const PfPrep& p, size_t i) {  // i a mul
     return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + i);
 }
 
-__global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, float* part, uint32_t* cnt,
-                                                         const float* bias, float* logits) {
-    __shared__ __align__(16) float sR[kRsE][kRsK + 4];
-    __shared__ __align__(16) float sX[kRsT][kRsK + 4];
-    const int e0 = blockIdx.x * kRsE, k0 = blockIdx.y * kRsK, tid = threadIdx.x;
-    for (int i = tid; i < kRsE * kRsK / 4; i += 256) {
-        const int r = i / (kRsK / 4), c = (i % (kRsK / 4)) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (e0 + r < p.E) v = *reinterpret_cast<const float4*>(p.router + (size_t)(e0 + r) * p.H + k0 + c);
-        *reinterpret_cast<float4*>(&sR[r][c]) = v;
-    }
-    const int el = tid >> 3, tg = tid & 7;  // expert e0 + el, tokens t0 + tg + 8 j
-    for (int t0 = 0; t0 < p.T; t0 += kRsT) {
-        __syncthreads();
-        for (int i = tid; i < kRsT * kRsK / 4; i += 256) {
-            const int r = i / (kRsK / 4), c = (i % (kRsK / 4)) * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + r < p.T) v = pf_x4(p, (size_t)(t0 + r) * p.H + k0 + c);
-            *reinterpret_cast<float4*>(&sX[r][c]) = v;
-        }
-        __syncthreads();
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int k = 0; k < kRsK; k += 4) {
-            const float4 r = *reinterpret_cast<const float4*>(&sR[el][k]);
+__global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, const float* bias,
+                                                         float* logits) {
+    __shared__ float s_part[8][kRsE * kRsTok];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int e0 = blockIdx.x * kRsE, t0 = blockIdx.y * kRsTok;
+    const int ne = min(kRsE, p.E - e0), nt = min(kRsTok, p.T - t0);
+    float acc[kRsE * kRsTok];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float4 xv = *reinterpret_cast<const float4*>(&sX[tg + 8 * j][k]);
-                acc[j] = fmaf(r.x, xv.x, acc[j]);
-                acc[j] = fmaf(r.y, xv.y, acc[j]);
-                acc[j] = fmaf(r.z, xv.z, acc[j]);
-                acc[j] = fmaf(r.w, xv.w, acc[j]);
-            }
-        }
-        if (e0 + el < p.E) {
+    for (int i = 0; i < kRsE * kRsTok; ++i) acc[i] = 0.f;
+    for (int q = tid; q < p.H / 4; q += 256) {
+        float4 rv[kRsE], xv[kRsTok];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int t = t0 + tg + 8 * j;
-                if (t < p.T) part[((size_t)blockIdx.y * p.T + t) * p.E + e0 + el] = acc[j];
+        for (int e = 0; e < kRsE; ++e)
+            rv[e] = e < ne ? *reinterpret_cast<const float4*>(p.router + (size_t)(e0 + e) * p.H + 4 * q)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int t = 0; t < kRsTok; ++t)
+            xv[t] = t < nt ? pf_x4(p, (size_t)(t0 + t) * p.H + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int e = 0; e < kRsE; ++e) {
+#pragma unroll
+            for (int t = 0; t < kRsTok; ++t) {
+                float a = acc[e * kRsTok + t];
+                a = fmaf(rv[e].x, xv[t].x, a);
+                a = fmaf(rv[e].y, xv[t].y, a);
+                a = fmaf(rv[e].z, xv[t].z, a);
+                a = fmaf(rv[e].w, xv[t].w, a);
+                acc[e * kRsTok + t] = a;
             }
         }
     }
-    // the last slice block of this expert column sums the partials
-    __shared__ int s_last;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t old = atomicAdd(cnt + blockIdx.x, 1u);
-        s_last = old == gridDim.y - 1;
+    // reduce-scatter over the warp: after the step with offset o a lane keeps
+    // the half of its values selected by its bit o; lane l ends with the sums
+    // of values 2l and 2l + 1
+#pragma unroll
+    for (int o = 16, n = kRsE * kRsTok; o >= 1; o >>= 1, n >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = up ? acc[i] : acc[i + n / 2];
+            const float keep = up ? acc[i + n / 2] : acc[i];
+            acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
     }
+    s_part[warp][2 * lane] = acc[0];
+    s_part[warp][2 * lane + 1] = acc[1];
     __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const int ne = min(kRsE, p.E - e0);
-    for (int i = tid; i < ne * p.T; i += 256) {
-        const int t = i / ne, e = e0 + i % ne;
-        float v = 0.f;
-        for (int q = 0; q < (int)gridDim.y; ++q) v += __ldcg(part + ((size_t)q * p.T + t) * p.E + e);
-        if (bias) v = __fadd_rn(v, bias[e]);
-        logits[(size_t)t * p.E + e] = v;
+    if (tid < kRsE * kRsTok) {
+        const int e = tid / kRsTok, t = tid % kRsTok;
+        if (e < ne && t < nt) {
+            float v = 0.f;
+            for (int w = 0; w < 8; ++w) v += s_part[w][tid];
+            if (bias) v = __fadd_rn(v, bias[e0 + e]);
+            logits[(size_t)(t0 + t) * p.E + e0 + e] = v;
+        }
     }
-    if (tid == 0) cnt[blockIdx.x] = 0;  // ready for the next call
 }
 
 // one block per router row
@@ -1483,24 +1564,29 @@ struct PfRoute {
     int32_t* ids_out;
     float* w_out;
     int32_t* counts;
-    const int32_t* ids_c;  // scatter: same as ids
+    int32_t* cursor;       // [n_routed] slots taken per held expert (zero on entry)
     int32_t* pair_tok;
     float* pair_w;
 };
 
-// one warp (block) per token
-__global__ void __launch_bounds__(32) k_pf_topk(PfRoute p) {
+// one warp per token, up to kPfTopkWarps tokens per block (blocks of one
+// warp spent more time being scheduled than routing)
+constexpr int kPfTopkWarps = 8;
+__global__ void __launch_bounds__(32 * kPfTopkWarps) k_pf_topk(PfRoute p) {
     extern __shared__ float s_sc[];
-    const int t = blockIdx.x, lane = threadIdx.x;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t >= p.T) return;
     int32_t* ids = p.ids + (size_t)t * p.K;
     float* w = p.w + (size_t)t * p.K;
     if (p.E <= 256) {
         topk_softmax_warp_fast(p.logits + (size_t)t * p.E, p.E, p.K, ids, w);
     } else {
-        unsigned char* taken = reinterpret_cast<unsigned char*>(s_sc + p.E);
-        for (int e = lane; e < p.E; e += 32) s_sc[e] = p.logits[(size_t)t * p.E + e];
+        // this warp's scores and taken flags: E floats + E bytes, 16-byte aligned
+        float* sc = s_sc + (size_t)(threadIdx.x >> 5) * (((size_t)p.E * 5 + 15) / 16 * 4);
+        unsigned char* taken = reinterpret_cast<unsigned char*>(sc + p.E);
+        for (int e = lane; e < p.E; e += 32) sc[e] = p.logits[(size_t)t * p.E + e];
         __syncwarp();
-        topk_softmax_warp(s_sc, taken, p.E, p.K, ids, w);
+        topk_softmax_warp(sc, taken, p.E, p.K, ids, w);
     }
     __syncwarp();
     if (lane < p.K) {
@@ -1512,50 +1598,46 @@ __global__ void __launch_bounds__(32) k_pf_topk(PfRoute p) {
     }
 }
 
-// one block (256 threads) per held expert: its pairs in token order
+// One thread per (token, slot) pair: a pair of a held expert takes the next
+// place of that expert's list, at the expert's offset (the exclusive prefix
+// sum of the pair counts, which every block forms itself) plus a slot from
+// the expert's cursor.  The order within an expert's list is the order the
+// slots were taken; each pair's GEMM result does not depend on its column.
 __global__ void __launch_bounds__(256) k_pf_scatter(PfRoute p) {
+    __shared__ int s_off[kPfMaxExperts];
     __shared__ int s_w[8];
-    __shared__ int s_off;
-    const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    int part = 0;
-    for (int i = tid; i < e; i += 256) part += p.counts[i];
-    part = __reduce_add_sync(0xffffffffu, part);
-    if (lane == 0) s_w[warp] = part;
-    __syncthreads();
-    if (tid == 0) {
-        int o = 0;
-        for (int i = 0; i < 8; ++i) o += s_w[i];
-        s_off = o;
-    }
-    __syncthreads();
-    int off = s_off;
-    const int gid = e + p.expert_begin;
-    for (int base = 0; base < p.T; base += 256) {
-        const int t = base + tid;
-        int slot = -1;
-        if (t < p.T)
-            for (int k = 0; k < p.K; ++k)
-                if (p.ids[(size_t)t * p.K + k] == gid) {
-                    slot = k;
-                    break;
-                }
-        const unsigned bal = __ballot_sync(0xffffffffu, slot >= 0);
-        __syncthreads();
-        if (lane == 0) s_w[warp] = __popc(bal);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int carry = 0;
+    for (int base = 0; base < p.n_routed; base += 256) {
+        const int e = base + tid;
+        const int c = e < p.n_routed ? p.counts[e] : 0;
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) s_w[warp] = incl;
         __syncthreads();
         int before = 0, total = 0;
         for (int i = 0; i < 8; ++i) {
             if (i < warp) before += s_w[i];
             total += s_w[i];
         }
-        if (slot >= 0) {
-            const int pos = off + before + __popc(bal & ((1u << lane) - 1u));
-            p.pair_tok[pos] = t;
-            p.pair_w[pos] = p.w[(size_t)t * p.K + slot];
-        }
-        off += total;
+        if (e < p.n_routed) s_off[e] = carry + before + incl - c;
+        carry += total;
+        __syncthreads();
     }
-    if (e == p.n_routed - 1 && tid == 0) p.counts[p.n_routed] = off;  // pairs in total
+    if (blockIdx.x == 0 && tid == 0) p.counts[p.n_routed] = carry;  // pairs in total
+    const int i = blockIdx.x * 256 + tid;
+    if (i < p.T * p.K) {
+        const int local = p.ids[i] - p.expert_begin;
+        if (local >= 0 && local < p.n_routed) {
+            const int pos = s_off[local] + atomicAdd(&p.cursor[local], 1);
+            p.pair_tok[pos] = i / p.K;
+            p.pair_w[pos] = p.w[i];
+        }
+    }
 }
 
 // x rows in pair order (one warp per pair row), the gate/up GEMM's B rows
@@ -1611,7 +1693,7 @@ bool prefill_supported(const moe_b200_layer* L, int flags) {
     const bool routed = !(flags & MOE_B200_SHARED_ONLY);
     const bool shared = L->shared_intermediate > 0 && !(flags & MOE_B200_NO_SHARED);
     if (!routed && !shared) return false;
-    if (L->hidden % 256 || L->hidden <= 0) return false;
+    if (L->hidden % 256 || L->hidden <= 0 || L->hidden > 256 * 8 * kPfPrepChunks) return false;
     if (routed) {
         if (L->expert_count <= 0 || L->expert_count > kPfMaxExperts) return false;
         if (L->top_k < 1 || L->top_k > kMaxTopK || L->n_experts > 4096) return false;
@@ -1634,16 +1716,13 @@ bool prefill_supported(const moe_b200_layer* L, int flags) {
 }
 
 struct PfWs {
-    size_t counts, xs_inv, sg, xh, xl, rh, rl, rs_inv, logits, part, ids, w, ptok, pw, act, xperm,
+    size_t counts, cursor, xs_inv, sg, xh, xl, rh, rl, rs_inv, logits, ids, w, ptok, pw, act, xperm,
         total;
 };
 
-// The CUDA-core router for few tokens (needs 16-byte aligned router rows;
-// its per-column arrival counters live in bytes [128, 256) of the
-// workspace, among the control words that stay zero between calls).
-constexpr int kRsCntOffset = 128;
+// The CUDA-core router for few tokens (needs 16-byte aligned router rows).
 static bool pf_small_router(const moe_b200_layer* L, int T) {
-    return T <= kPfSmallRouterT && L->n_experts <= 32 * kRsE && ((uintptr_t)L->router & 15u) == 0;
+    return T <= kPfSmallRouterT && ((uintptr_t)L->router & 15u) == 0;
 }
 
 static PfWs pf_ws(const moe_b200_layer* L, int T) {
@@ -1654,6 +1733,7 @@ static PfWs pf_ws(const moe_b200_layer* L, int T) {
     s.used = 256;
     PfWs w;
     w.counts = s.take((size_t)(L->expert_count + 1) * 4);
+    w.cursor = s.take((size_t)L->expert_count * 4);
     w.xs_inv = s.take((size_t)T * 4);
     w.sg = s.take((size_t)T * 4);
     w.xh = s.take((size_t)T * H * 2);
@@ -1662,7 +1742,6 @@ static PfWs pf_ws(const moe_b200_layer* L, int T) {
     w.rl = s.take(E * H * 2);
     w.rs_inv = s.take(E * 4);
     w.logits = s.take((size_t)T * E * 4);
-    w.part = s.take(pf_small_router(L, T) ? (size_t)(H / kRsK) * T * E * 4 : 0);
     w.ids = s.take((size_t)T * K * 4);
     w.w = s.take((size_t)T * K * 4);
     w.ptok = s.take((size_t)T * K * 4);
@@ -1799,6 +1878,7 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     pp.sg = reinterpret_cast<float*>(base + W.sg);
     pp.y = y;
     pp.counts = reinterpret_cast<int32_t*>(base + W.counts);
+    pp.cursor = reinterpret_cast<int32_t*>(base + W.cursor);
     const bool small_router = routed && pf_small_router(L, T) && ((uintptr_t)x & 15u) == 0;
     pp.want_lo = routed && !small_router;
     k_pf_prep_x<<<T, 256, 0, s>>>(pp);
@@ -1839,14 +1919,13 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     rp.ids_out = ids_out;
     rp.w_out = w_out;
     rp.counts = pp.counts;
+    rp.cursor = pp.cursor;
     rp.pair_tok = const_cast<int32_t*>(gp.pair_tok);
     rp.pair_w = const_cast<float*>(gp.pair_w);
 
     if (routed && small_router) {
-        float* part = reinterpret_cast<float*>(base + W.part);
-        uint32_t* rcnt = reinterpret_cast<uint32_t*>(base + kRsCntOffset);
-        k_pf_router_small<<<dim3((E + kRsE - 1) / kRsE, H / kRsK), 256, 0, s>>>(
-            pp, part, rcnt, L->router_bias, gp.logits);
+        k_pf_router_small<<<dim3((E + kRsE - 1) / kRsE, (T + kRsTok - 1) / kRsTok), 256, 0, s>>>(
+            pp, L->router_bias, gp.logits);
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
     } else if (routed) {
         k_pf_prep_router<<<E, 256, 0, s>>>(pp);
@@ -1870,10 +1949,14 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
             return pf_fail(ce, e);
     }
     if (routed) {
-        const size_t tsm = E > 256 ? (size_t)E * 5 : 0;
-        k_pf_topk<<<T, 32, tsm, s>>>(rp);
+        // more than 256 experts: each warp stages its scores in shared memory
+        // (E floats + E flags), within the default 48 KB per block
+        const size_t wsm = E > 256 ? ((size_t)E * 5 + 15) / 16 * 16 : 0;
+        int wpb = kPfTopkWarps;
+        while (wpb > 1 && (size_t)wpb * wsm > 48 * 1024) --wpb;
+        k_pf_topk<<<(T + wpb - 1) / wpb, 32 * wpb, (size_t)wpb * wsm, s>>>(rp);
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
-        k_pf_scatter<<<n_routed, 256, 0, s>>>(rp);
+        k_pf_scatter<<<(T * K + 255) / 256, 256, 0, s>>>(rp);
         if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
         k_pf_permute<<<(T * K + 7) / 8, 256, 0, s>>>(pp.counts + n_routed, rp.pair_tok, pp.xh,
                                                      reinterpret_cast<__half*>(base + W.xperm), H);
