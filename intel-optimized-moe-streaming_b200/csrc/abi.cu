@@ -43,6 +43,20 @@ struct Scratch {
     cudaStream_t stream = nullptr;
     void* buf = nullptr;
     size_t cap = 0;
+    void* host = nullptr;  // pinned staging for results read on the host
+    size_t hcap = 0;
+
+    cudaError_t ensure_host(size_t bytes) {
+        if (bytes <= hcap) return cudaSuccess;
+        if (host) cudaFreeHost(host);
+        host = nullptr;
+        hcap = 0;
+        const size_t want = align256(bytes);
+        cudaError_t e = cudaMallocHost(&host, want);
+        if (e != cudaSuccess) return e;
+        hcap = want;
+        return cudaSuccess;
+    }
 
     cudaError_t ensure(size_t bytes) {
         if (!stream) {
@@ -65,6 +79,7 @@ struct Scratch {
         if (cudaGetDevice(&prev) != cudaSuccess) return;
         cudaSetDevice(device);
         if (buf) cudaFree(buf);
+        if (host) cudaFreeHost(host);
         if (stream) cudaStreamDestroy(stream);
         cudaSetDevice(prev);
     }
@@ -89,6 +104,41 @@ static bool on_device(const void* p) {
 }
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// true when p is device (or managed) memory of the current device.
+static bool on_this_device(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    return (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) && a.device == dev;
+}
+
+// moe_quant_expert's output rule on the device: the rows of y up to and
+// including the first non-finite one (all rows when every one is finite)
+// go to out; res[0] = that row count, res[1] = 1 when a row was non-finite.
+__global__ void __launch_bounds__(256) k_emit_rows(const float* y, float* out, int n, int* res) {
+    __shared__ int s_first;
+    if (threadIdx.x == 0) s_first = n;
+    __syncthreads();
+    int first = n;
+    for (int r = threadIdx.x; r < n; r += blockDim.x)
+        if (!isfinite(y[r])) {
+            first = r;
+            break;
+        }
+    atomicMin(&s_first, first);
+    __syncthreads();
+    const int m = s_first < n ? s_first + 1 : n;
+    for (int r = threadIdx.x; r < m; r += blockDim.x) out[r] = y[r];
+    if (threadIdx.x == 0) {
+        res[0] = m;
+        res[1] = s_first < n ? 1 : 0;
+    }
+}
 
 static int check_qmat(int type, const void* base, int rows, int cols) {
     if (!supported(type) || cols % block_size(type)) return ST_TYPE;
@@ -259,7 +309,9 @@ int moe_quant_expert(int gate_type, const uint8_t* gate, int64_t gate_bytes,
         }
         const size_t o_act = st.take((size_t)2 * intermediate * 4);
         const size_t o_y = st.take((size_t)hidden * 4);
+        const size_t o_res = st.take(16);
         cudaError_t e = sc->ensure(st.used);
+        if (e == cudaSuccess) e = sc->ensure_host((size_t)hidden * 4 + 16);
         if (e != cudaSuccess) return fail(e, ST_INTERNAL);
         char* base = static_cast<char*>(sc->buf);
         const void* dptr[4];
@@ -291,13 +343,23 @@ int moe_quant_expert(int gate_type, const uint8_t* gate, int64_t gate_bytes,
         p.y = reinterpret_cast<float*>(base + o_y);
         e = launch_exact(p, sc->stream);
         if (e != cudaSuccess) return fail(e, ST_INTERNAL);
-        std::vector<float> y(hidden);
-        e = cudaMemcpyAsync(y.data(), p.y, (size_t)hidden * 4, cudaMemcpyDeviceToHost, sc->stream);
-        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
-        e = cudaStreamSynchronize(sc->stream);
-        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
         // rows up to and including the first non-finite one are written,
         // as the reference's output loop stops there (moe_quant_dot.cpp:207-211)
+        int* res_h = reinterpret_cast<int*>(static_cast<char*>(sc->host) + (size_t)hidden * 4);
+        if (((uintptr_t)output & 3u) == 0 && on_this_device(output)) {
+            int* res_d = reinterpret_cast<int*>(base + o_res);
+            k_emit_rows<<<1, 256, 0, sc->stream>>>(p.y, output, hidden, res_d);
+            e = cudaGetLastError();
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(res_h, res_d, 8, cudaMemcpyDeviceToHost, sc->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(sc->stream);
+            if (e != cudaSuccess) return fail(e, ST_INTERNAL);
+            return res_h[1] ? ST_NONFINITE : ST_OK;
+        }
+        float* y = static_cast<float*>(sc->host);
+        e = cudaMemcpyAsync(y, p.y, (size_t)hidden * 4, cudaMemcpyDeviceToHost, sc->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(sc->stream);
+        if (e != cudaSuccess) return fail(e, ST_INTERNAL);
         int n_out = hidden, status = ST_OK;
         for (int r = 0; r < hidden; ++r) {
             if (!std::isfinite(y[r])) {
@@ -307,10 +369,10 @@ int moe_quant_expert(int gate_type, const uint8_t* gate, int64_t gate_bytes,
             }
         }
         if (on_device(output)) {
-            e = cudaMemcpy(output, y.data(), (size_t)n_out * 4, cudaMemcpyHostToDevice);
+            e = cudaMemcpy(output, y, (size_t)n_out * 4, cudaMemcpyHostToDevice);
             if (e != cudaSuccess) return fail(e, ST_INTERNAL);
         } else {
-            std::memcpy(output, y.data(), (size_t)n_out * 4);
+            std::memcpy(output, y, (size_t)n_out * 4);
         }
         return status;
     } catch (...) {

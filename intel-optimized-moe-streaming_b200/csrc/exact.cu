@@ -9,8 +9,10 @@
 // them in shared memory.  It is the compatibility and cross-check engine;
 // the fast decode engine is in decode.cu.
 //
-//  k_gateup: one CTA per (token, slot, 16-row tile); one warp per row pair
-//            computes g and u, then the SwiGLU activation (reference
+//  k_gateup: one CTA per (token, slot, 8-row tile); one warp per row pair
+//            computes g and u (one loop over both rows when they share a
+//            format, the quant bytes read as 8-byte runs), then the SwiGLU
+//            activation (reference
 //            moe_quant_dot.cpp:196-206, shared expert shared_expert.py:247-249).
 //  k_down:   one CTA per (token, 8-row tile); one warp per output row sums
 //            weight_k * down_k(a_k) over the slots in top-k order, then adds
@@ -22,29 +24,169 @@
 
 namespace moeb200 {
 
-constexpr int kGateUpRows = 16;
+constexpr int kGateUpRows = 8;  // one row pair per warp
+
+// 8 bytes at a 2-byte aligned address as two little-endian words, by aligned
+// loads of exactly those bytes (read-only data: the non-coherent path).
+__device__ __forceinline__ uint2 ld8_a2(const uint8_t* p) {
+    if (((uintptr_t)p & 3u) == 0) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(p);
+        return make_uint2(__ldg(w), __ldg(w + 1));
+    }
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
+    const uint32_t m = __ldg(reinterpret_cast<const uint32_t*>(p + 2));
+    return make_uint2((uint32_t)__ldg(h) | (m << 16), (m >> 16) | ((uint32_t)__ldg(h + 3) << 16));
+}
+
+__device__ __forceinline__ int byte_of(const uint2 v, int k) {
+    return (int)(((k < 4 ? v.x : v.y) >> (8 * (k & 3))) & 0xFFu);
+}
+
+// Values 8*sub .. 8*sub+7 of one block: decode8<T>'s arithmetic (the same
+// roundings in the same order, so the same bits), with the eight quant
+// bytes (and Q5_K/Q6_K/Q3_K's high-bit bytes) read as two words.  Every
+// such run starts at an even offset of a 2-byte aligned block.
+template <int T>
+__device__ __forceinline__ void lane8(const uint8_t* b, int sub, float* w);
+
+template <>
+__device__ __forceinline__ void lane8<Q8_0>(const uint8_t* b, int sub, float* w) {
+    const float d = ld_f16(b);
+    const uint2 q = ld8_a2(b + 2 + 8 * sub);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = __fmul_rn((float)(int8_t)byte_of(q, j), d);
+}
+
+template <>
+__device__ __forceinline__ void lane8<Q4_K>(const uint8_t* b, int sub, float* w) {
+    const int i0 = 8 * sub, j = i0 >> 5;
+    int sc, mn;
+    k4_scale_min(b + 4, j, sc, mn);
+    const float d1 = __fmul_rn(ld_f16(b), (float)sc);
+    const float m1 = __fmul_rn(ld_f16(b + 2), (float)mn);
+    const uint2 q = ld8_a2(b + 16 + 32 * (i0 >> 6) + (i0 & 31));
+    const int sh = (j & 1) * 4;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = __fsub_rn(__fmul_rn(d1, (float)((byte_of(q, k) >> sh) & 15)), m1);
+}
+
+template <>
+__device__ __forceinline__ void lane8<Q5_K>(const uint8_t* b, int sub, float* w) {
+    const int i0 = 8 * sub, j = i0 >> 5;
+    int sc, mn;
+    k4_scale_min(b + 4, j, sc, mn);
+    const float dsc = __fmul_rn(ld_f16(b), (float)sc);
+    const float m1 = __fmul_rn(ld_f16(b + 2), (float)mn);
+    const uint2 q = ld8_a2(b + 48 + 32 * (i0 >> 6) + (i0 & 31));
+    const uint2 qh = ld8_a2(b + 16 + (i0 & 31));
+    const int sh = (j & 1) * 4;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int v = ((byte_of(q, k) >> sh) & 15) | (((byte_of(qh, k) >> j) & 1) << 4);
+        w[k] = __fsub_rn(__fmul_rn(dsc, (float)v), m1);
+    }
+}
+
+template <>
+__device__ __forceinline__ void lane8<Q6_K>(const uint8_t* b, int sub, float* w) {
+    const int i0 = 8 * sub;
+    const float ds = __fmul_rn(ld_f16(b + 208), (float)(int8_t)b[192 + (i0 >> 4)]);
+    const uint2 ql = ld8_a2(b + 64 * (i0 >> 7) + (i0 & 63));
+    const uint2 qh = ld8_a2(b + 128 + 32 * (i0 >> 7) + (i0 & 31));
+    const int sl = ((i0 >> 6) & 1) * 4, shh = ((i0 >> 5) & 3) * 2;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int v = (((byte_of(ql, k) >> sl) & 15) | (((byte_of(qh, k) >> shh) & 3) << 4)) - 32;
+        w[k] = __fmul_rn(ds, (float)v);
+    }
+}
+
+template <>
+__device__ __forceinline__ void lane8<Q3_K>(const uint8_t* b, int sub, float* w) {
+    const int i0 = 8 * sub, g = i0 >> 5;
+    const float ds = __fmul_rn(ld_f16(b + 108), (float)q3_scale(b + 96, i0 >> 4));
+    const uint2 ql = ld8_a2(b + 32 + 32 * (i0 >> 7) + (i0 & 31));
+    const uint2 hm = ld8_a2(b + (i0 & 31));
+    const int sl = 2 * (g & 3);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int v = ((byte_of(ql, k) >> sl) & 3) - ((((byte_of(hm, k) >> g) & 1) ^ 1) << 2);
+        w[k] = __fmul_rn(ds, (float)v);
+    }
+}
+
+// Dots of NR rows of format T with x (fp32 FMA, each lane summing its
+// 8-value runs s = lane, lane + 32, ... in order, then a warp tree).  The
+// rows share the loop so their loads overlap.
+template <int T, bool ROUND, int NR>
+__device__ __forceinline__ void rows_dot_t(const uint8_t* const (&rows)[NR],
+                                           const float* __restrict__ x, int cols, int lane,
+                                           float (&out)[NR]) {
+    constexpr int spb = block_size(T) >> 3, pb = block_bytes(T);
+    const int nsub = cols >> 3;
+    float acc[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) acc[r] = 0.f;
+#pragma unroll 4
+    for (int s = lane; s < nsub; s += 32) {
+        const int blk = s / spb, sub = s - blk * spb;
+        const float4 xa = __ldg(reinterpret_cast<const float4*>(x + 8 * s));
+        const float4 xb = __ldg(reinterpret_cast<const float4*>(x + 8 * s + 4));
+        float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        if (ROUND) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) xv[k] = round16(xv[k]);
+        }
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            float w[8];
+            lane8<T>(rows[r] + (int64_t)blk * pb, sub, w);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[r] = fmaf(ROUND ? round16(w[k]) : w[k], xv[k], acc[r]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r) out[r] = warp_sum(acc[r]);
+}
+
+template <bool ROUND, int NR>
+__device__ __forceinline__ void rows_dot(int type, const uint8_t* const (&rows)[NR],
+                                         const float* __restrict__ x, int cols, int lane,
+                                         float (&out)[NR]) {
+    switch (type) {
+        case Q8_0: rows_dot_t<Q8_0, ROUND, NR>(rows, x, cols, lane, out); break;
+        case Q3_K: rows_dot_t<Q3_K, ROUND, NR>(rows, x, cols, lane, out); break;
+        case Q4_K: rows_dot_t<Q4_K, ROUND, NR>(rows, x, cols, lane, out); break;
+        case Q5_K: rows_dot_t<Q5_K, ROUND, NR>(rows, x, cols, lane, out); break;
+        default:   rows_dot_t<Q6_K, ROUND, NR>(rows, x, cols, lane, out); break;
+    }
+}
 
 template <bool ROUND>
 __device__ __forceinline__ float row_dot(int type, const uint8_t* __restrict__ row,
                                          const float* __restrict__ x, int cols, int lane) {
-    const int bs = block_size(type), pb = block_bytes(type), spb = bs >> 3;
-    const int nsub = cols >> 3;
-    float acc = 0.f;
-    for (int s = lane; s < nsub; s += 32) {
-        const int blk = s / spb, sub = s - blk * spb;
-        float w[8];
-        decode8_any(type, row + (int64_t)blk * pb, sub, w);
-        const float4 xa = __ldg(reinterpret_cast<const float4*>(x + 8 * s));
-        const float4 xb = __ldg(reinterpret_cast<const float4*>(x + 8 * s + 4));
-        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float wk = ROUND ? round16(w[k]) : w[k];
-            const float xk = ROUND ? round16(xv[k]) : xv[k];
-            acc = fmaf(wk, xk, acc);
-        }
+    const uint8_t* const rows[1] = {row};
+    float out[1];
+    rows_dot<ROUND, 1>(type, rows, x, cols, lane, out);
+    return out[0];
+}
+
+// The gate and the up row of one intermediate row: one loop when they share
+// a format.
+template <bool ROUND>
+__device__ __forceinline__ void gate_up_dot(int gt, const uint8_t* g, int ut, const uint8_t* u,
+                                            const float* __restrict__ x, int cols, int lane,
+                                            float& gv, float& uv) {
+    if (gt == ut) {
+        const uint8_t* const rows[2] = {g, u};
+        float out[2];
+        rows_dot<ROUND, 2>(gt, rows, x, cols, lane, out);
+        gv = out[0];
+        uv = out[1];
+    } else {
+        gv = row_dot<ROUND>(gt, g, x, cols, lane);
+        uv = row_dot<ROUND>(ut, u, x, cols, lane);
     }
-    return warp_sum(acc);
 }
 
 __device__ __forceinline__ int slot_expert(const ExactPlan& p, int t, int k) {
@@ -80,11 +222,13 @@ __global__ void __launch_bounds__(256) k_gateup(ExactPlan p) {
         const bool rnd = ROUND && !shared;
         float g, u;
         if (rnd) {
-            g = round16(row_dot<true>(G.type, gbase + (int64_t)r * G.row_bytes, x, p.H, lane));
-            u = round16(row_dot<true>(U.type, ubase + (int64_t)r * U.row_bytes, x, p.H, lane));
+            gate_up_dot<true>(G.type, gbase + (int64_t)r * G.row_bytes, U.type,
+                              ubase + (int64_t)r * U.row_bytes, x, p.H, lane, g, u);
+            g = round16(g);
+            u = round16(u);
         } else {
-            g = row_dot<false>(G.type, gbase + (int64_t)r * G.row_bytes, x, p.H, lane);
-            u = row_dot<false>(U.type, ubase + (int64_t)r * U.row_bytes, x, p.H, lane);
+            gate_up_dot<false>(G.type, gbase + (int64_t)r * G.row_bytes, U.type,
+                               ubase + (int64_t)r * U.row_bytes, x, p.H, lane, g, u);
         }
         if (lane == 0) {
             float a;

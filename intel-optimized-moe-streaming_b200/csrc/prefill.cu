@@ -55,6 +55,7 @@
 #include <math.h>
 
 #include <mutex>
+#include <utility>
 
 #include "launch.h"
 #include "topk.cuh"
@@ -496,6 +497,7 @@ __device__ __forceinline__ bool epi_any(bool pred) {
 
 template <int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant__ PfParams p) {
+    pdl_enter();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1070,6 +1072,7 @@ __device__ __forceinline__ bool bd_k_loop(int groups, uint8_t* bufs, uint32_t bu
 
 template <int MODE>
 __global__ void __launch_bounds__(kBdThreads, kBdCtasPerSm) k_bd_gemm(const __grid_constant__ PfParams p) {
+    pdl_enter();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1371,6 +1374,7 @@ constexpr int kPfPrepChunks = 4;
 // one block (256 threads) per token; block 0 also clears the pair counts and
 // the pair cursors of the held experts
 __global__ void __launch_bounds__(256) k_pf_prep_x(PfPrep p) {
+    pdl_enter();
     __shared__ float s_red[2][8];
     const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (t == 0)
@@ -1477,6 +1481,7 @@ __device__ __forceinline__ float4 pf_x4(const PfPrep& p, size_t i) {  // i a mul
 
 __global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, const float* bias,
                                                          float* logits) {
+    pdl_enter();
     __shared__ float s_part[8][kRsE * kRsTok];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int e0 = blockIdx.x * kRsE, t0 = blockIdx.y * kRsTok;
@@ -1535,6 +1540,7 @@ __global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, const float* 
 
 // one block per router row
 __global__ void __launch_bounds__(256) k_pf_prep_router(PfPrep p) {
+    pdl_enter();
     __shared__ float s_red[8];
     const int e = blockIdx.x;
     const float* r = p.router + (size_t)e * p.H;
@@ -1573,6 +1579,7 @@ struct PfRoute {
 // warp spent more time being scheduled than routing)
 constexpr int kPfTopkWarps = 8;
 __global__ void __launch_bounds__(32 * kPfTopkWarps) k_pf_topk(PfRoute p) {
+    pdl_enter();
     extern __shared__ float s_sc[];
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (t >= p.T) return;
@@ -1604,6 +1611,7 @@ __global__ void __launch_bounds__(32 * kPfTopkWarps) k_pf_topk(PfRoute p) {
 // the expert's cursor.  The order within an expert's list is the order the
 // slots were taken; each pair's GEMM result does not depend on its column.
 __global__ void __launch_bounds__(256) k_pf_scatter(PfRoute p) {
+    pdl_enter();
     __shared__ int s_off[kPfMaxExperts];
     __shared__ int s_w[8];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1643,6 +1651,7 @@ __global__ void __launch_bounds__(256) k_pf_scatter(PfRoute p) {
 // x rows in pair order (one warp per pair row), the gate/up GEMM's B rows
 __global__ void __launch_bounds__(256) k_pf_permute(const int32_t* npairs, const int32_t* pair_tok,
                                                     const __half* xh, __half* xperm, int H) {
+    pdl_enter();
     const int pr = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (pr >= *npairs) return;
     const uint4* src = reinterpret_cast<const uint4*>(xh + (size_t)pair_tok[pr] * H);
@@ -1652,6 +1661,30 @@ __global__ void __launch_bounds__(256) k_pf_permute(const int32_t* npairs, const
 
 // ---------------------------------------------------------------------------
 // host side
+
+// Calls of at most this many tokens launch their kernels with programmatic
+// stream serialization: each prefill kernel begins with pdl_enter, so it may
+// start launching while the previous kernel of the stream finishes, which
+// hides most of the gap between a small call's short kernels (B200: 32
+// tokens 123 -> 114 us, 64 tokens 135 -> 130 us per call).  A 4096-token
+// call was slower that way (671 -> 697 us) and launches plainly.
+constexpr int kPfPdlMaxT = kPfSmallRouterT;
+
+template <typename... P, typename... A>
+static cudaError_t pf_launch(int T, void (*k)(P...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t s, A&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = T <= kPfPdlMaxT ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
+}
 
 static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1796,8 +1829,7 @@ static cudaError_t pf_launch_gemm(PfParams& p, int grid, cudaStream_t s) {
     const cudaError_t attr = cudaFuncSetAttribute(
         k_pf_gemm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
     if (attr != cudaSuccess) return attr;
-    k_pf_gemm<MODE><<<grid, kPfThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    return pf_launch(p.T, k_pf_gemm<MODE>, dim3(grid), dim3(kPfThreads), smem, s, p);
 }
 
 // The warp-level MMA path for few tokens (k_bd_gemm): every side's gate and
@@ -1834,8 +1866,7 @@ static cudaError_t bd_launch(PfParams& p, int grid, cudaStream_t s) {
     const cudaError_t attr = cudaFuncSetAttribute(
         k_bd_gemm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (attr != cudaSuccess) return attr;
-    k_bd_gemm<MODE><<<grid, kBdThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    return pf_launch(p.T, k_bd_gemm<MODE>, dim3(grid), dim3(kBdThreads), smem, s, p);
 }
 
 static int pf_fail(cudaError_t* ce, cudaError_t e) {
@@ -1881,8 +1912,7 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     pp.cursor = reinterpret_cast<int32_t*>(base + W.cursor);
     const bool small_router = routed && pf_small_router(L, T) && ((uintptr_t)x & 15u) == 0;
     pp.want_lo = routed && !small_router;
-    k_pf_prep_x<<<T, 256, 0, s>>>(pp);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = pf_launch(T, k_pf_prep_x, dim3(T), dim3(256), 0, s, pp);
     if (e != cudaSuccess) return pf_fail(ce, e);
 
     PfParams gp{};
@@ -1924,12 +1954,12 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     rp.pair_w = const_cast<float*>(gp.pair_w);
 
     if (routed && small_router) {
-        k_pf_router_small<<<dim3((E + kRsE - 1) / kRsE, (T + kRsTok - 1) / kRsTok), 256, 0, s>>>(
-            pp, L->router_bias, gp.logits);
-        if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
+        e = pf_launch(T, k_pf_router_small, dim3((E + kRsE - 1) / kRsE, (T + kRsTok - 1) / kRsTok),
+                      dim3(256), 0, s, pp, L->router_bias, gp.logits);
+        if (e != cudaSuccess) return pf_fail(ce, e);
     } else if (routed) {
-        k_pf_prep_router<<<E, 256, 0, s>>>(pp);
-        if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
+        if ((e = pf_launch(T, k_pf_prep_router, dim3(E), dim3(256), 0, s, pp)) != cudaSuccess)
+            return pf_fail(ce, e);
         // router logits
         PfParams rp2 = gp;
         bool ok = make_map(&rp2.rmap[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.rh, H, E, (uint64_t)H * 2, 64, 128, true) &&
@@ -1954,13 +1984,18 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
         const size_t wsm = E > 256 ? ((size_t)E * 5 + 15) / 16 * 16 : 0;
         int wpb = kPfTopkWarps;
         while (wpb > 1 && (size_t)wpb * wsm > 48 * 1024) --wpb;
-        k_pf_topk<<<(T + wpb - 1) / wpb, 32 * wpb, (size_t)wpb * wsm, s>>>(rp);
-        if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
-        k_pf_scatter<<<(T * K + 255) / 256, 256, 0, s>>>(rp);
-        if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
-        k_pf_permute<<<(T * K + 7) / 8, 256, 0, s>>>(pp.counts + n_routed, rp.pair_tok, pp.xh,
-                                                     reinterpret_cast<__half*>(base + W.xperm), H);
-        if ((e = cudaGetLastError()) != cudaSuccess) return pf_fail(ce, e);
+        if ((e = pf_launch(T, k_pf_topk, dim3((T + wpb - 1) / wpb), dim3(32 * wpb), (size_t)wpb * wsm,
+                           s, rp)) != cudaSuccess)
+            return pf_fail(ce, e);
+        if ((e = pf_launch(T, k_pf_scatter, dim3((T * K + 255) / 256), dim3(256), 0, s, rp)) != cudaSuccess)
+            return pf_fail(ce, e);
+        const int32_t* npairs = pp.counts + n_routed;
+        const int32_t* ptok = rp.pair_tok;
+        const __half* xh = pp.xh;
+        __half* xperm = reinterpret_cast<__half*>(base + W.xperm);
+        if ((e = pf_launch(T, k_pf_permute, dim3((T * K + 7) / 8), dim3(256), 0, s, npairs, ptok, xh,
+                           xperm, H)) != cudaSuccess)
+            return pf_fail(ce, e);
     }
 
     // expert GEMMs: warp-level MMA for few tokens, the tcgen05 pipeline otherwise

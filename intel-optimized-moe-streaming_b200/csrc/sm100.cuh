@@ -207,6 +207,16 @@ __device__ __forceinline__ float wait_word_gpu(const uint64_t* p, uint32_t tag, 
     return __uint_as_float((uint32_t)w);
 }
 
+// Programmatic dependent launch, at the top of a kernel: let the stream's
+// next kernel begin launching, then wait until the previous kernel has
+// completed and its writes are visible (both no-ops when the launch was not
+// programmatic).  Every block of the kernel is resident or done before the
+// next one can launch, so its waiting blocks never hold back this kernel.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
