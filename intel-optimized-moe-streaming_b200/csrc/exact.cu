@@ -162,6 +162,48 @@ __device__ __forceinline__ void rows_dot(int type, const uint8_t* const (&rows)[
     }
 }
 
+// Two rows of format T, row r with its own vector x_r: the same per-row
+// arithmetic and order as rows_dot_t, the two rows' loads in one loop.
+template <int T, bool ROUND>
+__device__ __forceinline__ float2 dot2x_t(const uint8_t* r0, const float* __restrict__ x0,
+                                          const uint8_t* r1, const float* __restrict__ x1,
+                                          int cols, int lane) {
+    constexpr int spb = block_size(T) >> 3, pb = block_bytes(T);
+    const int nsub = cols >> 3;
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll 2
+    for (int s = lane; s < nsub; s += 32) {
+        const int blk = s / spb, sub = s - blk * spb;
+        const float4 p0 = __ldg(reinterpret_cast<const float4*>(x0 + 8 * s));
+        const float4 q0 = __ldg(reinterpret_cast<const float4*>(x0 + 8 * s + 4));
+        const float4 p1 = __ldg(reinterpret_cast<const float4*>(x1 + 8 * s));
+        const float4 q1 = __ldg(reinterpret_cast<const float4*>(x1 + 8 * s + 4));
+        const float v0[8] = {p0.x, p0.y, p0.z, p0.w, q0.x, q0.y, q0.z, q0.w};
+        const float v1[8] = {p1.x, p1.y, p1.z, p1.w, q1.x, q1.y, q1.z, q1.w};
+        float w0[8], w1[8];
+        lane8<T>(r0 + (int64_t)blk * pb, sub, w0);
+        lane8<T>(r1 + (int64_t)blk * pb, sub, w1);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            a0 = fmaf(ROUND ? round16(w0[k]) : w0[k], ROUND ? round16(v0[k]) : v0[k], a0);
+            a1 = fmaf(ROUND ? round16(w1[k]) : w1[k], ROUND ? round16(v1[k]) : v1[k], a1);
+        }
+    }
+    return make_float2(warp_sum(a0), warp_sum(a1));
+}
+
+template <bool ROUND>
+__device__ __forceinline__ float2 dot2x(int type, const uint8_t* r0, const float* x0,
+                                        const uint8_t* r1, const float* x1, int cols, int lane) {
+    switch (type) {
+        case Q8_0: return dot2x_t<Q8_0, ROUND>(r0, x0, r1, x1, cols, lane);
+        case Q3_K: return dot2x_t<Q3_K, ROUND>(r0, x0, r1, x1, cols, lane);
+        case Q4_K: return dot2x_t<Q4_K, ROUND>(r0, x0, r1, x1, cols, lane);
+        case Q5_K: return dot2x_t<Q5_K, ROUND>(r0, x0, r1, x1, cols, lane);
+        default:   return dot2x_t<Q6_K, ROUND>(r0, x0, r1, x1, cols, lane);
+    }
+}
+
 template <bool ROUND>
 __device__ __forceinline__ float row_dot(int type, const uint8_t* __restrict__ row,
                                          const float* __restrict__ x, int cols, int lane) {
@@ -255,23 +297,51 @@ __global__ void __launch_bounds__(256) k_gateup(ExactPlan p) {
     }
 }
 
-template <bool ROUND>
+// PAIR: two held slots' rows per loop (their loads overlap, at twice the
+// registers; for few tokens, where the GPU is latency-bound).
+template <bool ROUND, bool PAIR>
 __global__ void __launch_bounds__(256) k_down(ExactPlan p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x, h = blockIdx.y * 8 + warp;
     if (h >= p.H) return;
     float combined = 0.f;
-    for (int k = 0; k < p.K; ++k) {
-        const int ge = slot_expert(p, t, k);
-        if (!held(p, ge)) continue;
-        const int64_t e = ge - p.expert_begin;
-        const float* a = p.act + ((size_t)t * (p.K + 1) + k) * p.Imax;
-        float v = row_dot<ROUND>(p.down.type,
-                                 p.down.base + e * p.down.stride + (int64_t)h * p.down.row_bytes,
-                                 a, p.I, lane);
-        if (ROUND) v = round16(v);
-        const float wk = p.w ? p.w[(size_t)t * p.K + k] : 1.0f;
-        combined = __fadd_rn(combined, __fmul_rn(wk, v));
+    if constexpr (!PAIR) {
+        for (int k = 0; k < p.K; ++k) {
+            const int ge = slot_expert(p, t, k);
+            if (!held(p, ge)) continue;
+            const int64_t e = ge - p.expert_begin;
+            const float* a = p.act + ((size_t)t * (p.K + 1) + k) * p.Imax;
+            float v = row_dot<ROUND>(p.down.type,
+                                     p.down.base + e * p.down.stride + (int64_t)h * p.down.row_bytes,
+                                     a, p.I, lane);
+            if (ROUND) v = round16(v);
+            const float wk = p.w ? p.w[(size_t)t * p.K + k] : 1.0f;
+            combined = __fadd_rn(combined, __fmul_rn(wk, v));
+        }
+    } else {
+        // the held slots two at a time, combined in top-k order
+        int k = 0;
+        while (k < p.K) {
+            int ks[2];
+            int n = 0;
+            for (; k < p.K && n < 2; ++k)
+                if (held(p, slot_expert(p, t, k))) ks[n++] = k;
+            if (n == 0) break;
+            const int k1 = n == 2 ? ks[1] : ks[0];
+            const int64_t e0 = slot_expert(p, t, ks[0]) - p.expert_begin;
+            const int64_t e1 = slot_expert(p, t, k1) - p.expert_begin;
+            const float2 d = dot2x<ROUND>(
+                p.down.type, p.down.base + e0 * p.down.stride + (int64_t)h * p.down.row_bytes,
+                p.act + ((size_t)t * (p.K + 1) + ks[0]) * p.Imax,
+                p.down.base + e1 * p.down.stride + (int64_t)h * p.down.row_bytes,
+                p.act + ((size_t)t * (p.K + 1) + k1) * p.Imax, p.I, lane);
+            const float out[2] = {d.x, d.y};
+            for (int i = 0; i < n; ++i) {
+                const float v = ROUND ? round16(out[i]) : out[i];
+                const float wk = p.w ? p.w[(size_t)t * p.K + ks[i]] : 1.0f;
+                combined = __fadd_rn(combined, __fmul_rn(wk, v));
+            }
+        }
     }
     if (p.sdown.base != nullptr) {
         const float* a = p.act + ((size_t)t * (p.K + 1) + p.K) * p.Imax;
@@ -286,12 +356,17 @@ cudaError_t launch_exact(const ExactPlan& p, cudaStream_t stream) {
     if (p.T <= 0) return cudaSuccess;
     dim3 g1(p.T * (p.K + 1), (p.Imax + kGateUpRows - 1) / kGateUpRows);
     dim3 g2(p.T, (p.H + 7) / 8);
+    // a few tokens with several slots: paired down rows (B200: the 1-token
+    // layer 56 -> 48 us); otherwise one row at a time (more warps resident)
+    const bool pair = p.T <= 4 && p.K >= 2;
     if (p.round16) {
         k_gateup<true><<<g1, 256, 0, stream>>>(p);
-        k_down<true><<<g2, 256, 0, stream>>>(p);
+        if (pair) k_down<true, true><<<g2, 256, 0, stream>>>(p);
+        else k_down<true, false><<<g2, 256, 0, stream>>>(p);
     } else {
         k_gateup<false><<<g1, 256, 0, stream>>>(p);
-        k_down<false><<<g2, 256, 0, stream>>>(p);
+        if (pair) k_down<false, true><<<g2, 256, 0, stream>>>(p);
+        else k_down<false, false><<<g2, 256, 0, stream>>>(p);
     }
     return cudaGetLastError();
 }

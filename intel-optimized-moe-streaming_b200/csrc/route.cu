@@ -49,16 +49,22 @@ __global__ void __launch_bounds__(32) k_topk(RoutePlan p) {
     extern __shared__ float s_scores[];
     unsigned char* taken = reinterpret_cast<unsigned char*>(s_scores + p.E);
     const int t = blockIdx.x, lane = threadIdx.x;
-    if (p.K > 0) {
+    if (p.K > 0 && p.E <= 256) {
+        // the same selection and weights from registers (topk.cuh)
+        topk_softmax_warp_fast(p.scores + (size_t)t * p.E, p.E, p.K, p.ids + (size_t)t * p.K,
+                               p.w + (size_t)t * p.K);
+    } else if (p.K > 0) {
         for (int e = lane; e < p.E; e += 32) s_scores[e] = p.scores[(size_t)t * p.E + e];
         __syncwarp();
         topk_softmax_warp(s_scores, taken, p.E, p.K, p.ids + (size_t)t * p.K,
                           p.w + (size_t)t * p.K);
     }
     if (p.gate_inp) {
+        // lane-strided, each lane in order (unrolled so the loads overlap)
         const float* xr = p.x + (size_t)t * p.H;
         float acc = 0.f;
-        for (int i = lane; i < p.H; i += 32) acc = fmaf(xr[i], p.gate_inp[i], acc);
+#pragma unroll 8
+        for (int i = lane; i < p.H; i += 32) acc = fmaf(__ldg(xr + i), __ldg(p.gate_inp + i), acc);
         acc = warp_sum(acc);
         if (lane == 0) p.sg[t] = shared_sigmoid(acc);
     }
