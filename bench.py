@@ -1039,6 +1039,58 @@ def run_prefill_only(args) -> None:
     print(json.dumps(out), flush=True)
 
 
+def run_kernel_times(args) -> None:
+    """Per-kernel device time of one tensor-core layer call at 32, 64 (the
+    config-3 layer with its Zipf bias) and 4096 tokens (config 4), from the
+    CUDA activity records torch.profiler collects (no replay, no
+    serialisation), mean over 10 calls, beside the call's own CUDA-event
+    time.  The kernels are profiled with programmatic dependent launch off
+    (MOE_B200_NO_PDL): with it, a kernel's span would include its wait for
+    the previous kernel.  A diagnostic: nothing of it is a bench value."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    from flash_moe_b200 import synth
+    from flash_moe_b200.backend import B200ExpertBackend
+    from flash_moe_b200.store import ExpertArena
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    arena = ExpertArena(dev)
+    arena.add_layer(0, synth.make_layer(seed=0))
+    arena.add_layer(1, synth.make_layer(seed=0, zipf_s=1.1))
+    be = B200ExpertBackend(arena)
+    cases = (("tokens_32", 1, synth.make_tokens(3001, 32, 2048), torch.float32),
+             ("tokens_64", 1, synth.make_tokens(3000, 64, 2048), torch.float32),
+             ("tokens_4096", 0, synth.make_tokens(404, 4096, 2048), torch.bfloat16))
+    out = {}
+    n = 10
+    for name, layer, xs, dt in cases:
+        x = torch.from_numpy(xs).to(dev).to(dt)
+        y = torch.empty((x.shape[0], 2048), dtype=torch.float32, device=dev)
+        ms = _time_calls(lambda: be.prefill_device(layer, x, y), 20)
+        os.environ["MOE_B200_NO_PDL"] = "1"
+        ms_plain = _time_calls(lambda: be.prefill_device(layer, x, y), 20)
+        try:
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                for _ in range(n):
+                    be.prefill_device(layer, x, y)
+                torch.cuda.synchronize()
+        finally:
+            del os.environ["MOE_B200_NO_PDL"]
+        per = {}
+        for ev in prof.events():
+            if ev.device_type == torch.autograd.DeviceType.CUDA:
+                t = getattr(ev, "device_time", None)
+                t = ev.cuda_time if t is None else t
+                key = ev.name.split("(")[0].replace("moeb200::", "").replace("void ", "")
+                per[key] = per.get(key, 0.0) + t / n
+        assert be.prefill_errors() == 0
+        out[name] = {"us_per_call": round(ms * 1e3, 1),
+                     "us_per_call_plain_launches": round(ms_plain * 1e3, 1),
+                     "kernel_us_per_call": {k: round(v, 1) for k, v in per.items()},
+                     "kernel_sum_us": round(sum(per.values()), 1)}
+    print(json.dumps({"kernel_times": out}), flush=True)
+
+
 def check_last_step(runner, steps: int) -> float:
     """Max relative error of the last timed step's output (runner.y) against
     the exact fp32 engine (every weight dequantised bit-exactly, fp32 FMA;
@@ -1342,9 +1394,10 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak", type=float, default=0.5)
-    ap.add_argument("--only", choices=["prefill", "delta", "trace", "e2e"], default=None,
+    ap.add_argument("--only", choices=["prefill", "delta", "trace", "e2e", "kernels"], default=None,
                     help="run only one measurement: the config-4 prefill or the DeltaNet step "
-                         "(for profiling), or the decode kernel's phase timeline")
+                         "(for profiling), the decode kernel's phase timeline, the host-call "
+                         "breakdown, or per-kernel device times of the tensor-core calls")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the prefill and batched-decode measurements (N = 1)")
     args = ap.parse_args()
@@ -1358,6 +1411,8 @@ def main() -> None:
         run_trace(args)
     elif args.only == "e2e":
         run_e2e_breakdown(args)
+    elif args.only == "kernels":
+        run_kernel_times(args)
     elif args.only == "delta":
         import torch
         dev = torch.device("cuda", 0)

@@ -54,6 +54,7 @@
 #include <cuda_bf16.h>
 #include <math.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <utility>
 
@@ -1682,7 +1683,9 @@ static cudaError_t pf_launch(int T, void (*k)(P...), dim3 grid, dim3 block, size
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = T <= kPfPdlMaxT ? 1 : 0;
+    // MOE_B200_NO_PDL (diagnostics): plain launches, so that a profiler's
+    // kernel spans do not include the programmatic wait for the previous one
+    cfg.numAttrs = (T <= kPfPdlMaxT && !std::getenv("MOE_B200_NO_PDL")) ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
 }
 
