@@ -790,13 +790,15 @@ def bench_stack_ep(backend, base_layer: int, dev, world: int, rank: int, peaks: 
         ids.append(lid)
     H = base.weights.hidden
     lib = backend.lib
-    stream = torch.cuda.current_stream(dev).cuda_stream
     x1 = torch.from_numpy(synth.make_tokens(7000, 1, H)).to(dev)
     h, n, m = (torch.empty_like(x1) for _ in range(3))
     outs = [torch.empty_like(x1) for _ in range(2)]
     flags = backend.flags | (_lib.NO_SHARED if rank else 0)
 
     def chain1(layer_flags):
+        # the stream current at the call: inside a graph capture, the
+        # capturing stream, so that the norm kernels join the graph
+        stream = torch.cuda.current_stream(dev).cuda_stream
         src = x1
         for i, lid in enumerate(ids):
             _lib.check(lib.moe_b200_block_prepare(src.data_ptr(), h.data_ptr(), n.data_ptr(), 1, H,
@@ -827,6 +829,7 @@ def bench_stack_ep(backend, base_layer: int, dev, world: int, rank: int, peaks: 
     # chain is compared block by block: one near-tied routing that flips in
     # an early block changes everything after it)
     x39, y_fast = outs[0].clone(), last.clone()
+    stream = torch.cuda.current_stream(dev).cuda_stream
     _lib.check(lib.moe_b200_block_prepare(x39.data_ptr(), h.data_ptr(), n.data_ptr(), 1, H, 1e-6,
                                           stream), "moe_b200_block_prepare")
     backend.forward_layer_device(ids[-1], n, m, flags=_lib.EXACT | (_lib.NO_SHARED if rank else 0))
