@@ -26,11 +26,12 @@
 //                    at most 128 tokens)
 //   k_pf_gemm<ROUTER> logits = x . router^T (+ bias)
 //   k_pf_topk        per token (one warp): top-k + softmax (topk.cuh), pair
-//                    counts per held expert
-//   k_pf_scatter     per pair: its slot in the held expert's pair list
-//                    (expert offsets by a prefix sum of the counts, a slot
-//                    cursor per expert)
-//   k_pf_permute     x rows in pair order (contiguous B rows per expert)
+//                    counts per held expert (done by k_pf_router_small for
+//                    few tokens and at most 256 experts)
+//   k_pf_pairs       per pair (one warp): its slot in the held expert's pair
+//                    list (expert offsets by a prefix sum of the counts, a
+//                    slot cursor per expert) and the copy of its x row there
+//                    (contiguous B rows per expert)
 //   k_pf_gemm<GATEUP> act = silu(x Wg^T) * (x Wu^T) per pair, fp16
 //   k_pf_gemm<DOWN>  y[token] += w * (act Wd^T) per pair (fp32 reductions)
 //
@@ -1460,6 +1461,41 @@ __global__ void __launch_bounds__(256) k_pf_prep_x(PfPrep p) {
     }
 }
 
+struct PfRoute {
+    int T, E, K, expert_begin, n_routed;
+    const float* logits;
+    int32_t* ids;
+    float* w;
+    int32_t* ids_out;
+    float* w_out;
+    int32_t* counts;
+    int32_t* cursor;       // [n_routed] slots taken per held expert (zero on entry)
+    int32_t* pair_tok;
+    float* pair_w;
+};
+
+// After a token's selection (ids, w of token t): the caller's routing rows
+// and the pair count of each held expert (lanes 0..K-1).
+__device__ __forceinline__ void pf_route_emit(const PfRoute& p, int t, const int32_t* ids,
+                                              const float* w, int lane) {
+    __syncwarp();
+    if (lane < p.K) {
+        const int id = ids[lane];
+        if (p.ids_out) p.ids_out[(size_t)t * p.K + lane] = id;
+        if (p.w_out) p.w_out[(size_t)t * p.K + lane] = w[lane];
+        const int local = id - p.expert_begin;
+        if (local >= 0 && local < p.n_routed) atomicAdd(&p.counts[local], 1);
+    }
+}
+
+// Top-k and weights of token t for E <= 256 (one warp, scores through L2).
+__device__ __forceinline__ void pf_route_token(const PfRoute& p, int t, int lane) {
+    int32_t* ids = p.ids + (size_t)t * p.K;
+    float* w = p.w + (size_t)t * p.K;
+    topk_softmax_warp_fast(p.logits + (size_t)t * p.E, p.E, p.K, ids, w);
+    pf_route_emit(p, t, ids, w, lane);
+}
+
 // Router logits of a few tokens on the CUDA cores, in fp32, for T <=
 // kPfSmallRouterT (where the tensor-core router would run on a handful of
 // SMs).  Block (x, y) computes the kRsE x kRsTok dots of experts
@@ -1480,8 +1516,12 @@ __device__ __forceinline__ float4 pf_x4(const PfPrep& p, size_t i) {  // i a mul
     return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + i);
 }
 
+// With `tcnt` (an arrival counter per token tile, zero between calls; E <=
+// 256) the last block of a token tile to finish also routes its tokens, one
+// warp per token: the top-k kernel's work without its launch.
 __global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, const float* bias,
-                                                         float* logits) {
+                                                         float* logits, PfRoute rp,
+                                                         uint32_t* tcnt) {
     pdl_enter();
     __shared__ float s_part[8][kRsE * kRsTok];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1537,6 +1577,16 @@ __global__ void __launch_bounds__(256) k_pf_router_small(PfPrep p, const float* 
             logits[(size_t)(t0 + t) * p.E + e0 + e] = v;
         }
     }
+    if (!tcnt) return;
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(tcnt + blockIdx.y, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (warp < nt) pf_route_token(rp, t0 + warp, lane);
+    if (tid == 0) tcnt[blockIdx.y] = 0;  // ready for the next call
 }
 
 // one block per router row
@@ -1563,18 +1613,6 @@ __global__ void __launch_bounds__(256) k_pf_prep_router(PfPrep p) {
     if (threadIdx.x == 0) p.rs_inv[e] = ldexpf(1.f, -k);
 }
 
-struct PfRoute {
-    int T, E, K, expert_begin, n_routed;
-    const float* logits;
-    int32_t* ids;
-    float* w;
-    int32_t* ids_out;
-    float* w_out;
-    int32_t* counts;
-    int32_t* cursor;       // [n_routed] slots taken per held expert (zero on entry)
-    int32_t* pair_tok;
-    float* pair_w;
-};
 
 // one warp per token, up to kPfTopkWarps tokens per block (blocks of one
 // warp spent more time being scheduled than routing)
@@ -1584,34 +1622,30 @@ __global__ void __launch_bounds__(32 * kPfTopkWarps) k_pf_topk(PfRoute p) {
     extern __shared__ float s_sc[];
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (t >= p.T) return;
+    if (p.E <= 256) {
+        pf_route_token(p, t, lane);
+        return;
+    }
     int32_t* ids = p.ids + (size_t)t * p.K;
     float* w = p.w + (size_t)t * p.K;
-    if (p.E <= 256) {
-        topk_softmax_warp_fast(p.logits + (size_t)t * p.E, p.E, p.K, ids, w);
-    } else {
-        // this warp's scores and taken flags: E floats + E bytes, 16-byte aligned
-        float* sc = s_sc + (size_t)(threadIdx.x >> 5) * (((size_t)p.E * 5 + 15) / 16 * 4);
-        unsigned char* taken = reinterpret_cast<unsigned char*>(sc + p.E);
-        for (int e = lane; e < p.E; e += 32) sc[e] = p.logits[(size_t)t * p.E + e];
-        __syncwarp();
-        topk_softmax_warp(sc, taken, p.E, p.K, ids, w);
-    }
+    // this warp's scores and taken flags: E floats + E bytes, 16-byte aligned
+    float* sc = s_sc + (size_t)(threadIdx.x >> 5) * (((size_t)p.E * 5 + 15) / 16 * 4);
+    unsigned char* taken = reinterpret_cast<unsigned char*>(sc + p.E);
+    for (int e = lane; e < p.E; e += 32) sc[e] = p.logits[(size_t)t * p.E + e];
     __syncwarp();
-    if (lane < p.K) {
-        const int id = ids[lane];
-        if (p.ids_out) p.ids_out[(size_t)t * p.K + lane] = id;
-        if (p.w_out) p.w_out[(size_t)t * p.K + lane] = w[lane];
-        const int local = id - p.expert_begin;
-        if (local >= 0 && local < p.n_routed) atomicAdd(&p.counts[local], 1);
-    }
+    topk_softmax_warp(sc, taken, p.E, p.K, ids, w);
+    pf_route_emit(p, t, ids, w, lane);
 }
 
-// One thread per (token, slot) pair: a pair of a held expert takes the next
-// place of that expert's list, at the expert's offset (the exclusive prefix
+// One warp per (token, slot) pair: a pair of a held expert takes the next
+// place of that expert's list -- the expert's offset (the exclusive prefix
 // sum of the pair counts, which every block forms itself) plus a slot from
-// the expert's cursor.  The order within an expert's list is the order the
-// slots were taken; each pair's GEMM result does not depend on its column.
-__global__ void __launch_bounds__(256) k_pf_scatter(PfRoute p) {
+// the expert's cursor -- and the warp copies the token's fp16 row there (the
+// gate/up GEMM's B rows, an expert's pairs contiguous).  The order within an
+// expert's list is the order the slots were taken; each pair's GEMM result
+// does not depend on its column.
+__global__ void __launch_bounds__(256) k_pf_pairs(PfRoute p, const __half* xh, __half* xperm,
+                                                  int H) {
     pdl_enter();
     __shared__ int s_off[kPfMaxExperts];
     __shared__ int s_w[8];
@@ -1638,26 +1672,21 @@ __global__ void __launch_bounds__(256) k_pf_scatter(PfRoute p) {
         __syncthreads();
     }
     if (blockIdx.x == 0 && tid == 0) p.counts[p.n_routed] = carry;  // pairs in total
-    const int i = blockIdx.x * 256 + tid;
-    if (i < p.T * p.K) {
-        const int local = p.ids[i] - p.expert_begin;
-        if (local >= 0 && local < p.n_routed) {
-            const int pos = s_off[local] + atomicAdd(&p.cursor[local], 1);
-            p.pair_tok[pos] = i / p.K;
-            p.pair_w[pos] = p.w[i];
-        }
+    const int i = blockIdx.x * 8 + warp;
+    if (i >= p.T * p.K) return;
+    const int local = p.ids[i] - p.expert_begin;
+    if (local < 0 || local >= p.n_routed) return;
+    int pos = 0;
+    if (lane == 0) pos = s_off[local] + atomicAdd(&p.cursor[local], 1);
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+    const int t = i / p.K;
+    if (lane == 0) {
+        p.pair_tok[pos] = t;
+        p.pair_w[pos] = p.w[i];
     }
-}
-
-// x rows in pair order (one warp per pair row), the gate/up GEMM's B rows
-__global__ void __launch_bounds__(256) k_pf_permute(const int32_t* npairs, const int32_t* pair_tok,
-                                                    const __half* xh, __half* xperm, int H) {
-    pdl_enter();
-    const int pr = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (pr >= *npairs) return;
-    const uint4* src = reinterpret_cast<const uint4*>(xh + (size_t)pair_tok[pr] * H);
-    uint4* dst = reinterpret_cast<uint4*>(xperm + (size_t)pr * H);
-    for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
+    const uint4* src = reinterpret_cast<const uint4*>(xh + (size_t)t * H);
+    uint4* dst = reinterpret_cast<uint4*>(xperm + (size_t)pos * H);
+    for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
 }
 
 // ---------------------------------------------------------------------------
@@ -1757,6 +1786,11 @@ struct PfWs {
 };
 
 // The CUDA-core router for few tokens (needs 16-byte aligned router rows).
+// Its per-token-tile arrival counters (at most 32 tiles of kRsTok tokens)
+// live in bytes [128, 256) of the workspace, among the control words that
+// stay zero between calls.
+constexpr int kRsCntOffset = 128;
+static_assert(kPfSmallRouterT / kRsTok <= (256 - kRsCntOffset) / 4, "token tiles");
 static bool pf_small_router(const moe_b200_layer* L, int T) {
     return T <= kPfSmallRouterT && ((uintptr_t)L->router & 15u) == 0;
 }
@@ -1956,9 +1990,14 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
     rp.pair_tok = const_cast<int32_t*>(gp.pair_tok);
     rp.pair_w = const_cast<float*>(gp.pair_w);
 
+    // the small router routes its tokens itself (up to 256 experts; arrival
+    // counters in workspace bytes 128..255, control words that stay zero
+    // between calls)
+    const bool fused_topk = routed && small_router && E <= 256;
     if (routed && small_router) {
+        uint32_t* tcnt = fused_topk ? reinterpret_cast<uint32_t*>(base + kRsCntOffset) : nullptr;
         e = pf_launch(T, k_pf_router_small, dim3((E + kRsE - 1) / kRsE, (T + kRsTok - 1) / kRsTok),
-                      dim3(256), 0, s, pp, L->router_bias, gp.logits);
+                      dim3(256), 0, s, pp, L->router_bias, gp.logits, rp, tcnt);
         if (e != cudaSuccess) return pf_fail(ce, e);
     } else if (routed) {
         if ((e = pf_launch(T, k_pf_prep_router, dim3(E), dim3(256), 0, s, pp)) != cudaSuccess)
@@ -1987,17 +2026,14 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
         const size_t wsm = E > 256 ? ((size_t)E * 5 + 15) / 16 * 16 : 0;
         int wpb = kPfTopkWarps;
         while (wpb > 1 && (size_t)wpb * wsm > 48 * 1024) --wpb;
-        if ((e = pf_launch(T, k_pf_topk, dim3((T + wpb - 1) / wpb), dim3(32 * wpb), (size_t)wpb * wsm,
+        if (!fused_topk &&
+            (e = pf_launch(T, k_pf_topk, dim3((T + wpb - 1) / wpb), dim3(32 * wpb), (size_t)wpb * wsm,
                            s, rp)) != cudaSuccess)
             return pf_fail(ce, e);
-        if ((e = pf_launch(T, k_pf_scatter, dim3((T * K + 255) / 256), dim3(256), 0, s, rp)) != cudaSuccess)
-            return pf_fail(ce, e);
-        const int32_t* npairs = pp.counts + n_routed;
-        const int32_t* ptok = rp.pair_tok;
         const __half* xh = pp.xh;
         __half* xperm = reinterpret_cast<__half*>(base + W.xperm);
-        if ((e = pf_launch(T, k_pf_permute, dim3((T * K + 7) / 8), dim3(256), 0, s, npairs, ptok, xh,
-                           xperm, H)) != cudaSuccess)
+        if ((e = pf_launch(T, k_pf_pairs, dim3((T * K + 7) / 8), dim3(256), 0, s, rp, xh, xperm, H)) !=
+            cudaSuccess)
             return pf_fail(ce, e);
     }
 
@@ -2091,7 +2127,10 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
 int prefill_kernels(const moe_b200_layer* L, int T) {
     const bool routed = !(L->flags & MOE_B200_SHARED_ONLY);
     if (!routed) return 3;
-    return pf_small_router(L, T) ? 7 : 8;
+    // prep, router (small: with the top-k when E <= 256; else prep_router,
+    // router GEMM, top-k), pairs, gate/up, down
+    if (pf_small_router(L, T)) return L->n_experts <= 256 ? 5 : 6;
+    return 7;
 }
 
 }  // namespace moeb200
