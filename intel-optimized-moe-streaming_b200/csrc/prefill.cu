@@ -75,7 +75,8 @@ constexpr int kPfDqWarp0 = 6;
 constexpr int kPfRawWarp = 14;
 constexpr int kPfDqThreads = 256;
 constexpr int kPfMaxN = 256;
-constexpr int kPfRouterN = 64;
+constexpr int kPfRouterN = 256;     // ROUTER: tokens per unit (MMA N)
+constexpr int kPfRouterChunks = 8;  // ROUTER: K chunks (units per token tile and row tile)
 constexpr uint32_t kPfPolls = 1u << 22;
 constexpr int kPfMaxExperts = 1024;
 
@@ -109,6 +110,8 @@ struct __align__(64) PfParams {
     int has_shared;
     int T, H, E, Imax;
     int segs;                // ROUTER: K segments (2: x exact in fp16; 3)
+    int rchunks;             // ROUTER: K chunks of the segs * H / 64 stages
+    float* rpart;            // ROUTER: [rchunks x T x E] scaled partial logits
     int stages, raw_slots;
     uint32_t stage_bytes, a_bytes, raw_slot_bytes;
     const int32_t* counts;   // [n_routed] pairs per held expert
@@ -344,6 +347,7 @@ struct PfUnit {
     int rt;    // row tile
     int prow;  // first pair row (act rows for the shared side start after the routed)
     int tok0;  // shared / router: first token
+    int kc;    // router: K chunk
 };
 
 template <int MODE>
@@ -351,11 +355,13 @@ __device__ __forceinline__ PfUnit pf_unit(const PfParams& p, const PfShared& sh,
                                           const int* s_tfirst, const int* s_poff, int u) {
     PfUnit r;
     if (MODE == PF_ROUTER) {
-        const int rt_n = (p.E + 127) / 128;
+        const int rt_n = (p.E + 127) / 128, tt_n = (p.T + kPfRouterN - 1) / kPfRouterN;
         r.side = 0;
         r.e = 0;
         r.rt = u % rt_n;
-        r.tok0 = (u / rt_n) * kPfRouterN;
+        const int rest = u / rt_n;
+        r.tok0 = (rest % tt_n) * kPfRouterN;
+        r.kc = rest / tt_n;
         r.n = min(kPfRouterN, p.T - r.tok0);
         r.prow = r.tok0;
         return r;
@@ -504,7 +510,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = p.stages, R = p.raw_slots;
-    constexpr int NBUF = MODE == PF_ROUTER ? 1 : 2;  // accumulator buffers (256 columns each)
+    constexpr int NBUF = 2;  // accumulator buffers (256 columns each)
     const uint64_t t_start = clock64();
     uint64_t c0 = 0, c1 = 0;  // this role's wait cycles (traced lanes only)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * p.stage_bytes +
@@ -580,7 +586,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
     if (MODE == PF_ROUTER) {
-        sh.n_units = ((p.E + 127) / 128) * ((p.T + kPfRouterN - 1) / kPfRouterN);
+        sh.n_units = ((p.E + 127) / 128) * ((p.T + kPfRouterN - 1) / kPfRouterN) * p.rchunks;
     } else {
         sh.ntiles_r = p.n_routed > 0 ? s_tfirst[p.n_routed] : 0;
         sh.pairs = p.n_routed > 0 ? s_poff[p.n_routed] : 0;
@@ -599,8 +605,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
             const PfUnit un = pf_unit<MODE>(p, sh, s_tfirst, s_poff, u);
             const int N16 = (un.n + 15) & ~15;
             if (MODE == PF_ROUTER) {
-                const int kst = p.H / 64;
-                for (int k = 0; k < p.segs * kst && ok; ++k) {
+                const int kst = p.H / 64, total = p.segs * kst;
+                const int k0 = total * un.kc / p.rchunks, k1 = total * (un.kc + 1) / p.rchunks;
+                for (int k = k0; k < k1 && ok; ++k) {
                     const int seg = k / kst, kk = (k % kst) * 64;
                     const uint32_t st = it_s & 0xFFFFu, ph = it_s >> 16;
                     int good = 1;
@@ -692,7 +699,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 const PfUnit un = pf_unit<MODE>(p, sh, s_tfirst, s_poff, u);
                 const int N16 = (un.n + 15) & ~15;
                 const uint32_t idesc = umma_idesc_f16(128, N16);
-                const int nk = (MODE == PF_ROUTER) ? p.segs * (p.H / 64) : p.side[un.side].K / 64;
+                int nk = p.side[un.side].K / 64;
+                if (MODE == PF_ROUTER) {
+                    const int total = p.segs * (p.H / 64);
+                    nk = total * (un.kc + 1) / p.rchunks - total * un.kc / p.rchunks;
+                }
                 const uint32_t b = it_acc % NBUF, aph = (it_acc / NBUF) & 1u;
                 ok = pf_wait_t(&acc_empty[b], aph ^ 1u, s_abort, p.err, p.trace ? &c1 : nullptr);
                 if (!ok) break;
@@ -705,15 +716,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(smem + (size_t)st * p.stage_bytes);
                     const uint32_t b0 = a0 + p.a_bytes;
-                    // ROUTER: stage k accumulates into accumulator k % 8 (64
-                    // columns each), which bounds the rounding the MMA
-                    // accumulator adds per output; the epilogue sums the 8.
-                    const uint32_t dcol = MODE == PF_ROUTER ? 64u * (uint32_t)(k & 7) : 0u;
-                    const int first = MODE == PF_ROUTER ? 8 : 1;
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_f16(dbase + dcol, umma_desc_sw128(a0 + 32 * ks),
-                                 umma_desc_sw128(b0 + 32 * ks), idesc, (k >= first) || ks != 0);
+                        umma_f16(dbase, umma_desc_sw128(a0 + 32 * ks), umma_desc_sw128(b0 + 32 * ks),
+                                 idesc, (k > 0) || ks != 0);
                     umma_commit(&empty[st]);
                     it_s = ring_next(it_s, S);
                 }
@@ -753,43 +759,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
             tc_fence_after();
             const uint32_t tq = tmem + ((uint32_t)(32 * warp) << 16) + 256u * b;
             for (int c0 = 0; c0 < un.n; c0 += 16) {
-                uint32_t v[16], v2[16];
+                uint32_t v[16];
                 tmem_ld16(tq + c0, v);
                 tmem_wait_ld();
                 if (MODE == PF_ROUTER) {
-                    // sum of the 8 accumulators in the fixed order
-                    // ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7))
-                    float q[2][16];
-#pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        float pr[2][16];
-#pragma unroll
-                        for (int pp = 0; pp < 2; ++pp) {
-                            const int a = 4 * half + 2 * pp;
-                            if (a > 0) {
-                                tmem_ld16(tq + 64 * a + c0, v);
-                            }
-                            tmem_ld16(tq + 64 * (a + 1) + c0, v2);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int j = 0; j < 16; ++j)
-                                pr[pp][j] = __fadd_rn(__uint_as_float(v[j]), __uint_as_float(v2[j]));
-                        }
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) q[half][j] = __fadd_rn(pr[0][j], pr[1][j]);
-                    }
+                    // this K chunk's dot, the power-of-two scales undone (exact);
+                    // the top-k kernel adds the chunks in a fixed order and the bias
                     const int e = un.rt * 128 + trow;
                     if (e < p.E) {
                         const float rs = p.rs_inv[e];
-                        const float bias = p.bias ? p.bias[e] : 0.f;
+                        float* out = p.rpart + (size_t)un.kc * p.T * p.E + e;
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const int col = c0 + j;
                             if (col >= un.n) break;
-                            const float acc = __fadd_rn(q[0][j], q[1][j]);
-                            float sc = __fmul_rn(__fmul_rn(acc, rs), s_cw[col]);
-                            if (p.bias) sc = __fadd_rn(sc, bias);
-                            p.logits[(size_t)s_ctok[col] * p.E + e] = sc;
+                            out[(size_t)s_ctok[col] * p.E] =
+                                __fmul_rn(__fmul_rn(__uint_as_float(v[j]), rs), s_cw[col]);
                         }
                     }
                 } else if (MODE == PF_GATEUP) {
@@ -1463,7 +1448,10 @@ __global__ void __launch_bounds__(256) k_pf_prep_x(PfPrep p) {
 
 struct PfRoute {
     int T, E, K, expert_begin, n_routed;
-    const float* logits;
+    float* logits;
+    const float* part;     // null, or [nparts x T x E] scaled partial logits of the
+    int nparts;            // tensor-core router, added here in a fixed order
+    const float* bias;     // with part: the router bias [E] or null
     int32_t* ids;
     float* w;
     int32_t* ids_out;
@@ -1486,6 +1474,30 @@ __device__ __forceinline__ void pf_route_emit(const PfRoute& p, int t, const int
         const int local = id - p.expert_begin;
         if (local >= 0 && local < p.n_routed) atomicAdd(&p.counts[local], 1);
     }
+}
+
+// Token t's logits from the tensor-core router's K-chunk partials: added
+// in a fixed order (eight: ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)),
+// else in chunk order), then the bias.  One warp; the sums go to p.logits.
+__device__ __forceinline__ void pf_logits_from_parts(const PfRoute& p, int t, int lane) {
+    const size_t stride = (size_t)p.T * p.E;
+    for (int e = lane; e < p.E; e += 32) {
+        const float* q = p.part + (size_t)t * p.E + e;
+        float v;
+        if (p.nparts == 8) {
+            float a[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[j] = __ldcg(q + j * stride);
+            v = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
+                          __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
+        } else {
+            v = __ldcg(q);
+            for (int j = 1; j < p.nparts; ++j) v = __fadd_rn(v, __ldcg(q + j * stride));
+        }
+        if (p.bias) v = __fadd_rn(v, p.bias[e]);
+        p.logits[(size_t)t * p.E + e] = v;
+    }
+    __syncwarp();
 }
 
 // Top-k and weights of token t for E <= 256 (one warp, scores through L2).
@@ -1622,6 +1634,7 @@ __global__ void __launch_bounds__(32 * kPfTopkWarps) k_pf_topk(PfRoute p) {
     extern __shared__ float s_sc[];
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (t >= p.T) return;
+    if (p.part) pf_logits_from_parts(p, t, lane);
     if (p.E <= 256) {
         pf_route_token(p, t, lane);
         return;
@@ -1781,7 +1794,7 @@ bool prefill_supported(const moe_b200_layer* L, int flags) {
 }
 
 struct PfWs {
-    size_t counts, cursor, xs_inv, sg, xh, xl, rh, rl, rs_inv, logits, ids, w, ptok, pw, act, xperm,
+    size_t counts, cursor, xs_inv, sg, xh, xl, rh, rl, rs_inv, logits, rpart, ids, w, ptok, pw, act, xperm,
         total;
 };
 
@@ -1812,6 +1825,7 @@ static PfWs pf_ws(const moe_b200_layer* L, int T) {
     w.rl = s.take(E * H * 2);
     w.rs_inv = s.take(E * 4);
     w.logits = s.take((size_t)T * E * 4);
+    w.rpart = s.take((size_t)kPfRouterChunks * T * E * 4);
     w.ids = s.take((size_t)T * K * 4);
     w.w = s.take((size_t)T * K * 4);
     w.ptok = s.take((size_t)T * K * 4);
@@ -2010,13 +2024,18 @@ int prefill_run(const moe_b200_layer* L, const void* x, int x_bf16, int T, float
                   make_map(&rp2.rbmap[1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pp.xl, H, T, (uint64_t)H * 2, 64, 16, true);
         if (!ok) return ST_INTERNAL;
         rp2.segs = 3;
-        rp2.stages = 6;
+        rp2.rchunks = kPfRouterChunks;
+        rp2.rpart = reinterpret_cast<float*>(base + W.rpart);
+        rp2.stages = 4;
         rp2.raw_slots = 0;
         rp2.a_bytes = 16384;
         rp2.stage_bytes = 16384 + kPfRouterN * 128;
         rp2.raw_slot_bytes = 0;
         rp2.n_routed = 0;
-        const int units = ((E + 127) / 128) * ((T + kPfRouterN - 1) / kPfRouterN);
+        rp.part = rp2.rpart;
+        rp.nparts = rp2.rchunks;
+        rp.bias = L->router_bias;
+        const int units = ((E + 127) / 128) * ((T + kPfRouterN - 1) / kPfRouterN) * rp2.rchunks;
         if ((e = pf_launch_gemm<PF_ROUTER>(rp2, units < sms ? units : sms, s)) != cudaSuccess)
             return pf_fail(ce, e);
     }
