@@ -233,6 +233,24 @@ def test_prefill_kernel_count():
     assert n.value == 5
 
 
+@pytest.mark.parametrize("tokens", [24, 160])
+def test_prefill_more_than_256_experts(oracle, tokens):
+    """More than 256 experts: the top-k runs as its own kernel with each
+    token's scores staged in shared memory, after the CUDA-core router (few
+    tokens) or after the tensor-core router, whose K-chunk partials it adds
+    first (many tokens)."""
+    lw = synth.make_layer(seed=37, hidden=1024, inter=256, n_experts=320, top_k=8,
+                          gate_type=Q4_K, up_type=Q4_K, down_type=Q8_0, shared_inter=256)
+    xs = synth.make_tokens(37 + tokens, tokens, lw.hidden)
+    be = _backend(lw)
+    s = be.store.layer(0).with_flags(0)
+    n = C.c_int(0)
+    assert be.lib.moe_b200_prefill_kernels(C.byref(s), tokens, C.byref(n)) == 0
+    assert n.value == (6 if tokens <= 128 else 7)
+    y, ids, w = _prefill(be, xs)
+    check_prefill(oracle, lw, xs, y, ids, w)
+
+
 @pytest.mark.parametrize("name,tokens", [("p_q3q4q8", 40), ("p_bias_q5", 48), ("p_h1024", 17)])
 def test_few_tokens_both_expert_gemm_paths(oracle, name, tokens):
     """At most 48 tokens the expert GEMMs run on warp-level MMA (k_bd_gemm);
