@@ -243,13 +243,14 @@ MOE_B200_API int moe_b200_prefill_workspace(const moe_b200_layer* layer, int32_t
                                             size_t* bytes);
 
 /* 1 when moe_b200_prefill handles this layer and its flags: hidden,
- * intermediate and shared_intermediate multiples of 256; Q8_0, Q3_K,
- * Q4_K, Q5_K or Q6_K weights whose rows are multiples of 16 bytes; gate
- * and up of one format; at most 1024 held experts. */
+ * intermediate and shared_intermediate multiples of 256, hidden at most
+ * 8192; Q8_0, Q3_K, Q4_K, Q5_K or Q6_K weights whose rows are multiples of
+ * 16 bytes; gate and up of one format; at most 1024 held experts. */
 MOE_B200_API int moe_b200_prefill_supported(const moe_b200_layer* layer);
 
 /* Number of kernels one moe_b200_prefill call of `tokens` tokens launches
- * (8; 7 for at most 128 tokens, whose router runs on the CUDA cores; 3 with
+ * (7; for at most 128 tokens, whose router runs on the CUDA cores, 5 with at
+ * most 256 experts -- the router also selects the top-k -- else 6; 3 with
  * MOE_B200_SHARED_ONLY). */
 MOE_B200_API int moe_b200_prefill_kernels(const moe_b200_layer* layer, int tokens, int* kernels);
 
