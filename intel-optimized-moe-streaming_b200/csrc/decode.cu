@@ -108,7 +108,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
     float* s_sg = reinterpret_cast<float*>(sm + p.o_misc + 324);
     float* s_part = reinterpret_cast<float*>(sm + p.o_misc + 384);     // [32] partial sums
     float* s_scores = reinterpret_cast<float*>(sm + p.o_misc + 512);   // [S]
-    unsigned char* s_taken = reinterpret_cast<unsigned char*>(s_scores + S);
     float* s_vout = reinterpret_cast<float*>(sm + p.o_misc + 512 + ((5 * S + 15) & ~15));
     float* x32 = reinterpret_cast<float*>(sm + p.o_x32);
     float* h32 = reinterpret_cast<float*>(sm + p.o_h32);
@@ -537,7 +536,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(const __grid_
                 const int v = sh ? A : (it - np_s) / np_i;
                 const int gp = sh ? it : (it - np_s) % np_i;
                 const int lpr = sh ? p.lpr_is : p.lpr_i;
-                const int ng = sh ? ng_s : ng_i;
                 const int rpw = 32 / lpr, sub = lane / lpr, pr = lane % lpr;
                 const int type = sh ? L0.shared_down_type : L0.down_type;
                 const int64_t rb = sh ? rb_sd : rb_down;
